@@ -1,0 +1,156 @@
+/*
+ * hexmoe.h — C ABI of libhexmoe.so, the sm_100a HEX fused-MoE layer.
+ *
+ * HEX (Header-Encoded eXperts) stores one expert matrix W [rows, cols] as
+ *   idx          uint32 [rows, cols/32*bits]  one little-endian bit stream of `bits`
+ *                                            (3 or 4) per block of 32 inputs
+ *   block_scale  uint8  [rows, cols/block]   fp8 e4m3 code per `block` inputs
+ *   expert_scale float32                     one per matrix
+ *   levels       float32 [2^bits]            the expert's own sorted table
+ *   W[o, i] = levels[idx(o, i)] * (fp8(block_scale[o, i / block]) * expert_scale)
+ * stacked over the n experts of a tier (experts sharing one index width).  The
+ * reference layout (blackhole/anatomy/hex.py:21-31, runtime/blackhole_runtime/
+ * hex_ref.py:1-12) fixes block = 32; block = 128 is accepted as well (same bit
+ * stream, one scale per 128 inputs).
+ *
+ * Every entry point takes plain device pointers and sizes, runs on the caller's
+ * stream (a cudaStream_t passed as void*, NULL = legacy default stream), makes
+ * no host synchronisation and allocates no device memory: scratch is a caller
+ * buffer sized by the matching *_workspace_bytes() call.  Calls are re-entrant;
+ * a layer handle is immutable after creation and may be shared across streams.
+ * Every call returns HEXMOE_OK or an error code; hexmoe_last_error() gives the
+ * message of the calling thread's last failure.
+ */
+#ifndef HEXMOE_H
+#define HEXMOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define HEXMOE_ABI_VERSION 1
+#define HEXMOE_MAX_TIERS 4
+
+/* Status codes.  The reference raises AssertionError / ValueError for the
+ * argument cases (hex_moe.py:289-290, vllm_hex.py:101-139). */
+enum hexmoe_status {
+  HEXMOE_OK = 0,
+  HEXMOE_E_ARG = 1,         /* bad shape, size, pointer alignment or value     */
+  HEXMOE_E_DTYPE = 2,       /* unsupported dtype code                         */
+  HEXMOE_E_CUDA = 3,        /* a CUDA runtime / driver call failed            */
+  HEXMOE_E_UNSUPPORTED = 4, /* no sm_100 device, or a limit of this build      */
+  HEXMOE_E_DEVICE = 5       /* a kernel flagged an error (see hexmoe_device_status) */
+};
+
+/* Element types of activations / outputs. */
+enum hexmoe_dtype { HEXMOE_F32 = 0, HEXMOE_BF16 = 1, HEXMOE_F16 = 2 };
+/* Element types of expert-id tensors. */
+enum hexmoe_index_dtype { HEXMOE_I32 = 0, HEXMOE_I64 = 1 };
+
+/* One projection of one tier: the four HEX parts, stacked over the tier's experts.
+ * `rows`/`cols` of the stack are given by the owning layer (rows_pad, cols_pad). */
+typedef struct hexmoe_parts {
+  const uint32_t* idx;          /* [n, rows_pad, cols_pad/32*bits]       */
+  const uint8_t* block_scale;   /* [n, rows_pad, cols_pad/block]         */
+  const float* expert_scale;    /* [n]                                   */
+  const float* levels;          /* [n, 2^bits]                           */
+} hexmoe_parts;
+
+/* One tier (runtime/blackhole_runtime/hex_moe.py:174-198, HexTier). */
+typedef struct hexmoe_tier {
+  int32_t bits;                 /* 3 (8 levels) or 4 (16 levels)         */
+  int32_t n;                    /* experts in this tier                  */
+  const int32_t* experts;       /* device int32 [n]: global expert ids   */
+  hexmoe_parts gate, up, down;  /* gate/up: [I, H], down: [H, I]         */
+} hexmoe_tier;
+
+/* A routed-expert SwiGLU MoE layer split over HEX tiers.
+ * hidden_pad / inter_pad are the row lengths the parts are stored with: a
+ * multiple of 128 at least hidden / inter.  They equal hidden / inter for every
+ * production shape (the parts are then read exactly as the reference stores
+ * them); smaller shapes are zero-padded once at load time by the host layer. */
+typedef struct hexmoe_layer_desc {
+  int32_t num_experts;          /* E: global ids are 0..E-1              */
+  int32_t hidden;               /* H                                     */
+  int32_t inter;                /* I (moe_intermediate)                  */
+  int32_t hidden_pad;
+  int32_t inter_pad;
+  int32_t block;                /* fp8 scale block: 32 or 128            */
+  int32_t num_tiers;            /* 1..HEXMOE_MAX_TIERS                   */
+  hexmoe_tier tiers[HEXMOE_MAX_TIERS];
+} hexmoe_layer_desc;
+
+typedef struct hexmoe_layer hexmoe_layer;   /* opaque, immutable after create */
+
+/* Library identity. */
+int hexmoe_abi_version(void);
+const char* hexmoe_last_error(void);
+
+/* Reads (and, with clear != 0, resets) the device error word of `device` that
+ * kernels set on a bounded-wait timeout or an out-of-range expert id.  Blocks
+ * until the device is idle.  0 means no error was recorded. */
+int hexmoe_device_status(int device, int clear, int32_t* status_out);
+
+/* Builds the kernel-side view of a layer (tensor maps over every idx stack,
+ * the global->(tier, local) expert map) on the current device.  Replaces the
+ * per-call argument marshalling of _launch (hex_moe.py:286-301) and the
+ * lookup built in HexTier.prepare (hex_moe.py:193-196). */
+int hexmoe_layer_create(const hexmoe_layer_desc* desc, hexmoe_layer** out);
+int hexmoe_layer_destroy(hexmoe_layer* layer);
+
+/* Scratch bytes hexmoe_forward needs for `tokens` tokens at top-`topk` with
+ * tile height `block_m` (16, 32, 64 or 128; 0 = automatic, as
+ * default_config hex_moe.py:264-283 picks it) and activation dtype x_dtype. */
+size_t hexmoe_forward_workspace_bytes(const hexmoe_layer* layer, int64_t tokens, int32_t topk,
+                                      int32_t block_m, int32_t x_dtype);
+
+/* Routed-expert output out[T, H] = sum_j w[t, j] * down_e(silu(gate_e x_t) * up_e x_t),
+ * e = topk_ids[t, j].  Replaces hex_moe (hex_moe.py:374-382) / hex_moe_fused
+ * (hex_moe.py:304-325).  x [T, H] (row stride H) in x_dtype; topk_weights f32
+ * [T, topk]; topk_ids [T, topk] in ids_dtype (global ids); out [T, H] in
+ * out_dtype (x_dtype, or F32).  The activation handed from gate/up to down is
+ * rounded to the compute dtype (bf16 for F32 inputs) as in the reference. */
+int hexmoe_forward(const hexmoe_layer* layer, const void* x, int32_t x_dtype, int64_t tokens,
+                   int32_t topk, const float* topk_weights, const void* topk_ids,
+                   int32_t ids_dtype, void* out, int32_t out_dtype, int32_t block_m,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* Group slots by expert, each expert's run padded to block_m (align,
+ * hex_moe.py:201-222): sorted_ids int32 [max_blocks*block_m] (padding = S),
+ * expert_ids int32 [max_blocks] (-1 = unused), npp int32 [1] = padded length,
+ * with max_blocks = ceil(S/block_m) + min(E, S).  Stable: slots of one expert
+ * keep their order, so the output equals the reference's bit for bit. */
+size_t hexmoe_align_workspace_bytes(int64_t num_slots, int32_t num_experts);
+int hexmoe_align(const void* ids, int32_t ids_dtype, int64_t num_slots, int32_t num_experts,
+                 int32_t block_m, int32_t* sorted_ids, int32_t* expert_ids, int32_t* npp,
+                 void* workspace, size_t workspace_bytes, void* stream);
+
+/* Dequantize one projection of one tier (the _hex_dequant_kernel launches of
+ * dequant_all, hex_moe.py:154-168 and 328-346): for local expert e < n, row o <
+ * rows, input i < cols,
+ *   out[experts[e] * stride_e + (row_off + o) * stride_row + i]
+ *     = levels[e, code] * (fp8(block_scale[e, o, i/block]) * expert_scale[e])
+ * computed in fp32 with round-to-nearest products, then rounded to out_dtype
+ * (RNE).  Bit-exact against blackhole/anatomy/hex.py:180-204.  experts may be
+ * NULL (then e itself is the output index).  rows_pad/cols_pad: stored shape. */
+int hexmoe_dequant(const hexmoe_parts* parts, int32_t bits, int32_t block, int32_t n,
+                   int32_t rows, int32_t cols, int32_t rows_pad, int32_t cols_pad,
+                   const int32_t* experts, void* out, int32_t out_dtype, int64_t stride_e,
+                   int64_t stride_row, int64_t row_off, void* stream);
+
+/* Router: probabilities = softmax(logits[t, :E]) in fp32, the topk largest
+ * (ties: lower expert id first), renormalised to sum 1 when renormalize != 0
+ * (Qwen3 norm_topk_prob).  logits f32/bf16/f16 [T, E] row stride E.  The
+ * reference leaves routing to vLLM (vllm_hex.py:145-146); this is its
+ * counterpart for callers that route on the device themselves. */
+int hexmoe_route_topk(const void* logits, int32_t logits_dtype, int64_t tokens,
+                      int32_t num_experts, int32_t topk, int32_t renormalize,
+                      float* topk_weights, int32_t* topk_ids, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* HEXMOE_H */
