@@ -1,0 +1,392 @@
+// api.cu — the C ABI of libhexmoe.so (include/hexmoe.h).
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "internal.cuh"
+
+using namespace hexmoe;
+
+struct hexmoe_layer {
+  hexmoe_layer_desc desc;
+  int device;
+  int num_sms;
+  // idx tensor maps per tier: gate, up, down
+  CUtensorMap tm_idx[kMaxTiers][3];
+};
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(HEXMOE_E_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D row-major tensor map: inner dimension `cols` elements, `rows` rows, row
+// pitch `pitch_bytes`, box {box_cols, box_rows}.
+int make_tmap(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t cols, uint64_t rows,
+              uint64_t pitch_bytes, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swz, const char* what) {
+  auto fn = encode_fn();
+  if (!fn) return fail(HEXMOE_E_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  if (reinterpret_cast<uintptr_t>(base) % 16) return fail(HEXMOE_E_ARG, "%s: base address not 16-byte aligned", what);
+  if (pitch_bytes % 16) return fail(HEXMOE_E_ARG, "%s: row pitch %llu not a multiple of 16 bytes", what,
+                                    static_cast<unsigned long long>(pitch_bytes));
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {pitch_bytes};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  (void)elem_bytes;
+  CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(HEXMOE_E_CUDA, "%s: cuTensorMapEncodeTiled failed (%d)", what, static_cast<int>(r));
+  return HEXMOE_OK;
+}
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+int auto_block_m(int64_t S, int32_t E) {
+  const int64_t avg = (S + E - 1) / std::max(E, 1);
+  if (avg <= 16) return 16;
+  if (avg <= 32) return 32;
+  if (avg <= 64) return 64;
+  return 128;
+}
+
+struct WsLayout {
+  size_t sid, eid, npp, xcast, act, y, total;
+  int64_t max_blocks;
+};
+
+WsLayout ws_layout(const hexmoe_layer_desc& d, int64_t T, int32_t k, int32_t bm, int32_t x_dtype) {
+  WsLayout w{};
+  const int64_t S = T * k;
+  w.max_blocks = (S + bm - 1) / bm + std::min<int64_t>(d.num_experts, S);
+  size_t off = 0;
+  w.sid = off; off = align_up(off + sizeof(int32_t) * w.max_blocks * bm, 256);
+  w.eid = off; off = align_up(off + sizeof(int32_t) * w.max_blocks, 256);
+  w.npp = off; off = align_up(off + 16, 256);
+  w.xcast = off; off = align_up(off + (x_dtype == HEXMOE_F32 ? 2 * static_cast<size_t>(T) * d.hidden : 0), 256);
+  w.act = off; off = align_up(off + 2 * static_cast<size_t>(w.max_blocks) * bm * d.inter_pad, 256);
+  w.y = off; off = align_up(off + 2 * static_cast<size_t>(S) * d.hidden, 256);
+  w.total = off;
+  return w;
+}
+
+int check_dtype16(int32_t dt, const char* what) {
+  if (dt != HEXMOE_F32 && dt != HEXMOE_BF16 && dt != HEXMOE_F16) return fail(HEXMOE_E_DTYPE, "%s: bad dtype %d", what, dt);
+  return HEXMOE_OK;
+}
+
+// Shared-memory and TMEM carve-up of one GEMM launch (see GemmParams).
+int plan_gemm(GemmParams& p, bool glu, int bm, int k_pad, int block) {
+  const int nproj = glu ? 2 : 1;
+  const uint32_t spr = static_cast<uint32_t>(k_pad / block);
+  p.sz_scale = static_cast<uint32_t>(align_up(128u * spr, 1024));
+  p.off_scale = 3072;
+  p.off_ring = static_cast<uint32_t>(align_up(p.off_scale + 2u * nproj * p.sz_scale, 1024));
+  p.sz_idx = static_cast<uint32_t>(nproj * 128 * 16 * 4);
+  p.sz_stage = p.sz_idx + static_cast<uint32_t>(align_up(2u * bm * 128u, 1024));
+  const int64_t budget = 232448 - 1024;
+  const int64_t avail = budget - p.off_ring;
+  const int dr = static_cast<int>(std::min<int64_t>(kMaxDR, avail / p.sz_stage));
+  if (dr < 2) return fail(HEXMOE_E_UNSUPPORTED, "reduction length %d with scale block %d needs more shared memory", k_pad, block);
+  p.dr = dr;
+  p.smem_bytes = std::max<uint32_t>(p.off_ring + dr * p.sz_stage + 1024, 120 * 1024);
+  p.acc_stride = static_cast<uint32_t>(nproj * bm);
+  p.a_stride = static_cast<uint32_t>(32 * nproj);
+  p.nbuf = (2 * p.acc_stride + 2 * p.a_stride <= kTmemCols) ? 2 : 1;
+  p.a_base = p.nbuf * p.acc_stride;
+  p.da = static_cast<int>(std::min<uint32_t>(kMaxDA, (kTmemCols - p.a_base) / p.a_stride));
+  if (p.da < 2) return fail(HEXMOE_E_UNSUPPORTED, "block_m %d leaves no tensor memory for operands", bm);
+  return HEXMOE_OK;
+}
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) == cudaSuccess && prev != dev) cudaSetDevice(dev);
+    else prev = -1;
+  }
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+}  // namespace
+
+extern "C" {
+
+int hexmoe_abi_version(void) { return HEXMOE_ABI_VERSION; }
+
+const char* hexmoe_last_error(void) { return g_last_error.c_str(); }
+
+int hexmoe_device_status(int device, int clear, int32_t* status_out) {
+  DeviceGuard g(device);
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "hexmoe_device_status: synchronize");
+  int32_t v = 0;
+  e = read_device_error(&v, clear != 0);
+  if (e != cudaSuccess) return cuda_fail(e, "hexmoe_device_status: read");
+  if (status_out) *status_out = v;
+  return HEXMOE_OK;
+}
+
+int hexmoe_build_expert_map(const hexmoe_layer_desc* desc, int32_t* map_out, void* stream) {
+  if (!desc || !map_out) return fail(HEXMOE_E_ARG, "hexmoe_build_expert_map: null argument");
+  if (desc->num_experts <= 0 || desc->num_tiers < 1 || desc->num_tiers > kMaxTiers)
+    return fail(HEXMOE_E_ARG, "hexmoe_build_expert_map: %d experts, %d tiers", desc->num_experts, desc->num_tiers);
+  if (!device_error_word()) return fail(HEXMOE_E_CUDA, "device error word unavailable");
+  cudaError_t e = launch_build_expert_map(*desc, map_out, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "expert map launch");
+  return HEXMOE_OK;
+}
+
+int hexmoe_layer_create(const hexmoe_layer_desc* desc, hexmoe_layer** out) {
+  if (!desc || !out) return fail(HEXMOE_E_ARG, "hexmoe_layer_create: null argument");
+  *out = nullptr;
+  const hexmoe_layer_desc& d = *desc;
+  if (d.num_experts <= 0 || d.num_experts > 2048) return fail(HEXMOE_E_ARG, "num_experts %d outside 1..2048", d.num_experts);
+  if (d.hidden <= 0 || d.inter <= 0 || d.hidden % 32 || d.inter % 32)
+    return fail(HEXMOE_E_ARG, "hidden %d / inter %d must be positive multiples of 32", d.hidden, d.inter);
+  if (d.hidden_pad < d.hidden || d.inter_pad < d.inter || d.hidden_pad % 128 || d.inter_pad % 128)
+    return fail(HEXMOE_E_ARG, "hidden_pad %d / inter_pad %d must be multiples of 128 covering hidden / inter",
+                d.hidden_pad, d.inter_pad);
+  if (d.block != 32 && d.block != 128) return fail(HEXMOE_E_ARG, "scale block %d is not 32 or 128", d.block);
+  if (d.num_tiers < 1 || d.num_tiers > kMaxTiers) return fail(HEXMOE_E_ARG, "num_tiers %d outside 1..%d", d.num_tiers, kMaxTiers);
+  if (!d.expert_map) return fail(HEXMOE_E_ARG, "expert_map is null");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  int major = 0, minor = 0, sms = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (major != 10 || minor != 0)
+    return fail(HEXMOE_E_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a", dev, major, minor);
+  auto* L = new hexmoe_layer();
+  L->desc = d;
+  L->device = dev;
+  L->num_sms = sms;
+  for (int t = 0; t < d.num_tiers; ++t) {
+    const hexmoe_tier& tr = d.tiers[t];
+    if (tr.bits != 3 && tr.bits != 4) { delete L; return fail(HEXMOE_E_ARG, "tier %d: bits %d is not 3 or 4", t, tr.bits); }
+    if (tr.n <= 0 || tr.n > 65535) { delete L; return fail(HEXMOE_E_ARG, "tier %d: %d experts", t, tr.n); }
+    const hexmoe_parts* parts[3] = {&tr.gate, &tr.up, &tr.down};
+    for (int j = 0; j < 3; ++j) {
+      const hexmoe_parts& pp = *parts[j];
+      if (!pp.idx || !pp.block_scale || !pp.expert_scale || !pp.levels) {
+        delete L;
+        return fail(HEXMOE_E_ARG, "tier %d projection %d: null part", t, j);
+      }
+      if (reinterpret_cast<uintptr_t>(pp.block_scale) % 16) {
+        delete L;
+        return fail(HEXMOE_E_ARG, "tier %d projection %d: block_scale not 16-byte aligned", t, j);
+      }
+      const int rows = j < 2 ? d.inter_pad : d.hidden_pad;
+      const int cols = j < 2 ? d.hidden_pad : d.inter_pad;
+      const uint64_t wpr = static_cast<uint64_t>(cols) / 32 * tr.bits;
+      int rc = make_tmap(&L->tm_idx[t][j], pp.idx, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, wpr,
+                         static_cast<uint64_t>(tr.n) * rows, wpr * 4, 4u * tr.bits, 128, CU_TENSOR_MAP_SWIZZLE_NONE,
+                         "idx tensor map");
+      if (rc != HEXMOE_OK) { delete L; return rc; }
+    }
+  }
+  if (!device_error_word()) { delete L; return fail(HEXMOE_E_CUDA, "device error word unavailable"); }
+  *out = L;
+  return HEXMOE_OK;
+}
+
+int hexmoe_layer_destroy(hexmoe_layer* layer) {
+  delete layer;
+  return HEXMOE_OK;
+}
+
+size_t hexmoe_forward_workspace_bytes(const hexmoe_layer* layer, int64_t tokens, int32_t topk, int32_t block_m,
+                                      int32_t x_dtype) {
+  if (!layer || tokens < 0 || topk <= 0) return 0;
+  const int bm = block_m > 0 ? block_m : auto_block_m(tokens * topk, layer->desc.num_experts);
+  return ws_layout(layer->desc, tokens, topk, bm, x_dtype).total;
+}
+
+int hexmoe_forward(const hexmoe_layer* layer, const void* x, int32_t x_dtype, int64_t tokens, int32_t topk,
+                   const float* topk_weights, const void* topk_ids, int32_t ids_dtype, void* out, int32_t out_dtype,
+                   int32_t block_m, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!layer) return fail(HEXMOE_E_ARG, "hexmoe_forward: null layer");
+  const hexmoe_layer_desc& d = layer->desc;
+  if (tokens < 0 || topk <= 0 || topk > d.num_experts) return fail(HEXMOE_E_ARG, "tokens %lld / topk %d", static_cast<long long>(tokens), topk);
+  if (int rc = check_dtype16(x_dtype, "x")) return rc;
+  if (int rc = check_dtype16(out_dtype, "out")) return rc;
+  if (out_dtype != x_dtype && out_dtype != HEXMOE_F32) return fail(HEXMOE_E_DTYPE, "out dtype must be x dtype or f32");
+  if (ids_dtype != HEXMOE_I32 && ids_dtype != HEXMOE_I64) return fail(HEXMOE_E_DTYPE, "ids dtype %d", ids_dtype);
+  if (tokens == 0) return HEXMOE_OK;
+  if (!x || !topk_weights || !topk_ids || !out || !workspace) return fail(HEXMOE_E_ARG, "hexmoe_forward: null pointer");
+  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(out) % 16 ||
+      reinterpret_cast<uintptr_t>(workspace) % 256)
+    return fail(HEXMOE_E_ARG, "x / out must be 16-byte and workspace 256-byte aligned");
+  const int64_t S = tokens * topk;
+  if (S >= (1ll << 31) - 1) return fail(HEXMOE_E_ARG, "too many slots");
+  const int bm = block_m > 0 ? block_m : auto_block_m(S, d.num_experts);
+  if (bm != 16 && bm != 32 && bm != 64 && bm != 128) return fail(HEXMOE_E_ARG, "block_m %d not in {16, 32, 64, 128}", bm);
+  const WsLayout w = ws_layout(d, tokens, topk, bm, x_dtype);
+  if (workspace_bytes < w.total)
+    return fail(HEXMOE_E_ARG, "workspace %zu bytes < %zu needed", workspace_bytes, w.total);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev != layer->device) return fail(HEXMOE_E_ARG, "layer was created on device %d, current device is %d", layer->device, dev);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int32_t* dev_err = device_error_word();
+  if (!dev_err) return fail(HEXMOE_E_CUDA, "device error word unavailable");
+  char* ws = static_cast<char*>(workspace);
+  int32_t* sid = reinterpret_cast<int32_t*>(ws + w.sid);
+  int32_t* eid = reinterpret_cast<int32_t*>(ws + w.eid);
+  int32_t* npp = reinterpret_cast<int32_t*>(ws + w.npp);
+  void* act = ws + w.act;
+  void* y = ws + w.y;
+  const bool bf16 = x_dtype != HEXMOE_F16;     // f32 activations are computed in bf16
+  const void* x16 = x;
+  cudaError_t e;
+  if (x_dtype == HEXMOE_F32) {
+    x16 = ws + w.xcast;
+    e = launch_cast_to16(static_cast<const float*>(x), ws + w.xcast, true, tokens * d.hidden, st);
+    if (e != cudaSuccess) return cuda_fail(e, "cast");
+  }
+  e = launch_align(topk_ids, ids_dtype == HEXMOE_I64, S, d.num_experts, bm, sid, eid, npp, nullptr, 0, dev_err, st, true);
+  if (e != cudaSuccess) return cuda_fail(e, "align launch");
+
+  const CUtensorMapDataType dt16 = bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  // ---- gate/up
+  GemmParams p{};
+  for (int t = 0; t < d.num_tiers; ++t) {
+    p.tm_idx[t][0] = layer->tm_idx[t][0];
+    p.tm_idx[t][1] = layer->tm_idx[t][1];
+    p.bs[t][0] = d.tiers[t].gate.block_scale; p.bs[t][1] = d.tiers[t].up.block_scale;
+    p.es[t][0] = d.tiers[t].gate.expert_scale; p.es[t][1] = d.tiers[t].up.expert_scale;
+    p.lev[t][0] = d.tiers[t].gate.levels; p.lev[t][1] = d.tiers[t].up.levels;
+    p.bits[t] = d.tiers[t].bits;
+  }
+  p.num_tiers = d.num_tiers;
+  p.expert_map = d.expert_map;
+  p.num_experts = d.num_experts;
+  p.sorted_ids = sid; p.expert_ids = eid; p.npp = npp;
+  p.bm = bm; p.max_blocks = static_cast<int32_t>(w.max_blocks);
+  p.num_slots = static_cast<int32_t>(S); p.topk = topk;
+  p.rows_pad = d.inter_pad; p.rows_store = d.inter_pad;
+  p.k_pad = d.hidden_pad; p.block = d.block;
+  p.m_tiles = d.inter_pad / kTileM;
+  p.out = act; p.ld_out = d.inter_pad;
+  p.topk_w = topk_weights;
+  p.dev_err = dev_err;
+  if (int rc = plan_gemm(p, true, bm, d.hidden_pad, d.block)) return rc;
+  if (int rc = make_tmap(&p.tm_b, x16, dt16, 2, d.hidden, tokens, 2ull * d.hidden, 64, 1,
+                         CU_TENSOR_MAP_SWIZZLE_128B, "x tensor map"))
+    return rc;
+  int grid = static_cast<int>(std::min<int64_t>(layer->num_sms, w.max_blocks * p.m_tiles));
+  e = launch_gemm(p, true, bf16, grid, st, true);
+  if (e != cudaSuccess) return cuda_fail(e, "gate/up launch");
+
+  // ---- down
+  GemmParams q = p;
+  for (int t = 0; t < d.num_tiers; ++t) {
+    q.tm_idx[t][0] = layer->tm_idx[t][2];
+    q.bs[t][0] = d.tiers[t].down.block_scale; q.bs[t][1] = nullptr;
+    q.es[t][0] = d.tiers[t].down.expert_scale; q.es[t][1] = nullptr;
+    q.lev[t][0] = d.tiers[t].down.levels; q.lev[t][1] = nullptr;
+  }
+  q.topk = 1;
+  q.rows_pad = d.hidden_pad; q.rows_store = d.hidden;
+  q.k_pad = d.inter_pad;
+  q.m_tiles = d.hidden_pad / kTileM;
+  q.out = y; q.ld_out = d.hidden;
+  if (int rc = plan_gemm(q, false, bm, d.inter_pad, d.block)) return rc;
+  if (int rc = make_tmap(&q.tm_b, act, dt16, 2, d.inter_pad, static_cast<uint64_t>(w.max_blocks) * bm,
+                         2ull * d.inter_pad, 64, static_cast<uint32_t>(bm), CU_TENSOR_MAP_SWIZZLE_128B, "act tensor map"))
+    return rc;
+  grid = static_cast<int>(std::min<int64_t>(layer->num_sms, w.max_blocks * q.m_tiles));
+  e = launch_gemm(q, false, bf16, grid, st, true);
+  if (e != cudaSuccess) return cuda_fail(e, "down launch");
+
+  // ---- combine
+  e = launch_combine(y, bf16 ? HEXMOE_BF16 : HEXMOE_F16, tokens, topk, d.hidden, d.hidden, out, out_dtype, st, true);
+  if (e != cudaSuccess) return cuda_fail(e, "combine launch");
+  return HEXMOE_OK;
+}
+
+size_t hexmoe_align_workspace_bytes(int64_t num_slots, int32_t num_experts) {
+  return align_scratch_bytes(num_slots, num_experts);
+}
+
+int hexmoe_align(const void* ids, int32_t ids_dtype, int64_t num_slots, int32_t num_experts, int32_t block_m,
+                 int32_t* sorted_ids, int32_t* expert_ids, int32_t* npp, void* workspace, size_t workspace_bytes,
+                 void* stream) {
+  if (ids_dtype != HEXMOE_I32 && ids_dtype != HEXMOE_I64) return fail(HEXMOE_E_DTYPE, "ids dtype %d", ids_dtype);
+  if (num_slots < 0 || num_slots >= (1ll << 31) - 1) return fail(HEXMOE_E_ARG, "num_slots %lld", static_cast<long long>(num_slots));
+  if (num_experts <= 0 || num_experts > 2048) return fail(HEXMOE_E_ARG, "num_experts %d outside 1..2048", num_experts);
+  if (block_m <= 0) return fail(HEXMOE_E_ARG, "block_m %d", block_m);
+  if (!npp || (num_slots > 0 && (!ids || !sorted_ids || !expert_ids))) return fail(HEXMOE_E_ARG, "hexmoe_align: null pointer");
+  (void)workspace;
+  (void)workspace_bytes;
+  int32_t* dev_err = device_error_word();
+  if (!dev_err) return fail(HEXMOE_E_CUDA, "device error word unavailable");
+  cudaError_t e = launch_align(ids, ids_dtype == HEXMOE_I64, num_slots, num_experts, block_m, sorted_ids, expert_ids,
+                               npp, nullptr, 0, dev_err, static_cast<cudaStream_t>(stream), false);
+  if (e != cudaSuccess) return cuda_fail(e, "align launch");
+  return HEXMOE_OK;
+}
+
+int hexmoe_dequant(const hexmoe_parts* parts, int32_t bits, int32_t block, int32_t n, int32_t rows, int32_t cols,
+                   int32_t rows_pad, int32_t cols_pad, const int32_t* experts, void* out, int32_t out_dtype,
+                   int64_t stride_e, int64_t stride_row, int64_t row_off, void* stream) {
+  if (!parts || !out) return fail(HEXMOE_E_ARG, "hexmoe_dequant: null pointer");
+  if (bits != 3 && bits != 4) return fail(HEXMOE_E_ARG, "bits %d is not 3 or 4", bits);
+  if (block != 32 && block != 128) return fail(HEXMOE_E_ARG, "scale block %d is not 32 or 128", block);
+  if (n < 0 || rows < 0 || cols < 0 || cols % 32 || rows_pad < rows || cols_pad < cols || cols_pad % block)
+    return fail(HEXMOE_E_ARG, "hexmoe_dequant: bad shape n=%d rows=%d cols=%d pad=%d,%d", n, rows, cols, rows_pad, cols_pad);
+  if (check_dtype16(out_dtype, "out")) return HEXMOE_E_DTYPE;
+  cudaError_t e = launch_dequant(*parts, bits, block, n, rows, cols, rows_pad, cols_pad, experts, out, out_dtype,
+                                 stride_e, stride_row, row_off, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "dequant launch");
+  return HEXMOE_OK;
+}
+
+int hexmoe_route_topk(const void* logits, int32_t logits_dtype, int64_t tokens, int32_t num_experts, int32_t topk,
+                      int32_t renormalize, float* topk_weights, int32_t* topk_ids, void* stream) {
+  if (check_dtype16(logits_dtype, "logits")) return HEXMOE_E_DTYPE;
+  if (tokens < 0 || num_experts <= 0 || topk <= 0 || topk > 32 || topk > num_experts)
+    return fail(HEXMOE_E_ARG, "route_topk: tokens %lld experts %d topk %d", static_cast<long long>(tokens), num_experts, topk);
+  if (tokens > 0 && (!logits || !topk_weights || !topk_ids)) return fail(HEXMOE_E_ARG, "route_topk: null pointer");
+  cudaError_t e = launch_route_topk(logits, logits_dtype, tokens, num_experts, topk, renormalize, topk_weights,
+                                    topk_ids, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "route_topk launch");
+  return HEXMOE_OK;
+}
+
+}  // extern "C"

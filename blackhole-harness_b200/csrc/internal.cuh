@@ -1,0 +1,82 @@
+// internal.cuh — structures shared by the C ABI (api.cu) and the kernels.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "hexmoe.h"
+
+namespace hexmoe {
+
+constexpr int kMaxTiers = HEXMOE_MAX_TIERS;
+constexpr int kTileM = 128;      // weight rows per tile (UMMA M)
+constexpr int kKStep = 128;      // reduction elements per TMA stage of index words
+constexpr int kMaxDR = 8;        // deepest index/activation ring
+constexpr int kMaxDA = 8;        // deepest TMEM operand ring
+constexpr int kGemmThreads = 448;  // 14 warps: TMA, MMA, 4 epilogue, 8 decode
+constexpr uint32_t kTmemCols = 512;
+
+// Everything the grouped-GEMM kernel needs; passed by value as a
+// __grid_constant__ parameter (tensor maps must live in parameter space).
+struct GemmParams {
+  CUtensorMap tm_idx[kMaxTiers][2];  // idx stacks viewed as [n*rows_pad, k_pad/32*bits] u32
+  CUtensorMap tm_b;                  // B rows: x [T, H] (gate/up) or act [rows, I_pad] (down)
+  const uint8_t* bs[kMaxTiers][2];
+  const float* es[kMaxTiers][2];
+  const float* lev[kMaxTiers][2];
+  int32_t bits[kMaxTiers];
+  int32_t num_tiers;
+  const int32_t* expert_map;   // [E]: (tier << 16) | local, -1 = no tier
+  int32_t num_experts;
+  const int32_t* sorted_ids;   // [max_blocks * bm], align() layout
+  const int32_t* expert_ids;   // [max_blocks]
+  const int32_t* npp;          // [1]
+  int32_t bm;                  // tokens per tile (align block_m), multiple of 16, <= 128
+  int32_t max_blocks;
+  int32_t num_slots;           // S = T * topk
+  int32_t topk;                // slot -> token divisor for the gate/up gather
+  int32_t rows_pad;            // weight rows per expert in the stack
+  int32_t rows_store;          // rows written to the output (<= rows_pad)
+  int32_t k_pad;               // reduction length (multiple of 128)
+  int32_t block;               // scale block: 32 or 128
+  int32_t m_tiles;             // rows_pad / 128
+  // shared-memory carve-up (byte offsets from the 1024-aligned base)
+  int32_t dr;                  // index/activation ring depth
+  uint32_t off_scale, sz_scale;  // two tile-scale buffers
+  uint32_t off_ring, sz_idx, sz_stage;  // ring stage = idx part + B part
+  uint32_t smem_bytes;         // dynamic shared memory to request
+  // TMEM carve-up (columns)
+  int32_t nbuf;                // accumulator buffers (1 or 2)
+  int32_t da;                  // operand ring depth
+  uint32_t acc_stride;         // columns per accumulator buffer
+  uint32_t a_base, a_stride;   // operand ring: first column, columns per stage
+  // output
+  void* out;                   // gate/up: act [max_blocks*bm, ld_out]; down: y [S, ld_out]
+  int64_t ld_out;
+  const float* topk_w;         // down: [S]
+  int32_t* dev_err;
+};
+
+// Launches the persistent grouped GEMM (gate/up with SwiGLU when glu, else down
+// with the top-k weight); returns a cudaError_t.
+cudaError_t launch_gemm(const GemmParams& p, bool glu, bool bf16, int grid, cudaStream_t stream, bool pdl);
+
+// Small kernels (kernels.cu).
+cudaError_t launch_align(const void* ids, bool ids64, int64_t S, int32_t E, int32_t bm, int32_t* sid, int32_t* eid,
+                         int32_t* npp, int32_t* scratch, size_t scratch_bytes, int32_t* dev_err, cudaStream_t st,
+                         bool pdl);
+size_t align_scratch_bytes(int64_t S, int32_t E);
+cudaError_t launch_dequant(const hexmoe_parts& parts, int bits, int block, int n, int rows, int cols, int rows_pad,
+                           int cols_pad, const int32_t* experts, void* out, int out_dtype, int64_t stride_e,
+                           int64_t stride_row, int64_t row_off, cudaStream_t st);
+cudaError_t launch_combine(const void* y, int y_dtype, int64_t T, int32_t topk, int32_t H, int64_t ld_y, void* out,
+                           int out_dtype, cudaStream_t st, bool pdl);
+cudaError_t launch_cast_to16(const float* x, void* out, bool bf16, int64_t n, cudaStream_t st);
+cudaError_t launch_route_topk(const void* logits, int dtype, int64_t T, int32_t E, int32_t k, int renorm, float* w,
+                              int32_t* ids, cudaStream_t st);
+int32_t* device_error_word();  // address of this device's error word (nullptr on failure)
+cudaError_t read_device_error(int32_t* value, bool clear);   // synchronous, current device
+cudaError_t launch_build_expert_map(const hexmoe_layer_desc& d, int32_t* map, cudaStream_t st);
+
+}  // namespace hexmoe

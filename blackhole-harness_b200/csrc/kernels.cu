@@ -1,0 +1,424 @@
+// kernels.cu — the small kernels around the grouped GEMM: the align plan, the
+// bit-exact dequantization, the top-k combine, the fp32 -> 16-bit cast and
+// the router.
+#include <cub/block/block_scan.cuh>
+
+#include "decode.cuh"
+#include "internal.cuh"
+
+namespace hexmoe {
+
+// Device error word: bit flags of DeviceError, set by any kernel of this library.
+__device__ int32_t g_dev_err;
+
+int32_t* device_error_word() {
+  static int32_t* addr[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (!addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_dev_err) != cudaSuccess) return nullptr;
+    addr[dev] = static_cast<int32_t*>(p);
+  }
+  return addr[dev];
+}
+
+cudaError_t read_device_error(int32_t* value, bool clear) {
+  cudaError_t e = cudaMemcpyFromSymbol(value, g_dev_err, sizeof(int32_t));
+  if (e != cudaSuccess || !clear) return e;
+  const int32_t z = 0;
+  return cudaMemcpyToSymbol(g_dev_err, &z, sizeof(z));
+}
+
+// global expert -> (tier << 16) | local; -1 where no tier holds the expert.
+__global__ void expert_map_kernel(hexmoe_layer_desc d, int32_t* map) {
+  for (int e = threadIdx.x; e < d.num_experts; e += blockDim.x) map[e] = -1;
+  __syncthreads();
+  for (int t = 0; t < d.num_tiers; ++t)
+    for (int i = threadIdx.x; i < d.tiers[t].n; i += blockDim.x) {
+      const int g = d.tiers[t].experts[i];
+      if (g >= 0 && g < d.num_experts) map[g] = (t << 16) | i;
+      else atomicOr(&g_dev_err, kDevErrExpertId);
+    }
+}
+
+cudaError_t launch_build_expert_map(const hexmoe_layer_desc& d, int32_t* map, cudaStream_t st) {
+  expert_map_kernel<<<1, 1024, 0, st>>>(d, map);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// align (runtime/blackhole_runtime/hex_moe.py:201-222), one CTA, stable.
+//
+// The S slots are cut into kAlignWarps contiguous segments, one per warp.
+// Pass 1: each warp counts its segment per expert (32 slots at a time, lanes
+// with the same expert grouped by __match_any_sync, the group leader adds the
+// group size) into its own row of hist[warp][E].  Pass 2: per expert, the
+// exclusive prefix of the rows over warps (so segment w starts after all
+// earlier segments' slots of that expert), the expert's count and block
+// count, and an exclusive scan of the block counts over experts.  Pass 3:
+// each warp walks its segment again in order; a slot's place inside its
+// expert's run is the running count of its warp's row plus its rank among
+// equal lanes of the chunk.  Together that is the order of a stable sort.
+constexpr int kAlignWarps = 16;
+constexpr int kAlignThreads = kAlignWarps * 32;
+constexpr int kAlignMaxExperts = 2048;
+
+template <bool I64>
+__global__ void __launch_bounds__(kAlignThreads, 1)
+    align_kernel(const void* __restrict__ ids_raw, int64_t S, int32_t E, int32_t bm, int32_t* __restrict__ sid,
+                 int32_t* __restrict__ eid, int32_t* __restrict__ npp, int32_t* dev_err) {
+  extern __shared__ int32_t sh[];
+  int32_t* hist = sh;                                  // [kAlignWarps][E]
+  int32_t* blk_start = sh + kAlignWarps * E;           // [E]
+  int32_t* counts = blk_start + E;                     // [E]
+  using Scan = cub::BlockScan<int32_t, kAlignThreads>;
+  __shared__ typename Scan::TempStorage scan_tmp;
+  __shared__ int32_t total_blocks;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_wait();
+  for (int i = threadIdx.x; i < kAlignWarps * E; i += kAlignThreads) hist[i] = 0;
+  __syncthreads();
+
+  const int64_t seg = (S + kAlignWarps - 1) / kAlignWarps;
+  const int64_t s_begin = warp * seg;
+  const int64_t s_end = s_begin + seg < S ? s_begin + seg : S;
+  auto load_id = [&](int64_t s) -> int32_t {
+    int64_t v = I64 ? static_cast<const int64_t*>(ids_raw)[s] : static_cast<const int32_t*>(ids_raw)[s];
+    if (v < 0 || v >= E) {
+      atomicOr(dev_err, kDevErrExpertId);
+      return -1;
+    }
+    return static_cast<int32_t>(v);
+  };
+  int32_t* my_hist = hist + warp * E;
+  // pass 1
+  for (int64_t c0 = s_begin; c0 < s_end; c0 += 32) {
+    const int64_t s = c0 + lane;
+    const int32_t e = s < s_end ? load_id(s) : -1;
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    if (e >= 0 && (peers & ((1u << lane) - 1u)) == 0) my_hist[e] += __popc(peers);
+    __syncwarp();
+  }
+  __syncthreads();
+  // pass 2: prefix over warps, counts, block counts
+  constexpr int kPer = kAlignMaxExperts / kAlignThreads;   // experts per thread (contiguous)
+  int32_t nblk[kPer];
+  int32_t local_sum = 0;
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int e = threadIdx.x * kPer + j;
+    nblk[j] = 0;
+    if (e < E) {
+      int32_t acc = 0;
+      for (int w = 0; w < kAlignWarps; ++w) {
+        const int32_t v = hist[w * E + e];
+        hist[w * E + e] = acc;
+        acc += v;
+      }
+      counts[e] = acc;
+      nblk[j] = (acc + bm - 1) / bm;
+      local_sum += nblk[j];
+    }
+  }
+  int32_t excl;
+  int32_t agg;
+  Scan(scan_tmp).ExclusiveSum(local_sum, excl, agg);
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int e = threadIdx.x * kPer + j;
+    if (e < E) {
+      blk_start[e] = excl;
+      excl += nblk[j];
+    }
+  }
+  if (threadIdx.x == 0) {
+    total_blocks = agg;
+    npp[0] = agg * bm;
+  }
+  __syncthreads();
+  const int64_t max_blocks = (S + bm - 1) / bm + (E < S ? E : S);
+  // expert of every block; padding of every run and of the tail
+  for (int e = warp; e < E; e += kAlignWarps) {
+    const int32_t b0 = blk_start[e];
+    const int32_t nb = (counts[e] + bm - 1) / bm;
+    for (int j = lane; j < nb; j += 32) eid[b0 + j] = e;
+    for (int64_t i = static_cast<int64_t>(b0) * bm + counts[e] + lane; i < static_cast<int64_t>(b0 + nb) * bm;
+         i += 32)
+      sid[i] = static_cast<int32_t>(S);
+  }
+  for (int64_t b = total_blocks + threadIdx.x; b < max_blocks; b += kAlignThreads) eid[b] = -1;
+  for (int64_t i = static_cast<int64_t>(total_blocks) * bm + threadIdx.x; i < max_blocks * bm; i += kAlignThreads)
+    sid[i] = static_cast<int32_t>(S);
+  // pass 3: scatter in stable order
+  for (int64_t c0 = s_begin; c0 < s_end; c0 += 32) {
+    const int64_t s = c0 + lane;
+    const int32_t e = s < s_end ? load_id(s) : -1;
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    int32_t base = 0;
+    if (e >= 0) base = my_hist[e];
+    __syncwarp();
+    if (e >= 0) {
+      const int rank = __popc(peers & ((1u << lane) - 1u));
+      sid[static_cast<int64_t>(blk_start[e]) * bm + base + rank] = static_cast<int32_t>(s);
+      if (rank == 0) my_hist[e] = base + __popc(peers);
+    }
+    __syncwarp();
+  }
+  pdl_launch_dependents();
+}
+
+size_t align_scratch_bytes(int64_t, int32_t) { return 0; }
+
+cudaError_t launch_align(const void* ids, bool ids64, int64_t S, int32_t E, int32_t bm, int32_t* sid, int32_t* eid,
+                         int32_t* npp, int32_t*, size_t, int32_t* dev_err, cudaStream_t st, bool pdl) {
+  if (E > kAlignMaxExperts) return cudaErrorInvalidValue;
+  const size_t smem = static_cast<size_t>(kAlignWarps + 2) * E * sizeof(int32_t);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(kAlignThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaError_t e;
+  if (ids64) {
+    static bool cfgd = false;
+    if (!cfgd) {
+      e = cudaFuncSetAttribute(align_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (kAlignWarps + 2) * kAlignMaxExperts * 4);
+      if (e != cudaSuccess) return e;
+      cfgd = true;
+    }
+    return cudaLaunchKernelEx(&cfg, align_kernel<true>, ids, S, E, bm, sid, eid, npp, dev_err);
+  }
+  static bool cfgd32 = false;
+  if (!cfgd32) {
+    e = cudaFuncSetAttribute(align_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (kAlignWarps + 2) * kAlignMaxExperts * 4);
+    if (e != cudaSuccess) return e;
+    cfgd32 = true;
+  }
+  return cudaLaunchKernelEx(&cfg, align_kernel<false>, ids, S, E, bm, sid, eid, npp, dev_err);
+}
+
+// ---------------------------------------------------------------------------
+// Dequantization (blackhole/anatomy/hex.py:180-204; the reference kernel is
+// _hex_dequant_kernel, runtime/blackhole_runtime/hex_moe.py:154-168).  One
+// thread per (expert, row, 32-input block): w = levels[code] * (fp8 * es),
+// both products rounded to nearest in fp32, then to the output type.
+template <int OUT>  // HEXMOE_F32 / HEXMOE_BF16 / HEXMOE_F16
+__global__ void dequant_kernel(hexmoe_parts parts, int bits, int block, int n, int rows, int cols, int rows_pad,
+                               int cols_pad, const int32_t* __restrict__ experts, void* __restrict__ out,
+                               int64_t stride_e, int64_t stride_row, int64_t row_off) {
+  const int nblk = cols / 32;
+  const int64_t total = static_cast<int64_t>(n) * rows * nblk;
+  const int wpr = cols_pad / 32 * bits;
+  const int spr = cols_pad / block;
+  const int L = 1 << bits;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int blk = static_cast<int>(i % nblk);
+    const int64_t er = i / nblk;
+    const int o = static_cast<int>(er % rows);
+    const int e = static_cast<int>(er / rows);
+    const int64_t rrow = static_cast<int64_t>(e) * rows_pad + o;
+    const uint32_t* wp = parts.idx + rrow * wpr + blk * bits;
+    uint32_t w[4];
+    for (int j = 0; j < bits; ++j) w[j] = __ldg(wp + j);
+    const uint32_t code = __ldg(parts.block_scale + rrow * spr + (blk * 32) / block);
+    const float s = __fmul_rn(fp8_hex_value(code), __ldg(parts.expert_scale + e));
+    const float* lev = parts.levels + static_cast<int64_t>(e) * L;
+    const int ge = experts ? __ldg(experts + e) : e;
+    char* dst = static_cast<char*>(out);
+    const int64_t base = ge * stride_e + (row_off + o) * stride_row + static_cast<int64_t>(blk) * 32;
+#pragma unroll 4
+    for (int j = 0; j < 32; ++j) {
+      const int off = j * bits;
+      const int wi = off >> 5, sh = off & 31;
+      uint32_t v = w[wi] >> sh;
+      if (sh + bits > 32) v |= w[wi + 1] << (32 - sh);
+      const float val = __fmul_rn(__ldg(lev + (v & (L - 1))), s);
+      if (OUT == HEXMOE_F32) reinterpret_cast<float*>(dst)[base + j] = val;
+      else if (OUT == HEXMOE_BF16) reinterpret_cast<__nv_bfloat16*>(dst)[base + j] = __float2bfloat16_rn(val);
+      else reinterpret_cast<__half*>(dst)[base + j] = __float2half_rn(val);
+    }
+  }
+}
+
+cudaError_t launch_dequant(const hexmoe_parts& parts, int bits, int block, int n, int rows, int cols, int rows_pad,
+                           int cols_pad, const int32_t* experts, void* out, int out_dtype, int64_t stride_e,
+                           int64_t stride_row, int64_t row_off, cudaStream_t st) {
+  const int64_t total = static_cast<int64_t>(n) * rows * (cols / 32);
+  if (total == 0) return cudaSuccess;
+  const int threads = 256;
+  const int64_t want = (total + threads - 1) / threads;
+  const int grid = static_cast<int>(want < 148 * 16 ? want : 148 * 16);
+  if (out_dtype == HEXMOE_F32)
+    dequant_kernel<HEXMOE_F32><<<grid, threads, 0, st>>>(parts, bits, block, n, rows, cols, rows_pad, cols_pad,
+                                                         experts, out, stride_e, stride_row, row_off);
+  else if (out_dtype == HEXMOE_BF16)
+    dequant_kernel<HEXMOE_BF16><<<grid, threads, 0, st>>>(parts, bits, block, n, rows, cols, rows_pad, cols_pad,
+                                                          experts, out, stride_e, stride_row, row_off);
+  else
+    dequant_kernel<HEXMOE_F16><<<grid, threads, 0, st>>>(parts, bits, block, n, rows, cols, rows_pad, cols_pad,
+                                                         experts, out, stride_e, stride_row, row_off);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Combine (runtime/blackhole_runtime/hex_moe.py:325, y.view(T, k, H).sum(1)):
+// out[t, h] = sum_j y[t*k + j, h], fp32 accumulation in slot order.
+template <typename YT, int OUT>
+__global__ void combine_kernel(const YT* __restrict__ y, int64_t T, int32_t k, int32_t H, int64_t ld_y,
+                               void* __restrict__ out) {
+  pdl_wait();
+  const int hv = H / 8;
+  const int64_t total = T * hv;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t t = i / hv;
+    const int h8 = static_cast<int>(i % hv) * 8;
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int j = 0; j < k; ++j) {
+      const uint4 v = *reinterpret_cast<const uint4*>(y + (t * k + j) * ld_y + h8);
+      const YT* e = reinterpret_cast<const YT*>(&v);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) acc[q] += static_cast<float>(e[q]);
+    }
+    const int64_t o = t * H + h8;
+    if (OUT == HEXMOE_F32) {
+      float4* d = reinterpret_cast<float4*>(static_cast<float*>(out) + o);
+      d[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      d[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    } else {
+      uint4 r;
+      uint32_t* rr = reinterpret_cast<uint32_t*>(&r);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) rr[q] = pack2<OUT == HEXMOE_BF16>(acc[2 * q], acc[2 * q + 1]);
+      *reinterpret_cast<uint4*>(static_cast<uint16_t*>(out) + o) = r;
+    }
+  }
+}
+
+template <typename YT>
+static cudaError_t combine_dispatch(const YT* y, int64_t T, int32_t k, int32_t H, int64_t ld_y, void* out,
+                                    int out_dtype, cudaStream_t st, bool pdl) {
+  const int64_t total = T * (H / 8);
+  if (total == 0) return cudaSuccess;
+  const int threads = 256;
+  const int64_t want = (total + threads - 1) / threads;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(want < 148 * 8 ? want : 148 * 8));
+  cfg.blockDim = dim3(threads);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  if (out_dtype == HEXMOE_F32) return cudaLaunchKernelEx(&cfg, combine_kernel<YT, HEXMOE_F32>, y, T, k, H, ld_y, out);
+  if (out_dtype == HEXMOE_BF16)
+    return cudaLaunchKernelEx(&cfg, combine_kernel<YT, HEXMOE_BF16>, y, T, k, H, ld_y, out);
+  return cudaLaunchKernelEx(&cfg, combine_kernel<YT, HEXMOE_F16>, y, T, k, H, ld_y, out);
+}
+
+cudaError_t launch_combine(const void* y, int y_dtype, int64_t T, int32_t topk, int32_t H, int64_t ld_y, void* out,
+                           int out_dtype, cudaStream_t st, bool pdl) {
+  if (y_dtype == HEXMOE_BF16)
+    return combine_dispatch(static_cast<const __nv_bfloat16*>(y), T, topk, H, ld_y, out, out_dtype, st, pdl);
+  return combine_dispatch(static_cast<const __half*>(y), T, topk, H, ld_y, out, out_dtype, st, pdl);
+}
+
+// ---------------------------------------------------------------------------
+__global__ void cast_kernel(const float* __restrict__ x, uint16_t* __restrict__ out, bool bf16, int64_t n) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    if (bf16) {
+      const __nv_bfloat16 v = __float2bfloat16_rn(x[i]);
+      out[i] = *reinterpret_cast<const uint16_t*>(&v);
+    } else {
+      const __half v = __float2half_rn(x[i]);
+      out[i] = *reinterpret_cast<const uint16_t*>(&v);
+    }
+  }
+}
+
+cudaError_t launch_cast_to16(const float* x, void* out, bool bf16, int64_t n, cudaStream_t st) {
+  if (n == 0) return cudaSuccess;
+  const int64_t want = (n + 255) / 256;
+  cast_kernel<<<static_cast<unsigned>(want < 148 * 8 ? want : 148 * 8), 256, 0, st>>>(
+      x, static_cast<uint16_t*>(out), bf16, n);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Router: one warp per token.  softmax in fp32, then k rounds of a warp-wide
+// arg-max (ties -> lower expert id), optional renormalisation.
+template <int DT>
+__global__ void route_topk_kernel(const void* __restrict__ logits, int64_t T, int32_t E, int32_t k, int renorm,
+                                  float* __restrict__ w, int32_t* __restrict__ ids) {
+  const int lane = threadIdx.x & 31;
+  const int64_t t = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+  if (t >= T) return;
+  auto logit = [&](int e) -> float {
+    const int64_t i = t * E + e;
+    if (DT == HEXMOE_F32) return static_cast<const float*>(logits)[i];
+    if (DT == HEXMOE_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(logits)[i]);
+    return __half2float(static_cast<const __half*>(logits)[i]);
+  };
+  float m = -INFINITY;
+  for (int e = lane; e < E; e += 32) m = fmaxf(m, logit(e));
+  for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  float sum = 0.f;
+  for (int e = lane; e < E; e += 32) sum += expf(logit(e) - m);
+  for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const float inv = 1.0f / sum;
+  // k rounds; experts already chosen are skipped by id (k <= 32)
+  float picked_w[32];
+  int picked_id[32];
+  float wsum = 0.f;
+  for (int r = 0; r < k; ++r) {
+    float best = -INFINITY;
+    int bid = 0x7fffffff;
+    for (int e = lane; e < E; e += 32) {
+      bool used = false;
+      for (int q = 0; q < r; ++q) used |= picked_id[q] == e;
+      if (used) continue;
+      const float v = logit(e);
+      if (v > best || (v == best && e < bid)) { best = v; bid = e; }
+    }
+    for (int o = 16; o; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bid, o);
+      if (ob > best || (ob == best && oi < bid)) { best = ob; bid = oi; }
+    }
+    picked_id[r] = bid;
+    picked_w[r] = expf(best - m) * inv;
+    wsum += picked_w[r];
+  }
+  if (lane == 0) {
+    for (int r = 0; r < k; ++r) {
+      w[t * k + r] = renorm ? picked_w[r] / wsum : picked_w[r];
+      ids[t * k + r] = picked_id[r];
+    }
+  }
+}
+
+cudaError_t launch_route_topk(const void* logits, int dtype, int64_t T, int32_t E, int32_t k, int renorm, float* w,
+                              int32_t* ids, cudaStream_t st) {
+  if (T == 0) return cudaSuccess;
+  const int threads = 256;
+  const unsigned grid = static_cast<unsigned>((T * 32 + threads - 1) / threads);
+  if (dtype == HEXMOE_F32) route_topk_kernel<HEXMOE_F32><<<grid, threads, 0, st>>>(logits, T, E, k, renorm, w, ids);
+  else if (dtype == HEXMOE_BF16)
+    route_topk_kernel<HEXMOE_BF16><<<grid, threads, 0, st>>>(logits, T, E, k, renorm, w, ids);
+  else route_topk_kernel<HEXMOE_F16><<<grid, threads, 0, st>>>(logits, T, E, k, renorm, w, ids);
+  return cudaGetLastError();
+}
+
+}  // namespace hexmoe

@@ -31,6 +31,12 @@
 extern "C" {
 #endif
 
+#if defined(__GNUC__)
+#define HEXMOE_API __attribute__((visibility("default")))
+#else
+#define HEXMOE_API
+#endif
+
 #define HEXMOE_ABI_VERSION 1
 #define HEXMOE_MAX_TIERS 4
 
@@ -81,30 +87,38 @@ typedef struct hexmoe_layer_desc {
   int32_t block;                /* fp8 scale block: 32 or 128            */
   int32_t num_tiers;            /* 1..HEXMOE_MAX_TIERS                   */
   hexmoe_tier tiers[HEXMOE_MAX_TIERS];
+  /* device int32 [num_experts]: (tier << 16) | local index of every global
+   * expert, -1 where no tier holds it (hexmoe_build_expert_map fills it) */
+  const int32_t* expert_map;
 } hexmoe_layer_desc;
 
 typedef struct hexmoe_layer hexmoe_layer;   /* opaque, immutable after create */
 
 /* Library identity. */
-int hexmoe_abi_version(void);
-const char* hexmoe_last_error(void);
+HEXMOE_API int hexmoe_abi_version(void);
+HEXMOE_API const char* hexmoe_last_error(void);
 
 /* Reads (and, with clear != 0, resets) the device error word of `device` that
  * kernels set on a bounded-wait timeout or an out-of-range expert id.  Blocks
  * until the device is idle.  0 means no error was recorded. */
-int hexmoe_device_status(int device, int clear, int32_t* status_out);
+HEXMOE_API int hexmoe_device_status(int device, int clear, int32_t* status_out);
+
+/* Fills map_out[num_experts] (device) from desc->tiers[].experts: the
+ * global -> (tier, local) lookup of HexTier.prepare (hex_moe.py:193-196),
+ * for all tiers at once.  desc->expert_map is not read. */
+HEXMOE_API int hexmoe_build_expert_map(const hexmoe_layer_desc* desc, int32_t* map_out, void* stream);
 
 /* Builds the kernel-side view of a layer (tensor maps over every idx stack,
  * the global->(tier, local) expert map) on the current device.  Replaces the
  * per-call argument marshalling of _launch (hex_moe.py:286-301) and the
  * lookup built in HexTier.prepare (hex_moe.py:193-196). */
-int hexmoe_layer_create(const hexmoe_layer_desc* desc, hexmoe_layer** out);
-int hexmoe_layer_destroy(hexmoe_layer* layer);
+HEXMOE_API int hexmoe_layer_create(const hexmoe_layer_desc* desc, hexmoe_layer** out);
+HEXMOE_API int hexmoe_layer_destroy(hexmoe_layer* layer);
 
 /* Scratch bytes hexmoe_forward needs for `tokens` tokens at top-`topk` with
  * tile height `block_m` (16, 32, 64 or 128; 0 = automatic, as
  * default_config hex_moe.py:264-283 picks it) and activation dtype x_dtype. */
-size_t hexmoe_forward_workspace_bytes(const hexmoe_layer* layer, int64_t tokens, int32_t topk,
+HEXMOE_API size_t hexmoe_forward_workspace_bytes(const hexmoe_layer* layer, int64_t tokens, int32_t topk,
                                       int32_t block_m, int32_t x_dtype);
 
 /* Routed-expert output out[T, H] = sum_j w[t, j] * down_e(silu(gate_e x_t) * up_e x_t),
@@ -113,7 +127,7 @@ size_t hexmoe_forward_workspace_bytes(const hexmoe_layer* layer, int64_t tokens,
  * [T, topk]; topk_ids [T, topk] in ids_dtype (global ids); out [T, H] in
  * out_dtype (x_dtype, or F32).  The activation handed from gate/up to down is
  * rounded to the compute dtype (bf16 for F32 inputs) as in the reference. */
-int hexmoe_forward(const hexmoe_layer* layer, const void* x, int32_t x_dtype, int64_t tokens,
+HEXMOE_API int hexmoe_forward(const hexmoe_layer* layer, const void* x, int32_t x_dtype, int64_t tokens,
                    int32_t topk, const float* topk_weights, const void* topk_ids,
                    int32_t ids_dtype, void* out, int32_t out_dtype, int32_t block_m,
                    void* workspace, size_t workspace_bytes, void* stream);
@@ -123,8 +137,8 @@ int hexmoe_forward(const hexmoe_layer* layer, const void* x, int32_t x_dtype, in
  * expert_ids int32 [max_blocks] (-1 = unused), npp int32 [1] = padded length,
  * with max_blocks = ceil(S/block_m) + min(E, S).  Stable: slots of one expert
  * keep their order, so the output equals the reference's bit for bit. */
-size_t hexmoe_align_workspace_bytes(int64_t num_slots, int32_t num_experts);
-int hexmoe_align(const void* ids, int32_t ids_dtype, int64_t num_slots, int32_t num_experts,
+HEXMOE_API size_t hexmoe_align_workspace_bytes(int64_t num_slots, int32_t num_experts);
+HEXMOE_API int hexmoe_align(const void* ids, int32_t ids_dtype, int64_t num_slots, int32_t num_experts,
                  int32_t block_m, int32_t* sorted_ids, int32_t* expert_ids, int32_t* npp,
                  void* workspace, size_t workspace_bytes, void* stream);
 
@@ -136,7 +150,7 @@ int hexmoe_align(const void* ids, int32_t ids_dtype, int64_t num_slots, int32_t 
  * computed in fp32 with round-to-nearest products, then rounded to out_dtype
  * (RNE).  Bit-exact against blackhole/anatomy/hex.py:180-204.  experts may be
  * NULL (then e itself is the output index).  rows_pad/cols_pad: stored shape. */
-int hexmoe_dequant(const hexmoe_parts* parts, int32_t bits, int32_t block, int32_t n,
+HEXMOE_API int hexmoe_dequant(const hexmoe_parts* parts, int32_t bits, int32_t block, int32_t n,
                    int32_t rows, int32_t cols, int32_t rows_pad, int32_t cols_pad,
                    const int32_t* experts, void* out, int32_t out_dtype, int64_t stride_e,
                    int64_t stride_row, int64_t row_off, void* stream);
@@ -146,7 +160,7 @@ int hexmoe_dequant(const hexmoe_parts* parts, int32_t bits, int32_t block, int32
  * (Qwen3 norm_topk_prob).  logits f32/bf16/f16 [T, E] row stride E.  The
  * reference leaves routing to vLLM (vllm_hex.py:145-146); this is its
  * counterpart for callers that route on the device themselves. */
-int hexmoe_route_topk(const void* logits, int32_t logits_dtype, int64_t tokens,
+HEXMOE_API int hexmoe_route_topk(const void* logits, int32_t logits_dtype, int64_t tokens,
                       int32_t num_experts, int32_t topk, int32_t renormalize,
                       float* topk_weights, int32_t* topk_ids, void* stream);
 

@@ -1,0 +1,263 @@
+"""GPU parity: libhexmoe.so through its C ABI (via the blackhole_b200 host layer)
+against the CPU oracle and the reference's golden vectors.
+
+Bars: dequantization bit-exact (f32) and equal to the nearest-even rounding of
+the f32 value (bf16 / f16); align bit-exact; layer outputs within
+rtol 2e-2 / atol 1e-2 of the oracle's fp32 moe_reference (the benchmark spec's
+tolerance).  Shapes follow the reference's own test (runtime/tests/
+test_hex_moe.py: E=12, H=128, I=64, k=4, T in 1/3/40) and the benchmark configs.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+from conftest import golden, golden_tiers
+from helpers import hex_tiers, np_tiers, rel_err, within
+
+from blackhole_b200 import hex_data as hd
+
+pytestmark = pytest.mark.gpu
+
+DEV = torch.device("cuda", 0)
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _clean_error_word():
+    from blackhole_b200.hex_moe import device_status
+    device_status(0, clear=True)
+    yield
+    assert device_status(0, clear=True) == 0, "a kernel set the device error word"
+
+
+def _bits(a: np.ndarray) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
+
+
+# ----------------------------------------------------------------------------- dequant
+
+
+@pytest.mark.parametrize("bits", [3, 4])
+def test_dequant_f32_bitexact_vs_reference_golden(bits):
+    from blackhole_b200.hex_moe import HexTier, dequant_all
+    z = golden(f"dequant_b{bits}.npz")
+    n, rows, cols = z["W"].shape                     # 3 x 20 x 96: gate-shaped stack
+    parts = {q: torch.as_tensor(z[q]).to(DEV) for q in ("idx", "block_scale", "expert_scale", "levels")}
+    # a one-tier layer whose gate/up/down all use these parts is not shape-consistent
+    # (down is [H, I]); dequantize through the C ABI directly instead
+    import ctypes
+    from blackhole_b200 import _lib
+    out = torch.empty(n, rows, cols, dtype=torch.float32, device=DEV)
+    p = _lib.Parts(parts["idx"].data_ptr(), parts["block_scale"].data_ptr(), parts["expert_scale"].data_ptr(),
+                   parts["levels"].data_ptr())
+    rc = _lib.lib.hexmoe_dequant(ctypes.byref(p), bits, 32, n, rows, cols, rows, cols, None, out.data_ptr(), _lib.F32,
+                                 out.stride(0), out.stride(1), 0, torch.cuda.current_stream().cuda_stream)
+    _lib.check(rc)
+    torch.cuda.synchronize()
+    assert np.array_equal(_bits(out.cpu().numpy()), _bits(z["W"]))
+    del HexTier, dequant_all
+
+
+@pytest.mark.parametrize("bits,block", [(3, 32), (4, 32), (3, 128), (4, 128)])
+def test_dequant_all_bitexact_vs_oracle(oracle, bits, block):
+    from blackhole_b200.hex_moe import dequant_all
+    E, H, I = 6, 256, 384
+    L = hd.synth_layer(E, H, I, str(bits), block, seed=20 + bits)
+    tiers = hex_tiers(L.tiers, E, DEV)
+    w13, w2 = dequant_all(tiers, torch.float32)
+    w13b, w2b = dequant_all(tiers, torch.bfloat16)
+    w13h, _ = dequant_all(tiers, torch.float16)
+    npt = np_tiers(L.tiers)[0]
+    g = oracle.dequant(npt["gate_proj"], bits, block)
+    u = oracle.dequant(npt["up_proj"], bits, block)
+    d = oracle.dequant(npt["down_proj"], bits, block)
+    got13 = w13.cpu().numpy()
+    assert np.array_equal(_bits(got13[:, :I]), _bits(g)) and np.array_equal(_bits(got13[:, I:]), _bits(u))
+    assert np.array_equal(_bits(w2.cpu().numpy()), _bits(d))
+    assert torch.equal(w13b.cpu(), torch.as_tensor(got13).to(torch.bfloat16))          # RNE of the f32 value
+    assert torch.equal(w2b.cpu(), torch.as_tensor(d).to(torch.bfloat16))
+    assert torch.equal(w13h.cpu(), torch.as_tensor(got13).to(torch.float16))
+
+
+def test_dequant_all_mixed_tiers_global_order(oracle):
+    from blackhole_b200.hex_moe import dequant_all
+    E, H, I = 10, 128, 256
+    L = hd.synth_layer(E, H, I, "mixed", 32, seed=5)
+    tiers = hex_tiers(L.tiers, E, DEV)
+    w13, w2 = dequant_all(tiers, torch.float32)
+    for t in np_tiers(L.tiers):
+        d = oracle.dequant(t["down_proj"], t["bits"], 32)
+        for local, e in enumerate(t["experts"].tolist()):
+            assert np.array_equal(_bits(w2[e].cpu().numpy()), _bits(d[local]))
+
+
+# ----------------------------------------------------------------------------- align
+
+
+def test_align_bitexact_vs_reference_golden():
+    from blackhole_b200.hex_moe import align
+    z = golden("align.npz")
+    names = sorted({k.rsplit("_", 1)[0] for k in z if k.endswith("_ids")})
+    for name in names:
+        n, bm = (int(v) for v in z[f"{name}_meta"])
+        for dt in (torch.int64, torch.int32):
+            ids = torch.as_tensor(z[f"{name}_ids"]).to(dt).to(DEV)
+            sid, eid, npp = align(ids, n, bm)
+            torch.cuda.synchronize()
+            assert np.array_equal(sid.cpu().numpy(), z[f"{name}_sid"]), name
+            assert np.array_equal(eid.cpu().numpy(), z[f"{name}_eid"]), name
+            assert np.array_equal(npp.cpu().numpy(), z[f"{name}_npp"]), name
+
+
+@pytest.mark.parametrize("S,E,bm", [(262144, 96, 128), (131072, 128, 64), (4096, 2048, 16), (100000, 7, 32)])
+def test_align_large_vs_oracle(oracle, S, E, bm):
+    from blackhole_b200.hex_moe import align
+    g = torch.Generator().manual_seed(S + E)
+    ids = torch.randint(0, E, (S,), generator=g)
+    sid, eid, npp = align(ids.to(DEV), E, bm)
+    want = oracle.align(ids.numpy(), E, bm)
+    assert np.array_equal(sid.cpu().numpy(), want[0])
+    assert np.array_equal(eid.cpu().numpy(), want[1])
+    assert np.array_equal(npp.cpu().numpy(), want[2])
+
+
+# ----------------------------------------------------------------------------- layer
+
+
+def _run_layer(oracle, L, w, ids, x, block_m=None, act="bfloat16"):
+    from blackhole_b200.hex_moe import hex_moe
+    tiers = hex_tiers(L.tiers, L.E, DEV)
+    cfg = {"BLOCK_M": block_m} if block_m else None
+    got = hex_moe(x.to(DEV), w.to(DEV), ids.to(DEV), tiers, cfg).float().cpu().numpy()
+    want = oracle.moe_reference(x.float().numpy(), w.numpy(), ids.numpy(), np_tiers(L.tiers), L.E, block=L.block,
+                                act_dtype=act)
+    return got, want
+
+
+@pytest.mark.parametrize("T", [1, 3, 40])
+def test_layer_matches_reference_golden_bf16(T):
+    """The reference's own test shapes and data (E=12, H=128, I=64 padded to one tile),
+    bf16 activations, against the reference moe_reference output."""
+    from blackhole_b200.hex_moe import HexTier, hex_moe
+    z = golden(f"moe_ref_T{T}.npz")
+    E = int(z["E"])
+    tiers = []
+    for t in golden_tiers(z):
+        parts = [{q: torch.as_tensor(v).to(DEV) for q, v in t[p].items()} for p in ("gate_proj", "up_proj", "down_proj")]
+        tiers.append(HexTier(t["bits"], torch.as_tensor(t["experts"]).to(DEV), *parts).prepare(E))
+    x = torch.as_tensor(z["xbf16"]).to(torch.bfloat16).to(DEV)
+    w = torch.as_tensor(z["w"]).to(DEV)
+    ids = torch.as_tensor(z["ids"]).to(DEV)
+    for path in ("auto", "fused", "dequant"):
+        got = hex_moe(x, w, ids, tiers, path=path).float().cpu().numpy()
+        assert within(got, z["out_bf16"]), (path, rel_err(got, z["out_bf16"]))
+    for bm in (16, 32, 64, 128):
+        got = hex_moe(x, w, ids, tiers, {"BLOCK_M": bm}).float().cpu().numpy()
+        assert within(got, z["out_bf16"]), (bm, rel_err(got, z["out_bf16"]))
+    # fp32 activations: computed in bf16 inside, returned in fp32
+    got32 = hex_moe(torch.as_tensor(z["x32"]).to(DEV), w, ids, tiers)
+    assert got32.dtype == torch.float32
+    assert within(got32.cpu().numpy(), z["out_f32"]), rel_err(got32.cpu().numpy(), z["out_f32"])
+
+
+def test_layer_cfg1_tiny_config(oracle):
+    c = hd.CONFIGS["cfg1"]
+    L = hd.synth_layer(c["E"], c["H"], c["I"], c["bits"], c["block"], seed=1)
+    w, ids = hd.synth_routing(c["T"][0], c["E"], c["k"], seed=2)
+    x = hd.synth_x(c["T"][0], c["H"], seed=3)
+    got, want = _run_layer(oracle, L, w, ids, x)
+    assert within(got, want), rel_err(got, want)
+    # and against the reference's own output on the same inputs (golden)
+    z = golden("moe_cfg1.npz")
+    assert within(got, z["out_bf16"]), rel_err(got, z["out_bf16"])
+
+
+@pytest.mark.parametrize("T", [1, 8, 64])
+def test_layer_decode_cfg2_shape(oracle, T):
+    c = hd.CONFIGS["cfg2"]
+    L = hd.synth_layer(c["E"], c["H"], c["I"], "3", c["block"], seed=7)
+    w, ids = hd.synth_routing(T, c["E"], c["k"], seed=T)
+    x = hd.synth_x(T, c["H"], seed=100 + T)
+    got, want = _run_layer(oracle, L, w, ids, x)
+    assert within(got, want), rel_err(got, want)
+
+
+@pytest.mark.parametrize("bits,block,bm", [("mixed", 128, 0), ("mixed", 32, 64), ("4", 32, 128), ("3", 128, 32)])
+def test_layer_prefill_mixed_tiers(oracle, bits, block, bm):
+    E, H, I, k, T = 24, 512, 384, 4, 700
+    L = hd.synth_layer(E, H, I, bits, block, seed=31)
+    w, ids = hd.synth_routing(T, E, k, seed=32)
+    x = hd.synth_x(T, H, seed=33)
+    got, want = _run_layer(oracle, L, w, ids, x, block_m=bm or None)
+    assert within(got, want), rel_err(got, want)
+
+
+def test_layer_fp16_activations(oracle):
+    E, H, I, k, T = 16, 256, 256, 4, 50
+    L = hd.synth_layer(E, H, I, "mixed", 32, seed=41)
+    w, ids = hd.synth_routing(T, E, k, seed=42)
+    x = hd.synth_x(T, H, seed=43, dtype=torch.float16)
+    got, want = _run_layer(oracle, L, w, ids, x, act="float16")
+    assert within(got, want), rel_err(got, want)
+
+
+def test_layer_skewed_routing_and_empty_experts(oracle):
+    """Zipf-skewed routing (many blocks for hot experts, empty experts) and a
+    batch where every token picks the same experts."""
+    E, H, I, k = 32, 256, 256, 4
+    L = hd.synth_layer(E, H, I, "3", 128, seed=51)
+    w, ids = hd.synth_routing(600, E, k, seed=52, zipf=1.2)
+    x = hd.synth_x(600, H, seed=53)
+    got, want = _run_layer(oracle, L, w, ids, x, block_m=32)
+    assert within(got, want), rel_err(got, want)
+    ids2 = torch.arange(k).repeat(300, 1)
+    w2 = torch.full((300, k), 1.0 / k)
+    x2 = hd.synth_x(300, H, seed=54)
+    got, want = _run_layer(oracle, L, w2, ids2, x2, block_m=16)
+    assert within(got, want), rel_err(got, want)
+
+
+def test_layer_empty_batch():
+    from blackhole_b200.hex_moe import hex_moe
+    L = hd.synth_layer(8, 128, 128, "3", 32, seed=1)
+    tiers = hex_tiers(L.tiers, 8, DEV)
+    out = hex_moe(torch.zeros(0, 128, dtype=torch.bfloat16, device=DEV), torch.zeros(0, 2, device=DEV),
+                  torch.zeros(0, 2, dtype=torch.long, device=DEV), tiers)
+    assert out.shape == (0, 128)
+
+
+def test_layer_deterministic_and_graph_capturable(oracle):
+    from blackhole_b200.hex_moe import hex_moe
+    E, H, I, k, T = 16, 256, 256, 4, 32
+    L = hd.synth_layer(E, H, I, "3", 128, seed=61)
+    tiers = hex_tiers(L.tiers, E, DEV)
+    w, ids = hd.synth_routing(T, E, k, seed=62)
+    x = hd.synth_x(T, H, seed=63).to(DEV)
+    w, ids = w.to(DEV), ids.to(DEV)
+    a = hex_moe(x, w, ids, tiers)
+    b = hex_moe(x, w, ids, tiers)
+    assert torch.equal(a, b)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        hex_moe(x, w, ids, tiers)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        c = hex_moe(x, w, ids, tiers)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(a, c)
+
+
+def test_route_topk_vs_torch():
+    from blackhole_b200.hex_moe import route_topk
+    g = torch.Generator().manual_seed(3)
+    for E, k in ((96, 8), (128, 8), (8, 2)):
+        logits = torch.randn(257, E, generator=g)
+        w, ids = route_topk(logits.to(DEV), k, renormalize=True)
+        p = torch.softmax(logits, -1)
+        ws, is_ = torch.topk(p, k, -1)
+        ws = ws / ws.sum(-1, keepdim=True)
+        assert torch.allclose(w.cpu(), ws, atol=1e-6, rtol=1e-5)
+        assert torch.equal(ids.cpu().long(), is_)
