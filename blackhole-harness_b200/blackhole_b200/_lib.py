@@ -22,6 +22,7 @@ EXPORTS = (
     "hexmoe_abi_version", "hexmoe_last_error", "hexmoe_device_status", "hexmoe_build_expert_map",
     "hexmoe_layer_create", "hexmoe_layer_destroy", "hexmoe_forward_workspace_bytes", "hexmoe_forward",
     "hexmoe_align_workspace_bytes", "hexmoe_align", "hexmoe_dequant", "hexmoe_route_topk",
+    "hexmoe_gather", "hexmoe_gate_up", "hexmoe_down", "hexmoe_combine",
 )
 
 
@@ -61,6 +62,10 @@ def _load() -> ctypes.CDLL:
         "hexmoe_dequant": (ctypes.c_int, [P, I32_, I32_, I32_, I32_, I32_, I32_, I32_, P, P, I32_, I64_, I64_, I64_,
                                           P]),
         "hexmoe_route_topk": (ctypes.c_int, [P, I32_, I64_, I32_, I32_, I32_, P, P, P]),
+        "hexmoe_gather": (ctypes.c_int, [P, I32_, I64_, I32_, I32_, I32_, P, P, I32_, P, P]),
+        "hexmoe_gate_up": (ctypes.c_int, [P, P, I32_, I64_, I32_, P, P, P, I32_, P, P]),
+        "hexmoe_down": (ctypes.c_int, [P, P, I32_, I64_, I32_, P, P, P, P, I32_, P, P]),
+        "hexmoe_combine": (ctypes.c_int, [P, I32_, I64_, I32_, I32_, P, I32_, P]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)

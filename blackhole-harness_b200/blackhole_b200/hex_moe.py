@@ -207,6 +207,59 @@ class _Layer:
         return out
 
 
+    # -- the phases of forward(), for callers that time or drive them apart
+    def plan(self, topk_ids: torch.Tensor, block_m: int):
+        return align(topk_ids.reshape(-1), self.E, block_m)
+
+    def max_blocks(self, slots: int, block_m: int) -> int:
+        return -(-slots // block_m) + min(self.E, slots)
+
+    def gather(self, x: torch.Tensor, k: int, plan, block_m: int, xs: torch.Tensor | None = None) -> torch.Tensor:
+        """Plan-ordered activation rows (16-bit; bf16 for fp32 x)."""
+        sid, _, npp = plan
+        T = x.shape[0]
+        dt = torch.bfloat16 if x.dtype == torch.float32 else x.dtype
+        if xs is None:
+            xs = torch.empty(self.max_blocks(T * k, block_m) * block_m, self.H, dtype=dt, device=x.device)
+        with torch.cuda.device(x.device):
+            rc = _lib.lib.hexmoe_gather(_ptr(x), _DT[x.dtype], T, self.H, k, self.E, _ptr(sid), _ptr(npp), block_m,
+                                        _ptr(xs), _stream(x.device))
+        _lib.check(rc, "hexmoe_gather")
+        return xs
+
+    def gate_up(self, xs: torch.Tensor, T: int, k: int, plan, block_m: int,
+                act: torch.Tensor | None = None) -> torch.Tensor:
+        sid, eid, npp = plan
+        if act is None:
+            act = torch.empty(self.max_blocks(T * k, block_m) * block_m, self.desc.inter_pad, dtype=xs.dtype,
+                              device=xs.device)
+        with torch.cuda.device(xs.device):
+            rc = _lib.lib.hexmoe_gate_up(self.handle, _ptr(xs), _DT[xs.dtype], T, k, _ptr(sid), _ptr(eid), _ptr(npp),
+                                         block_m, _ptr(act), _stream(xs.device))
+        _lib.check(rc, "hexmoe_gate_up")
+        return act
+
+    def down(self, act: torch.Tensor, topk_weights: torch.Tensor, plan, block_m: int,
+             y: torch.Tensor | None = None) -> torch.Tensor:
+        sid, eid, npp = plan
+        T, k = topk_weights.shape
+        if y is None:
+            y = torch.empty(T * k, self.H, dtype=act.dtype, device=act.device)
+        with torch.cuda.device(act.device):
+            rc = _lib.lib.hexmoe_down(self.handle, _ptr(act), _DT[act.dtype], T, k, _ptr(topk_weights), _ptr(sid),
+                                      _ptr(eid), _ptr(npp), block_m, _ptr(y), _stream(act.device))
+        _lib.check(rc, "hexmoe_down")
+        return y
+
+    def combine(self, y: torch.Tensor, T: int, k: int, out_dtype=None) -> torch.Tensor:
+        out = torch.empty(T, self.H, dtype=out_dtype or y.dtype, device=y.device)
+        with torch.cuda.device(y.device):
+            rc = _lib.lib.hexmoe_combine(_ptr(y), _DT[y.dtype], T, k, self.H, _ptr(out), _DT[out.dtype],
+                                         _stream(y.device))
+        _lib.check(rc, "hexmoe_combine")
+        return out
+
+
 def _layer(tiers: list[HexTier]) -> _Layer:
     key = tuple((id(t), _ptr(t.kernel_parts["gate_proj"]["idx"])) for t in tiers)
     cache = tiers[0].__dict__.setdefault("_b200_layers", {})
@@ -214,6 +267,12 @@ def _layer(tiers: list[HexTier]) -> _Layer:
     if L is None:
         L = cache[key] = _Layer(tiers)
     return L
+
+
+def layer_for(tiers: list[HexTier]) -> _Layer:
+    """The (cached) C-ABI layer handle of prepared tiers, with the phase calls
+    plan / gate_up / down / combine of hex_moe_fused."""
+    return _layer(tiers)
 
 
 def align(ids: torch.Tensor, n: int, block_m: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:

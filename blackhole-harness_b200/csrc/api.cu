@@ -16,8 +16,10 @@ struct hexmoe_layer {
   hexmoe_layer_desc desc;
   int device;
   int num_sms;
-  // idx tensor maps per tier: gate, up, down
-  CUtensorMap tm_idx[kMaxTiers][3];
+  int max_bits;
+  // idx tensor maps per tier (gate, up, down) and index-stage width
+  // (k_idx = 128, 256, 384, 512 -> slot 0..3; unused where k_idx does not divide)
+  CUtensorMap tm_idx[kMaxTiers][3][4];
 };
 
 namespace {
@@ -82,7 +84,7 @@ int auto_block_m(int64_t S, int32_t E) {
 }
 
 struct WsLayout {
-  size_t sid, eid, npp, xcast, act, y, total;
+  size_t sid, eid, npp, xs, act, y, total;
   int64_t max_blocks;
 };
 
@@ -94,7 +96,8 @@ WsLayout ws_layout(const hexmoe_layer_desc& d, int64_t T, int32_t k, int32_t bm,
   w.sid = off; off = align_up(off + sizeof(int32_t) * w.max_blocks * bm, 256);
   w.eid = off; off = align_up(off + sizeof(int32_t) * w.max_blocks, 256);
   w.npp = off; off = align_up(off + 16, 256);
-  w.xcast = off; off = align_up(off + (x_dtype == HEXMOE_F32 ? 2 * static_cast<size_t>(T) * d.hidden : 0), 256);
+  (void)x_dtype;
+  w.xs = off; off = align_up(off + 2 * static_cast<size_t>(w.max_blocks) * bm * d.hidden, 256);
   w.act = off; off = align_up(off + 2 * static_cast<size_t>(w.max_blocks) * bm * d.inter_pad, 256);
   w.y = off; off = align_up(off + 2 * static_cast<size_t>(S) * d.hidden, 256);
   w.total = off;
@@ -106,21 +109,38 @@ int check_dtype16(int32_t dt, const char* what) {
   return HEXMOE_OK;
 }
 
-// Shared-memory and TMEM carve-up of one GEMM launch (see GemmParams).
-int plan_gemm(GemmParams& p, bool glu, int bm, int k_pad, int block) {
+// Shared-memory and TMEM carve-up of one GEMM launch (see GemmParams).  The
+// index ring takes the widest stage (k_idx of 512, 384, 256 or 128 inputs)
+// that divides k_pad and still leaves an activation ring of useful depth:
+// TMA moves one box row per few cycles, so wide rows are what feed HBM rate.
+int plan_gemm(GemmParams& p, bool glu, int bm, int k_pad, int block, int max_bits) {
   const int nproj = glu ? 2 : 1;
   const uint32_t spr = static_cast<uint32_t>(k_pad / block);
   p.sz_scale = static_cast<uint32_t>(align_up(128u * spr, 1024));
-  p.off_scale = 3072;
-  p.off_ring = static_cast<uint32_t>(align_up(p.off_scale + 2u * nproj * p.sz_scale, 1024));
-  p.sz_idx = static_cast<uint32_t>(nproj * 128 * 16 * 4);
-  p.sz_stage = p.sz_idx + static_cast<uint32_t>(align_up(2u * bm * 128u, 1024));
-  const int64_t budget = 232448 - 1024;
-  const int64_t avail = budget - p.off_ring;
-  const int dr = static_cast<int>(std::min<int64_t>(kMaxDR, avail / p.sz_stage));
-  if (dr < 2) return fail(HEXMOE_E_UNSUPPORTED, "reduction length %d with scale block %d needs more shared memory", k_pad, block);
-  p.dr = dr;
-  p.smem_bytes = std::max<uint32_t>(p.off_ring + dr * p.sz_stage + 1024, 120 * 1024);
+  p.off_tab = 8192;                                    // after control block, fp8 table, tile records
+  p.off_scale = static_cast<uint32_t>(align_up(p.off_tab + 2u * nproj * 512u * 16u, 1024));
+  p.off_idx = static_cast<uint32_t>(align_up(p.off_scale + 2u * nproj * p.sz_scale, 1024));
+  p.sz_b = static_cast<uint32_t>(align_up(2u * bm * 128u, 1024));
+  const int64_t budget = 232448 - 1024 - p.off_idx;
+  const int db_min = bm >= 64 ? 3 : 4;
+  p.di = 0;
+  for (int k_idx : {512, 384, 256, 128}) {
+    if (k_pad % k_idx) continue;
+    const uint32_t sz = static_cast<uint32_t>(align_up(static_cast<size_t>(nproj) * 128 * k_idx * max_bits / 8, 1024));
+    for (int di = kMaxDI; di >= 2; --di) {
+      const int64_t rem = budget - static_cast<int64_t>(di) * sz;
+      if (rem <= 0) continue;
+      const int db = static_cast<int>(std::min<int64_t>(kMaxDB, rem / p.sz_b));
+      if (db >= db_min || (k_idx == 128 && db >= 2)) {
+        p.k_idx = k_idx; p.sz_idx = sz; p.di = di; p.db = db;
+        break;
+      }
+    }
+    if (p.di) break;
+  }
+  if (!p.di) return fail(HEXMOE_E_UNSUPPORTED, "reduction length %d / block_m %d do not fit shared memory", k_pad, bm);
+  p.off_b = static_cast<uint32_t>(align_up(p.off_idx + static_cast<size_t>(p.di) * p.sz_idx, 1024));
+  p.smem_bytes = std::max<uint32_t>(p.off_b + p.db * p.sz_b + 1024, 120 * 1024);
   p.acc_stride = static_cast<uint32_t>(nproj * bm);
   p.a_stride = static_cast<uint32_t>(32 * nproj);
   p.nbuf = (2 * p.acc_stride + 2 * p.a_stride <= kTmemCols) ? 2 : 1;
@@ -140,6 +160,95 @@ struct DeviceGuard {
     if (prev >= 0) cudaSetDevice(prev);
   }
 };
+
+
+int run_gate_up(const hexmoe_layer* layer, const void* xs, bool bf16, int64_t tokens, int32_t topk,
+                const int32_t* sid, const int32_t* eid, const int32_t* npp, int32_t bm, void* act, int32_t* dev_err,
+                cudaStream_t st, bool pdl) {
+  const hexmoe_layer_desc& d = layer->desc;
+  const int64_t S = tokens * topk;
+  const int64_t max_blocks = (S + bm - 1) / bm + std::min<int64_t>(d.num_experts, S);
+  const CUtensorMapDataType dt16 = bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  GemmParams p{};
+  for (int t = 0; t < d.num_tiers; ++t) {
+    p.bs[t][0] = d.tiers[t].gate.block_scale; p.bs[t][1] = d.tiers[t].up.block_scale;
+    p.es[t][0] = d.tiers[t].gate.expert_scale; p.es[t][1] = d.tiers[t].up.expert_scale;
+    p.lev[t][0] = d.tiers[t].gate.levels; p.lev[t][1] = d.tiers[t].up.levels;
+    p.bits[t] = d.tiers[t].bits;
+  }
+  p.num_tiers = d.num_tiers;
+  p.expert_map = d.expert_map;
+  p.num_experts = d.num_experts;
+  p.sorted_ids = sid; p.expert_ids = eid; p.npp = npp;
+  p.bm = bm; p.max_blocks = static_cast<int32_t>(max_blocks);
+  p.num_slots = static_cast<int32_t>(S);
+  p.rows_pad = d.inter_pad; p.rows_store = d.inter_pad;
+  p.k_pad = d.hidden_pad; p.block = d.block;
+  p.m_tiles = d.inter_pad / kTileM;
+  p.out = act; p.ld_out = d.inter_pad;
+  p.topk_w = nullptr;
+  p.dev_err = dev_err;
+  if (int rc = plan_gemm(p, true, bm, d.hidden_pad, d.block, layer->max_bits)) return rc;
+  for (int t = 0; t < d.num_tiers; ++t) {
+    p.tm_idx[t][0] = layer->tm_idx[t][0][p.k_idx / 128 - 1];
+    p.tm_idx[t][1] = layer->tm_idx[t][1][p.k_idx / 128 - 1];
+  }
+  if (int rc = make_tmap(&p.tm_b, xs, dt16, 2, d.hidden, static_cast<uint64_t>(max_blocks) * bm, 2ull * d.hidden, 64,
+                         static_cast<uint32_t>(bm), CU_TENSOR_MAP_SWIZZLE_128B, "x_sorted tensor map"))
+    return rc;
+  const int grid = static_cast<int>(std::min<int64_t>(layer->num_sms, max_blocks * p.m_tiles));
+  cudaError_t e = launch_gemm(p, true, bf16, grid, st, pdl);
+  if (e != cudaSuccess) return cuda_fail(e, "gate/up launch");
+  return HEXMOE_OK;
+}
+
+int run_down(const hexmoe_layer* layer, const void* act, bool bf16, int64_t tokens, int32_t topk,
+             const float* topk_weights, const int32_t* sid, const int32_t* eid, const int32_t* npp, int32_t bm,
+             void* y, int32_t* dev_err, cudaStream_t st, bool pdl) {
+  const hexmoe_layer_desc& d = layer->desc;
+  const int64_t S = tokens * topk;
+  const int64_t max_blocks = (S + bm - 1) / bm + std::min<int64_t>(d.num_experts, S);
+  const CUtensorMapDataType dt16 = bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  GemmParams q{};
+  for (int t = 0; t < d.num_tiers; ++t) {
+    q.bs[t][0] = d.tiers[t].down.block_scale;
+    q.es[t][0] = d.tiers[t].down.expert_scale;
+    q.lev[t][0] = d.tiers[t].down.levels;
+    q.bits[t] = d.tiers[t].bits;
+  }
+  q.num_tiers = d.num_tiers;
+  q.expert_map = d.expert_map;
+  q.num_experts = d.num_experts;
+  q.sorted_ids = sid; q.expert_ids = eid; q.npp = npp;
+  q.bm = bm; q.max_blocks = static_cast<int32_t>(max_blocks);
+  q.num_slots = static_cast<int32_t>(S);
+  q.rows_pad = d.hidden_pad; q.rows_store = d.hidden;
+  q.k_pad = d.inter_pad; q.block = d.block;
+  q.m_tiles = d.hidden_pad / kTileM;
+  q.out = y; q.ld_out = d.hidden;
+  q.topk_w = topk_weights;
+  q.dev_err = dev_err;
+  if (int rc = plan_gemm(q, false, bm, d.inter_pad, d.block, layer->max_bits)) return rc;
+  for (int t = 0; t < d.num_tiers; ++t) q.tm_idx[t][0] = layer->tm_idx[t][2][q.k_idx / 128 - 1];
+  if (int rc = make_tmap(&q.tm_b, act, dt16, 2, d.inter_pad, static_cast<uint64_t>(max_blocks) * bm,
+                         2ull * d.inter_pad, 64, static_cast<uint32_t>(bm), CU_TENSOR_MAP_SWIZZLE_128B, "act tensor map"))
+    return rc;
+  const int grid = static_cast<int>(std::min<int64_t>(layer->num_sms, max_blocks * q.m_tiles));
+  cudaError_t e = launch_gemm(q, false, bf16, grid, st, pdl);
+  if (e != cudaSuccess) return cuda_fail(e, "down launch");
+  return HEXMOE_OK;
+}
+
+int check_phase(const hexmoe_layer* layer, int32_t dt, int64_t tokens, int32_t topk, int32_t bm) {
+  if (!layer) return fail(HEXMOE_E_ARG, "null layer");
+  if (dt != HEXMOE_BF16 && dt != HEXMOE_F16) return fail(HEXMOE_E_DTYPE, "phase dtype must be BF16 or F16");
+  if (tokens < 0 || topk <= 0 || topk > layer->desc.num_experts) return fail(HEXMOE_E_ARG, "tokens / topk");
+  if (bm != 16 && bm != 32 && bm != 64 && bm != 128) return fail(HEXMOE_E_ARG, "block_m %d not in {16, 32, 64, 128}", bm);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev != layer->device) return fail(HEXMOE_E_ARG, "layer was created on device %d, current device is %d", layer->device, dev);
+  return HEXMOE_OK;
+}
 
 }  // namespace
 
@@ -196,10 +305,12 @@ int hexmoe_layer_create(const hexmoe_layer_desc* desc, hexmoe_layer** out) {
   L->desc = d;
   L->device = dev;
   L->num_sms = sms;
+  L->max_bits = 3;
   for (int t = 0; t < d.num_tiers; ++t) {
     const hexmoe_tier& tr = d.tiers[t];
     if (tr.bits != 3 && tr.bits != 4) { delete L; return fail(HEXMOE_E_ARG, "tier %d: bits %d is not 3 or 4", t, tr.bits); }
     if (tr.n <= 0 || tr.n > 65535) { delete L; return fail(HEXMOE_E_ARG, "tier %d: %d experts", t, tr.n); }
+    L->max_bits = std::max(L->max_bits, static_cast<int>(tr.bits));
     const hexmoe_parts* parts[3] = {&tr.gate, &tr.up, &tr.down};
     for (int j = 0; j < 3; ++j) {
       const hexmoe_parts& pp = *parts[j];
@@ -214,10 +325,14 @@ int hexmoe_layer_create(const hexmoe_layer_desc* desc, hexmoe_layer** out) {
       const int rows = j < 2 ? d.inter_pad : d.hidden_pad;
       const int cols = j < 2 ? d.hidden_pad : d.inter_pad;
       const uint64_t wpr = static_cast<uint64_t>(cols) / 32 * tr.bits;
-      int rc = make_tmap(&L->tm_idx[t][j], pp.idx, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, wpr,
-                         static_cast<uint64_t>(tr.n) * rows, wpr * 4, 4u * tr.bits, 128, CU_TENSOR_MAP_SWIZZLE_NONE,
-                         "idx tensor map");
-      if (rc != HEXMOE_OK) { delete L; return rc; }
+      for (int ki = 0; ki < 4; ++ki) {
+        const int k_idx = 128 * (ki + 1);
+        if (cols % k_idx) continue;
+        int rc = make_tmap(&L->tm_idx[t][j][ki], pp.idx, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, wpr,
+                           static_cast<uint64_t>(tr.n) * rows, wpr * 4, static_cast<uint32_t>(k_idx / 32 * tr.bits), 128,
+                           CU_TENSOR_MAP_SWIZZLE_NONE, "idx tensor map");
+        if (rc != HEXMOE_OK) { delete L; return rc; }
+      }
     }
   }
   if (!device_error_word()) { delete L; return fail(HEXMOE_E_CUDA, "device error word unavailable"); }
@@ -272,70 +387,75 @@ int hexmoe_forward(const hexmoe_layer* layer, const void* x, int32_t x_dtype, in
   void* act = ws + w.act;
   void* y = ws + w.y;
   const bool bf16 = x_dtype != HEXMOE_F16;     // f32 activations are computed in bf16
-  const void* x16 = x;
-  cudaError_t e;
-  if (x_dtype == HEXMOE_F32) {
-    x16 = ws + w.xcast;
-    e = launch_cast_to16(static_cast<const float*>(x), ws + w.xcast, true, tokens * d.hidden, st);
-    if (e != cudaSuccess) return cuda_fail(e, "cast");
-  }
-  e = launch_align(topk_ids, ids_dtype == HEXMOE_I64, S, d.num_experts, bm, sid, eid, npp, nullptr, 0, dev_err, st, true);
+  void* xs = ws + w.xs;
+  cudaError_t e = launch_align(topk_ids, ids_dtype == HEXMOE_I64, S, d.num_experts, bm, sid, eid, npp, nullptr, 0, dev_err, st, true);
   if (e != cudaSuccess) return cuda_fail(e, "align launch");
 
-  const CUtensorMapDataType dt16 = bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  // ---- gate/up
-  GemmParams p{};
-  for (int t = 0; t < d.num_tiers; ++t) {
-    p.tm_idx[t][0] = layer->tm_idx[t][0];
-    p.tm_idx[t][1] = layer->tm_idx[t][1];
-    p.bs[t][0] = d.tiers[t].gate.block_scale; p.bs[t][1] = d.tiers[t].up.block_scale;
-    p.es[t][0] = d.tiers[t].gate.expert_scale; p.es[t][1] = d.tiers[t].up.expert_scale;
-    p.lev[t][0] = d.tiers[t].gate.levels; p.lev[t][1] = d.tiers[t].up.levels;
-    p.bits[t] = d.tiers[t].bits;
-  }
-  p.num_tiers = d.num_tiers;
-  p.expert_map = d.expert_map;
-  p.num_experts = d.num_experts;
-  p.sorted_ids = sid; p.expert_ids = eid; p.npp = npp;
-  p.bm = bm; p.max_blocks = static_cast<int32_t>(w.max_blocks);
-  p.num_slots = static_cast<int32_t>(S); p.topk = topk;
-  p.rows_pad = d.inter_pad; p.rows_store = d.inter_pad;
-  p.k_pad = d.hidden_pad; p.block = d.block;
-  p.m_tiles = d.inter_pad / kTileM;
-  p.out = act; p.ld_out = d.inter_pad;
-  p.topk_w = topk_weights;
-  p.dev_err = dev_err;
-  if (int rc = plan_gemm(p, true, bm, d.hidden_pad, d.block)) return rc;
-  if (int rc = make_tmap(&p.tm_b, x16, dt16, 2, d.hidden, tokens, 2ull * d.hidden, 64, 1,
-                         CU_TENSOR_MAP_SWIZZLE_128B, "x tensor map"))
-    return rc;
-  int grid = static_cast<int>(std::min<int64_t>(layer->num_sms, w.max_blocks * p.m_tiles));
-  e = launch_gemm(p, true, bf16, grid, st, true);
-  if (e != cudaSuccess) return cuda_fail(e, "gate/up launch");
-
-  // ---- down
-  GemmParams q = p;
-  for (int t = 0; t < d.num_tiers; ++t) {
-    q.tm_idx[t][0] = layer->tm_idx[t][2];
-    q.bs[t][0] = d.tiers[t].down.block_scale; q.bs[t][1] = nullptr;
-    q.es[t][0] = d.tiers[t].down.expert_scale; q.es[t][1] = nullptr;
-    q.lev[t][0] = d.tiers[t].down.levels; q.lev[t][1] = nullptr;
-  }
-  q.topk = 1;
-  q.rows_pad = d.hidden_pad; q.rows_store = d.hidden;
-  q.k_pad = d.inter_pad;
-  q.m_tiles = d.hidden_pad / kTileM;
-  q.out = y; q.ld_out = d.hidden;
-  if (int rc = plan_gemm(q, false, bm, d.inter_pad, d.block)) return rc;
-  if (int rc = make_tmap(&q.tm_b, act, dt16, 2, d.inter_pad, static_cast<uint64_t>(w.max_blocks) * bm,
-                         2ull * d.inter_pad, 64, static_cast<uint32_t>(bm), CU_TENSOR_MAP_SWIZZLE_128B, "act tensor map"))
-    return rc;
-  grid = static_cast<int>(std::min<int64_t>(layer->num_sms, w.max_blocks * q.m_tiles));
-  e = launch_gemm(q, false, bf16, grid, st, true);
-  if (e != cudaSuccess) return cuda_fail(e, "down launch");
+  e = launch_gather_rows(x, x_dtype, tokens, d.hidden, sid, npp, w.max_blocks * bm, topk, S, xs, st, true);
+  if (e != cudaSuccess) return cuda_fail(e, "gather launch");
+  int rc = run_gate_up(layer, xs, bf16, tokens, topk, sid, eid, npp, bm, act, dev_err, st, true);
+  if (rc) return rc;
+  rc = run_down(layer, act, bf16, tokens, topk, topk_weights, sid, eid, npp, bm, y, dev_err, st, true);
+  if (rc) return rc;
 
   // ---- combine
   e = launch_combine(y, bf16 ? HEXMOE_BF16 : HEXMOE_F16, tokens, topk, d.hidden, d.hidden, out, out_dtype, st, true);
+  if (e != cudaSuccess) return cuda_fail(e, "combine launch");
+  return HEXMOE_OK;
+}
+
+int hexmoe_gather(const void* x, int32_t x_dtype, int64_t tokens, int32_t hidden, int32_t topk, int32_t num_experts,
+                  const int32_t* sorted_ids, const int32_t* npp, int32_t block_m, void* x_sorted, void* stream) {
+  if (check_dtype16(x_dtype, "x")) return HEXMOE_E_DTYPE;
+  if (tokens < 0 || hidden <= 0 || hidden % 32 || topk <= 0 || num_experts <= 0 || block_m <= 0)
+    return fail(HEXMOE_E_ARG, "hexmoe_gather: bad sizes");
+  if (tokens == 0) return HEXMOE_OK;
+  if (!x || !sorted_ids || !npp || !x_sorted || reinterpret_cast<uintptr_t>(x) % 16 ||
+      reinterpret_cast<uintptr_t>(x_sorted) % 16)
+    return fail(HEXMOE_E_ARG, "hexmoe_gather: null or unaligned pointer");
+  const int64_t S = tokens * topk;
+  const int64_t max_blocks = (S + block_m - 1) / block_m + std::min<int64_t>(num_experts, S);
+  cudaError_t e = launch_gather_rows(x, x_dtype, tokens, hidden, sorted_ids, npp, max_blocks * block_m, topk, S,
+                                     x_sorted, static_cast<cudaStream_t>(stream), false);
+  if (e != cudaSuccess) return cuda_fail(e, "gather launch");
+  return HEXMOE_OK;
+}
+
+int hexmoe_gate_up(const hexmoe_layer* layer, const void* x_sorted, int32_t x_dtype, int64_t tokens, int32_t topk,
+                   const int32_t* sorted_ids, const int32_t* expert_ids, const int32_t* npp, int32_t block_m,
+                   void* act, void* stream) {
+  if (int rc = check_phase(layer, x_dtype, tokens, topk, block_m)) return rc;
+  if (tokens == 0) return HEXMOE_OK;
+  if (!x_sorted || !sorted_ids || !expert_ids || !npp || !act) return fail(HEXMOE_E_ARG, "hexmoe_gate_up: null pointer");
+  int32_t* dev_err = device_error_word();
+  if (!dev_err) return fail(HEXMOE_E_CUDA, "device error word unavailable");
+  return run_gate_up(layer, x_sorted, x_dtype == HEXMOE_BF16, tokens, topk, sorted_ids, expert_ids, npp, block_m, act,
+                     dev_err, static_cast<cudaStream_t>(stream), false);
+}
+
+int hexmoe_down(const hexmoe_layer* layer, const void* act, int32_t act_dtype, int64_t tokens, int32_t topk,
+                const float* topk_weights, const int32_t* sorted_ids, const int32_t* expert_ids, const int32_t* npp,
+                int32_t block_m, void* y, void* stream) {
+  if (int rc = check_phase(layer, act_dtype, tokens, topk, block_m)) return rc;
+  if (tokens == 0) return HEXMOE_OK;
+  if (!act || !topk_weights || !sorted_ids || !expert_ids || !npp || !y)
+    return fail(HEXMOE_E_ARG, "hexmoe_down: null pointer");
+  int32_t* dev_err = device_error_word();
+  if (!dev_err) return fail(HEXMOE_E_CUDA, "device error word unavailable");
+  return run_down(layer, act, act_dtype == HEXMOE_BF16, tokens, topk, topk_weights, sorted_ids, expert_ids, npp,
+                  block_m, y, dev_err, static_cast<cudaStream_t>(stream), false);
+}
+
+int hexmoe_combine(const void* y, int32_t y_dtype, int64_t tokens, int32_t topk, int32_t hidden, void* out,
+                   int32_t out_dtype, void* stream) {
+  if (y_dtype != HEXMOE_BF16 && y_dtype != HEXMOE_F16) return fail(HEXMOE_E_DTYPE, "y dtype must be BF16 or F16");
+  if (check_dtype16(out_dtype, "out")) return HEXMOE_E_DTYPE;
+  if (tokens < 0 || topk <= 0 || hidden <= 0 || hidden % 8) return fail(HEXMOE_E_ARG, "combine: tokens / topk / hidden");
+  if (tokens == 0) return HEXMOE_OK;
+  if (!y || !out || reinterpret_cast<uintptr_t>(y) % 16 || reinterpret_cast<uintptr_t>(out) % 16)
+    return fail(HEXMOE_E_ARG, "combine: y / out must be non-null and 16-byte aligned");
+  cudaError_t e = launch_combine(y, y_dtype, tokens, topk, hidden, hidden, out, out_dtype,
+                                 static_cast<cudaStream_t>(stream), false);
   if (e != cudaSuccess) return cuda_fail(e, "combine launch");
   return HEXMOE_OK;
 }

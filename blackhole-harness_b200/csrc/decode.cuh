@@ -76,17 +76,31 @@ __device__ __forceinline__ Table16 make_table16(const float* lev, float s) {
 }
 
 // 8 codes of 3 bits at bits 0..23 of g (higher bits ignored) -> nibble j = code j.
+// The left shifts are written as multiplies so they can issue on the FMA pipe;
+// the merges and the mask are single lop3s on the integer pipe.
 __device__ __forceinline__ uint32_t spread3(uint32_t g) {
-  uint32_t x = lop3_sel(g, g << 4, 0x0000FFFFu);   // codes 4-7 -> bits 16..27
-  x = lop3_sel(x, x << 2, 0x00FF00FFu);           // pairs -> bytes
-  x = lop3_sel(x, x << 1, 0x0F0F0F0Fu);           // codes -> nibbles
-  return x & 0x77777777u;                          // bit 3 of each nibble clear (prmt index mode)
+  uint32_t x = lop3_sel(g, g * 16u, 0x0000FFFFu);   // codes 4-7 -> bits 16..27
+  x = lop3_sel(x, x * 4u, 0x00FF00FFu);             // pairs -> bytes
+  x = lop3_sel(x, x * 2u, 0x0F0F0F0Fu);             // codes -> nibbles
+  return x & 0x77777777u;                            // bit 3 of each nibble clear (prmt index mode)
+}
+
+__device__ __forceinline__ Table8 table8_from(const uint4& v) {
+  Table8 t;
+  t.l0 = v.x; t.l1 = v.y; t.h0 = v.z; t.h1 = v.w;
+  return t;
+}
+__device__ __forceinline__ Table16 table16_from(const uint4& lo, const uint4& hi) {
+  Table16 t;
+  t.la0 = lo.x; t.la1 = lo.y; t.lb0 = lo.z; t.lb1 = lo.w;
+  t.ha0 = hi.x; t.ha1 = hi.y; t.hb0 = hi.z; t.hb1 = hi.w;
+  return t;
 }
 
 // 8 consecutive weights (3-bit codes in g) -> 4 packed operand pairs, K order.
 __device__ __forceinline__ uint4 dec8_b3(uint32_t g, const Table8& t) {
   const uint32_t s0 = spread3(g);
-  const uint32_t s1 = s0 >> 16;
+  const uint32_t s1 = __umulhi(s0, 65536u);          // s0 >> 16 on the FMA pipe
   const uint32_t lo0 = prmt(t.l0, t.l1, s0), hi0 = prmt(t.h0, t.h1, s0);
   const uint32_t lo1 = prmt(t.l0, t.l1, s1), hi1 = prmt(t.h0, t.h1, s1);
   uint4 o;
@@ -100,8 +114,8 @@ __device__ __forceinline__ uint4 dec8_b3(uint32_t g, const Table8& t) {
 // 8 consecutive weights (4-bit codes, nibbles of w) -> 4 packed operand pairs.
 __device__ __forceinline__ uint4 dec8_b4(uint32_t w, const Table16& t) {
   const uint32_t s0 = w & 0x77777777u;
-  const uint32_t s1 = s0 >> 16;
-  const uint32_t w4 = w << 4;
+  const uint32_t s1 = __umulhi(s0, 65536u);
+  const uint32_t w4 = w * 16u;
   const uint32_t m0 = prmt(w4, w, 0xD9C8);   // 0xFF per byte where code bit 3 is set (codes 0-3)
   const uint32_t m1 = prmt(w4, w, 0xFBEA);   // codes 4-7
   const uint32_t lo0 = lop3_sel(prmt(t.lb0, t.lb1, s0), prmt(t.la0, t.la1, s0), m0);

@@ -8,17 +8,29 @@
 // side (16..128 columns), so a decode step with a handful of tokens per expert
 // still streams every weight once at full width.
 //
-// Warp roles (448 threads):
-//   warp 0      TMA: index words of the weight tile (2-D tensor map, 128 rows x
-//               128 inputs per stage), the token rows of the block (gate/up: one
-//               row gather per token, down: one box), and once per tile the
-//               tile's fp8 scale codes (1-D bulk copy)
+// Warp roles (32 x (7 + 8 x decoder groups) threads):
+//   warp 0      producer: per tile a record (block, weight tile, tier, valid
+//               rows, level tables, expert scales, the block's slot ids and
+//               top-k weights) into a small shared ring and the tile's fp8
+//               scale codes (1-D bulk copy); the index words of the weight
+//               tile, one 2-D TMA box of 128 rows x k_idx inputs (k_idx up to
+//               512, so each row moved is 144-256 bytes: TMA cost is per row),
+//               into a ring the decoders release
+//   last warp   activation producer: the block's rows of the plan-ordered
+//               activations, two 64-column boxes per 128 inputs, into a ring
+//               the MMA releases (its own warp, so a full activation ring never
+//               delays the next index stage)
 //   warp 1      TMEM allocation; one thread issues tcgen05.mma (A operand from
 //               TMEM, B from 128-B swizzled smem) and tcgen05.commit
 //   warps 2-5   epilogue: tcgen05.ld of the accumulators, SwiGLU (gate/up) or
-//               top-k weight (down), 16-bit stores
-//   warps 6-13  decode: per (row, 32-input block) the scaled level table, then
-//               prmt lookups of the packed codes, written to TMEM with tcgen05.st
+//               the top-k weight (down), 16-bit stores
+//   warps 6..   decoders, groups of 8 taking 128-input sub-blocks in turn:
+//               once per tile, the level table scaled by every one
+//               of the 256 fp8 scale codes (one entry per thread, shared
+//               memory); per 32-input block one table load and prmt lookups of
+//               the packed codes, written to TMEM with tcgen05.st; a store is
+//               waited for (and its stage handed to the MMA) only after the
+//               next half-stage is decoded, so the TMEM write latency overlaps
 // Every wait is bounded (ptx.cuh): a lost arrival ends the kernel with the
 // device error word set instead of hanging.
 #include "decode.cuh"
@@ -26,17 +38,33 @@
 
 namespace hexmoe {
 
+constexpr int kRecs = 4;   // tile records in flight
+
 struct Ctrl {
-  uint64_t r_full[kMaxDR], r_empty[kMaxDR];   // index / token-row ring
+  uint64_t x_full[kMaxDI], x_empty[kMaxDI];   // index-word ring
+  uint64_t b_full[kMaxDB], b_empty[kMaxDB];   // activation ring
   uint64_t a_full[kMaxDA], a_empty[kMaxDA];   // TMEM operand ring
   uint64_t s_full[2], s_empty[2];             // tile scale buffers
   uint64_t t_full[2], t_empty[2];             // accumulator buffers
+  uint64_t i_full[kRecs], i_empty[kRecs];     // tile records
+  uint64_t tab_ready[2];                      // code tables built (per buffer)
   uint64_t drain;
   uint32_t tmem_base;
   int32_t abort;
 };
 static_assert(sizeof(Ctrl) <= 2048, "control block");
-constexpr uint32_t kOffLut = 2048;            // fp8 decode table (256 floats)
+constexpr uint32_t kOffLut = 2048;    // fp8 decode table (256 floats)
+constexpr uint32_t kOffRec = 3072;    // tile records (kRecs x 1280 B, up to 8192)
+
+struct TileRec {
+  int32_t b, m, tier, local, bits, cnt, ok, pad;
+  float es[2];
+  float lev[2][16];
+  int32_t slot[128];    // down: the block's slot ids (valid rows)
+  float w[128];         // down: their top-k weights
+  uint8_t pad_to_1280[1280 - 40 - 128 - 1024];
+};
+static_assert(sizeof(TileRec) == 1280 && kOffRec + kRecs * 1280 <= 8192, "tile records");
 
 struct TileInfo {
   int32_t b, m, tier, local, bits;
@@ -75,24 +103,18 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
-template <bool BF16>
-__device__ __forceinline__ uint32_t to16x2(float lo, float hi) {
-  return pack2<BF16>(lo, hi);
-}
-
-
 // Decode the 32-input block BLK (0..3) of one stage row into 16 packed operand
-// registers (K order).  w: the row's stage words; sc: the stage's 4 scale codes.
-template <bool BF16, int BLK>
-__device__ __forceinline__ void decode_block(const uint32_t (&w)[16], int bits, uint32_t sc, const float* lut,
-                                             const float (&lev)[16], float es, uint32_t* r) {
-  const float s = __fmul_rn(lut[(sc >> (8 * BLK)) & 255u], es);
+// registers (K order).  w: the row's stage words; tab: this projection's code
+// tables (plane 0, then plane 1 at +256); code: the block's fp8 scale code.
+template <int BLK>
+__device__ __forceinline__ void decode_block(const uint32_t (&w)[16], int bits, const uint4* tab, uint32_t code,
+                                             uint32_t* r) {
   uint4 ch[4];
   if (bits == 3) {
-    const Table8 tb = make_table8<BF16>(lev, s);
+    const Table8 tb = table8_from(tab[code]);
     dec32_b3(w[3 * BLK], w[3 * BLK + 1], w[3 * BLK + 2], tb, ch);
   } else {
-    const Table16 tb = make_table16<BF16>(lev, s);
+    const Table16 tb = table16_from(tab[code], tab[256 + code]);
     dec32_b4(w[4 * BLK], w[4 * BLK + 1], w[4 * BLK + 2], w[4 * BLK + 3], tb, ch);
   }
 #pragma unroll
@@ -110,17 +132,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   Ctrl* c = reinterpret_cast<Ctrl*>(smem);
   float* lut = reinterpret_cast<float*>(smem + kOffLut);
+  TileRec* recs = reinterpret_cast<TileRec*>(smem + kOffRec);   // stride 1280 B
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int NPROJ = GLU ? 2 : 1;
   volatile int* abort_flag = &c->abort;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kMaxDR; ++i) { mbar_init(&c->r_full[i], 1); mbar_init(&c->r_empty[i], 1); }
-    for (int i = 0; i < kMaxDA; ++i) { mbar_init(&c->a_full[i], 8); mbar_init(&c->a_empty[i], 1); }
+    for (int i = 0; i < kMaxDI; ++i) { mbar_init(&c->x_full[i], 1); mbar_init(&c->x_empty[i], kDecWarps); }
+    for (int i = 0; i < kMaxDB; ++i) { mbar_init(&c->b_full[i], 1); mbar_init(&c->b_empty[i], 1); }
+    for (int i = 0; i < kMaxDA; ++i) { mbar_init(&c->a_full[i], GLU ? 8 : 4); mbar_init(&c->a_empty[i], 1); }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&c->s_full[i], 1); mbar_init(&c->s_empty[i], 8);
+      mbar_init(&c->s_full[i], 1); mbar_init(&c->s_empty[i], kDecWarps);
       mbar_init(&c->t_full[i], 1); mbar_init(&c->t_empty[i], 4);
+      mbar_init(&c->tab_ready[i], kDecWarps);
     }
+    for (int i = 0; i < kRecs; ++i) { mbar_init(&c->i_full[i], 1); mbar_init(&c->i_empty[i], 6 + kDecWarps); }
     mbar_init(&c->drain, 1);
     c->abort = 0;
     fence_mbar_init();
@@ -134,9 +160,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
     tmem_alloc(&c->tmem_base, kTmemCols);
     tmem_relinquish();
   }
-  if (warp >= 6) {
-    for (int i = threadIdx.x - 192; i < 256; i += 256) lut[i] = fp8_hex_value(static_cast<uint32_t>(i));
-  }
+  if (warp >= 6 && warp < 14) lut[threadIdx.x - 192] = fp8_hex_value(static_cast<uint32_t>(threadIdx.x - 192));
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -147,29 +171,54 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
 
   const int nbv = __ldg(p.npp) / p.bm;
   const int num_tiles = nbv * p.m_tiles;
-  const int ksteps = p.k_pad / kKStep;
+  const int ksteps = p.k_pad / kKStep;        // activation stages per tile
+  const int spi = p.k_idx / kKStep;           // 128-input sub-blocks per index stage
   const uint32_t spr = static_cast<uint32_t>(p.k_pad / p.block);   // scale bytes per weight row
   const uint32_t scale_tile = 128u * spr;                           // per projection
-  uint8_t* ring = smem + p.off_ring;
+  uint8_t* xring = smem + p.off_idx;
+  uint8_t* bring = smem + p.off_b;
   uint8_t* scale_buf = smem + p.off_scale;
+  uint4* tabs = reinterpret_cast<uint4*>(smem + p.off_tab);        // [2][NPROJ][2 planes][256]
 
   if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
+    // ------------------------------------------------------------ producer
     const uint64_t pol_stream = l2_policy_evict_first();
-    uint32_t rs = 0, rph = 0;
-    int issued = 0, s_issued = 0;
+    uint32_t xs = 0, xph = 0;
+    int x_issued = 0, s_issued = 0;
     bool aborted = false;
-    int it = 0;
-    for (int t = blockIdx.x; t < num_tiles && !aborted; t += gridDim.x) {
+    int cur = 0;
+    for (int t = blockIdx.x; t < num_tiles && !aborted; t += gridDim.x, ++cur) {
       const TileInfo ti = tile_info(p, t);
-      if (!ti.ok) continue;
-      const int cur = it++;
       const int cnt = block_rows(p, ti.b, lane);
-      const uint32_t wbox = 4u * ti.bits;                         // index words per row per stage
-      const uint32_t idx_bytes = NPROJ * 128u * wbox * 4u;
-      const uint32_t b_bytes = GLU ? static_cast<uint32_t>(cnt) * 256u : static_cast<uint32_t>(p.bm) * 256u;
-      const int sb = cur & 1;
-      if (!mbar_wait(&c->s_empty[sb], ((cur >> 1) & 1) ^ 1, abort_flag, p.dev_err)) { aborted = true; break; }
+      const int ri = cur % kRecs;
+      if (!mbar_wait_idle(&c->i_empty[ri], ((cur / kRecs) & 1) ^ 1, abort_flag, p.dev_err)) { aborted = true; break; }
+      {
+        TileRec* rec = recs + ri;
+        const int L = 1 << ti.bits;
+        if (lane < 16) {
+          for (int q = 0; q < NPROJ; ++q)
+            rec->lev[q][lane] = (ti.ok && lane < L) ? __ldg(p.lev[ti.tier][q] + ti.local * L + lane) : 0.0f;
+        }
+        if (lane < NPROJ) rec->es[lane] = ti.ok ? __ldg(p.es[ti.tier][lane] + ti.local) : 0.0f;
+        if (!GLU) {
+          for (int r = lane; r < cnt; r += 32) {
+            const int slot = __ldg(p.sorted_ids + static_cast<size_t>(ti.b) * p.bm + r);
+            rec->slot[r] = slot;
+            rec->w[r] = __ldg(p.topk_w + slot);
+          }
+        }
+        if (lane == 0) {
+          rec->b = ti.b; rec->m = ti.m; rec->tier = ti.tier; rec->local = ti.local;
+          rec->bits = ti.bits; rec->cnt = cnt; rec->ok = ti.ok;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&c->i_full[ri]);
+      }
+      if (!ti.ok) continue;
+      const uint32_t wst = static_cast<uint32_t>(p.k_idx / 32 * ti.bits);   // index words per row per stage
+      const uint32_t idx_bytes = NPROJ * 128u * wst * 4u;
+      const int sb = s_issued & 1;
+      if (!mbar_wait_idle(&c->s_empty[sb], ((s_issued >> 1) & 1) ^ 1, abort_flag, p.dev_err)) { aborted = true; break; }
       if (lane == 0) {
         mbar_arrive_expect_tx(&c->s_full[sb], scale_tile * NPROJ);
         for (int j = 0; j < NPROJ; ++j) {
@@ -179,42 +228,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
         }
       }
       ++s_issued;
-      // token rows this lane gathers (gate/up): r = lane + 32 j
-      int src_row[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int r = lane + 32 * j;
-        src_row[j] = -1;
-        if (GLU && r < cnt) src_row[j] = __ldg(p.sorted_ids + static_cast<size_t>(ti.b) * p.bm + r) / p.topk;
-      }
       const int32_t wrow = ti.local * p.rows_pad + ti.m * 128;
-      for (int ks = 0; ks < ksteps; ++ks) {
-        if (!mbar_wait(&c->r_empty[rs], rph ^ 1, abort_flag, p.dev_err)) { aborted = true; break; }
-        uint8_t* stage = ring + rs * p.sz_stage;
-        uint8_t* bdst = stage + p.sz_idx;
-        if (lane == 0) {
-          mbar_arrive_expect_tx(&c->r_full[rs], idx_bytes + b_bytes);
-          for (int j = 0; j < NPROJ; ++j)
-            tma_load_2d_hint(stage + j * 128 * wbox * 4, &p.tm_idx[ti.tier][j], &c->r_full[rs],
-                             ks * static_cast<int>(wbox), wrow, pol_stream);
-          if (!GLU) {
-            tma_load_2d(bdst, &p.tm_b, &c->r_full[rs], ks * kKStep, ti.b * p.bm);
-            tma_load_2d(bdst + p.bm * 128, &p.tm_b, &c->r_full[rs], ks * kKStep + 64, ti.b * p.bm);
+      for (int kb = 0; kb < ksteps; ++kb) {
+        if (kb % spi == 0) {
+          if (!mbar_wait_idle(&c->x_empty[xs], xph ^ 1, abort_flag, p.dev_err)) { aborted = true; break; }
+          if (lane == 0) {
+            uint8_t* dst = xring + xs * p.sz_idx;
+            mbar_arrive_expect_tx(&c->x_full[xs], idx_bytes);
+            for (int j = 0; j < NPROJ; ++j)
+              tma_load_2d_hint(dst + j * 128 * wst * 4, &p.tm_idx[ti.tier][j], &c->x_full[xs],
+                               (kb / spi) * static_cast<int>(wst), wrow, pol_stream);
           }
+          ++x_issued;
+          if (++xs == static_cast<uint32_t>(p.di)) { xs = 0; xph ^= 1; }
         }
-        __syncwarp();
-        if (GLU) {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            if (src_row[j] >= 0) {
-              const int r = lane + 32 * j;
-              tma_load_2d(bdst + r * 128, &p.tm_b, &c->r_full[rs], ks * kKStep, src_row[j]);
-              tma_load_2d(bdst + p.bm * 128 + r * 128, &p.tm_b, &c->r_full[rs], ks * kKStep + 64, src_row[j]);
-            }
-          }
-        }
-        ++issued;
-        if (++rs == static_cast<uint32_t>(p.dr)) { rs = 0; rph ^= 1; }
       }
     }
     if (aborted && lane == 0) {
@@ -223,32 +250,66 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
         const int q = s_issued - i;
         drain_wait(&c->s_full[q & 1], (q >> 1) & 1);
       }
-      const int n = issued < p.dr ? issued : p.dr;
-      for (int i = 1; i <= n; ++i) {
-        const int q = issued - i;
-        drain_wait(&c->r_full[q % p.dr], (q / p.dr) & 1);
+      for (int i = 1; i <= p.di && i <= x_issued; ++i) {
+        const int q = x_issued - i;
+        drain_wait(&c->x_full[q % p.di], (q / p.di) & 1);
+      }
+    }
+  } else if (warp == kBWarp) {
+    // ------------------------------------------------------------ activation producer
+    uint32_t bs = 0, bph = 0;
+    int b_issued = 0;
+    bool aborted = false;
+    int cur = 0;
+    const uint32_t b_bytes = static_cast<uint32_t>(p.bm) * 256u;
+    for (int t = blockIdx.x; t < num_tiles && !aborted; t += gridDim.x, ++cur) {
+      const int ri = cur % kRecs;
+      if (!mbar_wait_idle(&c->i_full[ri], (cur / kRecs) & 1, abort_flag, p.dev_err)) { aborted = true; break; }
+      const int ok = recs[ri].ok, b = recs[ri].b;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&c->i_empty[ri]);
+      if (!ok) continue;
+      for (int kb = 0; kb < ksteps; ++kb) {
+        if (!mbar_wait_idle(&c->b_empty[bs], bph ^ 1, abort_flag, p.dev_err)) { aborted = true; break; }
+        if (lane == 0) {
+          uint8_t* bdst = bring + bs * p.sz_b;
+          mbar_arrive_expect_tx(&c->b_full[bs], b_bytes);
+          tma_load_2d(bdst, &p.tm_b, &c->b_full[bs], kb * kKStep, b * p.bm);
+          tma_load_2d(bdst + p.bm * 128, &p.tm_b, &c->b_full[bs], kb * kKStep + 64, b * p.bm);
+        }
+        ++b_issued;
+        if (++bs == static_cast<uint32_t>(p.db)) { bs = 0; bph ^= 1; }
+      }
+    }
+    if (aborted && lane == 0) {
+      for (int i = 1; i <= p.db && i <= b_issued; ++i) {
+        const int q = b_issued - i;
+        drain_wait(&c->b_full[q % p.db], (q / p.db) & 1);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    uint32_t rs = 0, rph = 0, as = 0, aph = 0;
+    uint32_t bs = 0, bph = 0, as = 0, aph = 0;
     bool aborted = false;
-    int it = 0;
-    for (int t = blockIdx.x; t < num_tiles && !aborted; t += gridDim.x) {
-      const TileInfo ti = tile_info(p, t);
-      if (!ti.ok) continue;
-      const int cur = it++;
-      const int cnt = block_rows(p, ti.b, lane);
+    int cur = 0, acc_it = 0;
+    for (int t = blockIdx.x; t < num_tiles && !aborted; t += gridDim.x, ++cur) {
+      const int ri = cur % kRecs;
+      if (!mbar_wait(&c->i_full[ri], (cur / kRecs) & 1, abort_flag, p.dev_err)) { aborted = true; break; }
+      const int ok = recs[ri].ok, cnt = recs[ri].cnt;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&c->i_empty[ri]);
+      if (!ok) continue;
       const uint32_t n_mma = static_cast<uint32_t>(max(16, (cnt + 15) & ~15));
       const uint32_t idesc = umma_idesc(BF16, 128, n_mma);
-      const int ab = cur % p.nbuf;
-      if (!mbar_wait(&c->t_empty[ab], ((cur / p.nbuf) & 1) ^ 1, abort_flag, p.dev_err)) { aborted = true; break; }
+      const int ab = acc_it % p.nbuf;
+      if (!mbar_wait(&c->t_empty[ab], ((acc_it / p.nbuf) & 1) ^ 1, abort_flag, p.dev_err)) { aborted = true; break; }
+      ++acc_it;
       tc_fence_after();
       const uint32_t d0 = tmem + ab * p.acc_stride;
       const uint32_t d1 = d0 + p.bm;
       for (int ks = 0; ks < ksteps && !aborted; ++ks) {
-        if (!mbar_wait(&c->r_full[rs], rph, abort_flag, p.dev_err)) { aborted = true; break; }
-        const uint32_t bbase = smem_u32(ring + rs * p.sz_stage + p.sz_idx);
+        if (!mbar_wait(&c->b_full[bs], bph, abort_flag, p.dev_err)) { aborted = true; break; }
+        const uint32_t bbase = smem_u32(bring + bs * p.sz_b);
         for (int h = 0; h < 2; ++h) {
           if (!mbar_wait(&c->a_full[as], aph, abort_flag, p.dev_err)) { aborted = true; break; }
           tc_fence_after();
@@ -267,9 +328,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
           if (++as == static_cast<uint32_t>(p.da)) { as = 0; aph ^= 1; }
         }
         if (aborted) break;
-        if (lane == 0) umma_commit(&c->r_empty[rs]);
+        if (lane == 0) umma_commit(&c->b_empty[bs]);
         __syncwarp();
-        if (++rs == static_cast<uint32_t>(p.dr)) { rs = 0; rph ^= 1; }
+        if (++bs == static_cast<uint32_t>(p.db)) { bs = 0; bph ^= 1; }
       }
       if (aborted) break;
       if (lane == 0) umma_commit(&c->t_full[ab]);
@@ -284,19 +345,33 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
     const int q = warp & 3;
     const int row = q * 32 + lane;
     const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16);
-    int it = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
-      const TileInfo ti = tile_info(p, t);
-      if (!ti.ok) {
+    int cur = 0, acc_it = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++cur) {
+      const int ri = cur % kRecs;
+      if (!mbar_wait_idle(&c->i_full[ri], (cur / kRecs) & 1, abort_flag, p.dev_err)) break;
+      const int ok = recs[ri].ok, cnt = recs[ri].cnt, b = recs[ri].b, m = recs[ri].m;
+      // down: this warp's copy of the block's slot ids / weights (lane j holds rows j, j+32, ...)
+      int my_slot[4];
+      float my_w[4];
+      if (!GLU) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int r = lane + 32 * j;
+          my_slot[j] = r < cnt ? recs[ri].slot[r] : 0;
+          my_w[j] = r < cnt ? recs[ri].w[r] : 0.0f;
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&c->i_empty[ri]);
+      if (!ok) {
         if (warp == 2 && lane == 0) atomicOr(p.dev_err, kDevErrNoTier);
         continue;
       }
-      const int cur = it++;
-      const int cnt = block_rows(p, ti.b, lane);
-      const int ab = cur % p.nbuf;
-      if (!mbar_wait(&c->t_full[ab], (cur / p.nbuf) & 1, abort_flag, p.dev_err)) break;
+      const int ab = acc_it % p.nbuf;
+      if (!mbar_wait_idle(&c->t_full[ab], (acc_it / p.nbuf) & 1, abort_flag, p.dev_err)) break;
+      ++acc_it;
       tc_fence_after();
-      const int o = ti.m * 128 + row;
+      const int o = m * 128 + row;
       const bool store_row = o < p.rows_store;
       const uint32_t d0 = tl + ab * p.acc_stride;
       for (int n0 = 0; n0 < cnt; n0 += 16) {
@@ -313,8 +388,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
             if (n < cnt && store_row) {
               const float gv = __uint_as_float(g[j]);
               const float uv = __uint_as_float(u[j]);
-              const float a = gv / (1.0f + expf(-gv)) * uv;
-              const size_t off = (static_cast<size_t>(ti.b) * p.bm + n) * p.ld_out + o;
+              const float hg = 0.5f * gv;                      // silu(g) = g/2 * (1 + tanh(g/2))
+              const float a = fmaf(hg, tanh_approx(hg), hg) * uv;
+              const size_t off = (static_cast<size_t>(b) * p.bm + n) * p.ld_out + o;
               if (BF16) out_b[off] = __float2bfloat16_rn(a);
               else out_h[off] = __float2half_rn(a);
             }
@@ -325,9 +401,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const int n = n0 + j;
+            const int src = n & 31, grp = n >> 5;             // row n of the block lives in lane n % 32
+            const int slot = __shfl_sync(0xffffffffu, grp == 0 ? my_slot[0] : grp == 1 ? my_slot[1]
+                                                      : grp == 2 ? my_slot[2] : my_slot[3], src);
+            const float wt = __shfl_sync(0xffffffffu, grp == 0 ? my_w[0] : grp == 1 ? my_w[1]
+                                                      : grp == 2 ? my_w[2] : my_w[3], src);
             if (n < cnt && store_row) {
-              const int slot = __ldg(p.sorted_ids + static_cast<size_t>(ti.b) * p.bm + n);
-              const float v = __uint_as_float(g[j]) * __ldg(p.topk_w + slot);
+              const float v = __uint_as_float(g[j]) * wt;
               const size_t off = static_cast<size_t>(slot) * p.ld_out + o;
               if (BF16) out_b[off] = __float2bfloat16_rn(v);
               else out_h[off] = __float2half_rn(v);
@@ -342,86 +422,127 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
   } else {
     // ------------------------------------------------------------ decoders
     const int d = warp - 6;
+    const int group = d >> 3;                // takes the 128-input sub-blocks kb with kb % kDecGroups == group
     const int q = warp & 3;
     const int row = q * 32 + lane;
-    const int role = d >> 2;                 // gate/up: projection; down: block parity
+    const int role = (d & 7) >> 2;           // gate/up: projection; down: which half of a sub-block
     const int proj = GLU ? role : 0;
+    const int dt = threadIdx.x - 192;        // first code-table entry this thread builds
     const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16);
-    uint32_t rs = 0, rph = 0, as = 0, aph = 0;
+    uint32_t xs = 0, xph = 0, as = 0, aph = 0;
     bool aborted = false;
-    int it = 0;
-    for (int t = blockIdx.x; t < num_tiles && !aborted; t += gridDim.x) {
-      const TileInfo ti = tile_info(p, t);
-      if (!ti.ok) continue;
-      const int cur = it++;
-      const int L = 1 << ti.bits;
-      float lev[16];
-      const float* lsrc = p.lev[ti.tier][proj] + ti.local * L;
-#pragma unroll
-      for (int l = 0; l < 16; ++l) lev[l] = l < L ? __ldg(lsrc + l) : 0.0f;
-      const float es = __ldg(p.es[ti.tier][proj] + ti.local);
-      const int sb = cur & 1;
-      if (!mbar_wait(&c->s_full[sb], (cur >> 1) & 1, abort_flag, p.dev_err)) { aborted = true; break; }
+    int cur = 0, work = 0;
+    int pending = -1;                        // operand stage stored to TMEM but not yet handed over
+    for (int t = blockIdx.x; t < num_tiles && !aborted; t += gridDim.x, ++cur) {
+      const int ri = cur % kRecs;
+      if (!mbar_wait(&c->i_full[ri], (cur / kRecs) & 1, abort_flag, p.dev_err)) { aborted = true; break; }
+      const TileRec& rec = recs[ri];
+      const int ok = rec.ok, bits = rec.bits;
+      const int tb = work & 1;
+      if (ok) {
+        for (int e = dt; e < 256 * NPROJ; e += kDecWarps * 32) {
+          // entry (code e % 256) of projection e / 256's code table
+          const int j = e >> 8, code = e & 255;
+          const float s = __fmul_rn(lut[code], rec.es[j]);
+          uint4* tj = tabs + (tb * NPROJ + j) * 512;
+          if (bits == 3) {
+            const Table8 t8 = make_table8<BF16>(rec.lev[j], s);
+            tj[code] = make_uint4(t8.l0, t8.l1, t8.h0, t8.h1);
+          } else {
+            const Table16 t16 = make_table16<BF16>(rec.lev[j], s);
+            tj[code] = make_uint4(t16.la0, t16.la1, t16.lb0, t16.lb1);
+            tj[256 + code] = make_uint4(t16.ha0, t16.ha1, t16.hb0, t16.hb1);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&c->i_empty[ri]);
+      if (!ok) continue;
+      if (lane == 0) mbar_arrive(&c->tab_ready[tb]);
+      if (!mbar_wait(&c->tab_ready[tb], (work >> 1) & 1, abort_flag, p.dev_err)) { aborted = true; break; }
+      const int sb = work & 1;
+      if (!mbar_wait(&c->s_full[sb], (work >> 1) & 1, abort_flag, p.dev_err)) { aborted = true; break; }
+      ++work;
+      const uint4* tab = tabs + (tb * NPROJ + proj) * 512;
       const uint8_t* srow = scale_buf + (sb * NPROJ + proj) * p.sz_scale + row * spr;
-      const uint32_t wbox = 4u * ti.bits;
-      for (int ks = 0; ks < ksteps && !aborted; ++ks) {
-        if (!mbar_wait(&c->r_full[rs], rph, abort_flag, p.dev_err)) { aborted = true; break; }
-        const uint32_t* wsrc =
-            reinterpret_cast<const uint32_t*>(ring + rs * p.sz_stage) + (proj * 128 + row) * wbox;
+      const uint32_t wst = static_cast<uint32_t>(p.k_idx / 32 * bits);
+      for (int kb = 0; kb < ksteps && !aborted; ++kb) {
+        const int sub = kb % spi;
+        const bool mine_k = (kb % kDecGroups) == group;
+        if (sub == 0) {
+          if (!mbar_wait(&c->x_full[xs], xph, abort_flag, p.dev_err)) { aborted = true; break; }
+        }
         uint32_t w[16];
-        const uint4* w4 = reinterpret_cast<const uint4*>(wsrc);
-        {
+        if (mine_k) {
+          const uint4* w4 = reinterpret_cast<const uint4*>(xring + xs * p.sz_idx + ((proj * 128 + row) * wst) * 4) +
+                            sub * bits;
           const uint4 v0 = w4[0], v1 = w4[1], v2 = w4[2];
           w[0] = v0.x; w[1] = v0.y; w[2] = v0.z; w[3] = v0.w;
           w[4] = v1.x; w[5] = v1.y; w[6] = v1.z; w[7] = v1.w;
           w[8] = v2.x; w[9] = v2.y; w[10] = v2.z; w[11] = v2.w;
-          if (ti.bits == 4) {
+          if (bits == 4) {
             const uint4 v3 = w4[3];
             w[12] = v3.x; w[13] = v3.y; w[14] = v3.z; w[15] = v3.w;
           } else {
             w[12] = w[13] = w[14] = w[15] = 0u;
           }
         }
-        uint32_t sc;   // scale codes of the 4 blocks of this stage, one byte each
-        if (p.block == 32) sc = *reinterpret_cast<const uint32_t*>(srow + ks * 4);
-        else sc = static_cast<uint32_t>(srow[ks]) * 0x01010101u;
+        if (sub == spi - 1) {
+          // every sub-block of the stage this group reads is in registers: release it
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&c->x_empty[xs]);
+          if (++xs == static_cast<uint32_t>(p.di)) { xs = 0; xph ^= 1; }
+        }
+        if (!mine_k) {
+          // another group's two half-stages
+          as += 2;
+          if (as >= static_cast<uint32_t>(p.da)) { as -= p.da; aph ^= 1; }
+          continue;
+        }
+        uint32_t sc;   // scale codes of the 4 blocks of this 128-input step, one byte each
+        if (p.block == 32) sc = *reinterpret_cast<const uint32_t*>(srow + kb * 4);
+        else sc = static_cast<uint32_t>(srow[kb]) * 0x01010101u;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          if (!mbar_wait(&c->a_empty[as], aph ^ 1, abort_flag, p.dev_err)) { aborted = true; break; }
-          tc_fence_after();
-          const uint32_t acol = tl + p.a_base + as * p.a_stride;
-          if (GLU) {
+          const bool mine = GLU || role == h;
+          if (mine) {
             uint32_t r[32];
             if (h == 0) {
-              decode_block<BF16, 0>(w, ti.bits, sc, lut, lev, es, r);
-              decode_block<BF16, 1>(w, ti.bits, sc, lut, lev, es, r + 16);
+              decode_block<0>(w, bits, tab, sc & 255u, r);
+              decode_block<1>(w, bits, tab, (sc >> 8) & 255u, r + 16);
             } else {
-              decode_block<BF16, 2>(w, ti.bits, sc, lut, lev, es, r);
-              decode_block<BF16, 3>(w, ti.bits, sc, lut, lev, es, r + 16);
+              decode_block<2>(w, bits, tab, (sc >> 16) & 255u, r);
+              decode_block<3>(w, bits, tab, sc >> 24, r + 16);
             }
-            tmem_st32(acol + proj * 32, r);
-          } else {
-            uint32_t r[16];
-            if (h == 0) {
-              if (role == 0) decode_block<BF16, 0>(w, ti.bits, sc, lut, lev, es, r);
-              else decode_block<BF16, 1>(w, ti.bits, sc, lut, lev, es, r);
-            } else {
-              if (role == 0) decode_block<BF16, 2>(w, ti.bits, sc, lut, lev, es, r);
-              else decode_block<BF16, 3>(w, ti.bits, sc, lut, lev, es, r);
+            if (pending >= 0) {
+              // the previous half-stage's store is done: hand it to the MMA
+              // (before waiting for a free stage, which may be that one's successor in the ring)
+              tmem_st_wait();
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&c->a_full[pending]);
+              pending = -1;
             }
-            tmem_st16(acol + role * 16, r);
+            if (!mbar_wait(&c->a_empty[as], aph ^ 1, abort_flag, p.dev_err)) { aborted = true; break; }
+            tc_fence_after();
+            tmem_st32(tl + p.a_base + as * p.a_stride + proj * 32, r);
+            pending = static_cast<int>(as);
           }
-          tmem_st_wait();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&c->a_full[as]);
           if (++as == static_cast<uint32_t>(p.da)) { as = 0; aph ^= 1; }
         }
-        if (++rs == static_cast<uint32_t>(p.dr)) { rs = 0; rph ^= 1; }
+      }
+      if (pending >= 0 && !aborted) {
+        // end of the tile: hand over the last half-stage now
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&c->a_full[pending]);
+        pending = -1;
       }
       __syncwarp();
       if (!aborted && lane == 0) mbar_arrive(&c->s_empty[sb]);
     }
+    if (pending >= 0) tmem_st_wait();
   }
 
   tc_fence_before();
@@ -433,12 +554,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
 template <bool GLU, bool BF16>
 static cudaError_t launch_one(const GemmParams& p, int grid, cudaStream_t stream, bool pdl) {
   auto kern = hex_gemm_kernel<GLU, BF16>;
-  static int configured_bytes = 0;   // per instantiation; raised monotonically
+  static int configured_bytes[64] = {};   // per device and instantiation; raised monotonically
+  int dev = 0;
+  cudaGetDevice(&dev);
   const int bytes = static_cast<int>(p.smem_bytes);
-  if (bytes > configured_bytes) {
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (bytes > configured_bytes[dev]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     if (e != cudaSuccess) return e;
-    configured_bytes = bytes;
+    configured_bytes[dev] = bytes;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);

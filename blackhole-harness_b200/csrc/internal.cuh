@@ -11,17 +11,24 @@ namespace hexmoe {
 
 constexpr int kMaxTiers = HEXMOE_MAX_TIERS;
 constexpr int kTileM = 128;      // weight rows per tile (UMMA M)
-constexpr int kKStep = 128;      // reduction elements per TMA stage of index words
-constexpr int kMaxDR = 8;        // deepest index/activation ring
+constexpr int kKStep = 128;      // reduction elements per activation (B operand) stage
+constexpr int kMaxDI = 4;        // deepest index-word ring
+constexpr int kMaxDB = 8;        // deepest activation ring
 constexpr int kMaxDA = 8;        // deepest TMEM operand ring
-constexpr int kGemmThreads = 448;  // 14 warps: TMA, MMA, 4 epilogue, 8 decode
+#ifndef HEXMOE_DEC_GROUPS
+#define HEXMOE_DEC_GROUPS 1
+#endif
+constexpr int kDecGroups = HEXMOE_DEC_GROUPS;   // groups of 8 decoder warps, taking 128-input sub-blocks in turn
+constexpr int kDecWarps = 8 * kDecGroups;
+constexpr int kBWarp = 6 + kDecWarps;   // activation producer
+constexpr int kGemmThreads = (kBWarp + 1) * 32;  // index TMA, MMA, 4 epilogue, decoders, activation TMA
 constexpr uint32_t kTmemCols = 512;
 
 // Everything the grouped-GEMM kernel needs; passed by value as a
 // __grid_constant__ parameter (tensor maps must live in parameter space).
 struct GemmParams {
   CUtensorMap tm_idx[kMaxTiers][2];  // idx stacks viewed as [n*rows_pad, k_pad/32*bits] u32
-  CUtensorMap tm_b;                  // B rows: x [T, H] (gate/up) or act [rows, I_pad] (down)
+  CUtensorMap tm_b;                  // B rows in plan order: x_sorted [rows, H] (gate/up) or act [rows, I_pad] (down)
   const uint8_t* bs[kMaxTiers][2];
   const float* es[kMaxTiers][2];
   const float* lev[kMaxTiers][2];
@@ -35,16 +42,19 @@ struct GemmParams {
   int32_t bm;                  // tokens per tile (align block_m), multiple of 16, <= 128
   int32_t max_blocks;
   int32_t num_slots;           // S = T * topk
-  int32_t topk;                // slot -> token divisor for the gate/up gather
   int32_t rows_pad;            // weight rows per expert in the stack
   int32_t rows_store;          // rows written to the output (<= rows_pad)
   int32_t k_pad;               // reduction length (multiple of 128)
   int32_t block;               // scale block: 32 or 128
   int32_t m_tiles;             // rows_pad / 128
   // shared-memory carve-up (byte offsets from the 1024-aligned base)
-  int32_t dr;                  // index/activation ring depth
+  uint32_t off_tab;            // per-tile code tables: [2][nproj][2 planes][256] x 16 B
   uint32_t off_scale, sz_scale;  // two tile-scale buffers
-  uint32_t off_ring, sz_idx, sz_stage;  // ring stage = idx part + B part
+  int32_t k_idx;               // reduction elements per index stage (128..512, divides k_pad)
+  int32_t di;                  // index ring depth
+  uint32_t off_idx, sz_idx;    // index stage: [nproj][128 rows][k_idx*bits/32 words]
+  int32_t db;                  // activation ring depth
+  uint32_t off_b, sz_b;        // activation stage: [2 halves][bm rows][64 x 16-bit], 128-B swizzled
   uint32_t smem_bytes;         // dynamic shared memory to request
   // TMEM carve-up (columns)
   int32_t nbuf;                // accumulator buffers (1 or 2)
@@ -73,6 +83,11 @@ cudaError_t launch_dequant(const hexmoe_parts& parts, int bits, int block, int n
 cudaError_t launch_combine(const void* y, int y_dtype, int64_t T, int32_t topk, int32_t H, int64_t ld_y, void* out,
                            int out_dtype, cudaStream_t st, bool pdl);
 cudaError_t launch_cast_to16(const float* x, void* out, bool bf16, int64_t n, cudaStream_t st);
+// x_sorted[r] = x[sorted_ids[r] / topk] for every plan row r < npp holding a slot
+// (x in x_dtype, x_sorted 16-bit: bf16 for f32 input); padding rows untouched.
+cudaError_t launch_gather_rows(const void* x, int x_dtype, int64_t T, int32_t H, const int32_t* sid,
+                               const int32_t* npp, int64_t max_rows, int32_t topk, int64_t S, void* xs,
+                               cudaStream_t st, bool pdl);
 cudaError_t launch_route_topk(const void* logits, int dtype, int64_t T, int32_t E, int32_t k, int renorm, float* w,
                               int32_t* ids, cudaStream_t st);
 int32_t* device_error_word();  // address of this device's error word (nullptr on failure)

@@ -335,6 +335,61 @@ cudaError_t launch_combine(const void* y, int y_dtype, int64_t T, int32_t topk, 
 }
 
 // ---------------------------------------------------------------------------
+// Plan-ordered activations: xs[r] = x[sorted_ids[r] / topk] (one warp per row,
+// 16-byte vectors), so the grouped GEMM loads each block's tokens as one TMA
+// box instead of one gather per token.  f32 input is rounded to bf16 here.
+template <typename XT>
+__global__ void gather_rows_kernel(const XT* __restrict__ x, int32_t H, const int32_t* __restrict__ sid,
+                                   const int32_t* __restrict__ npp, int64_t max_rows, int32_t topk, int64_t S,
+                                   uint16_t* __restrict__ xs) {
+  pdl_wait();
+  const int64_t rows = min(static_cast<int64_t>(__ldg(npp)), max_rows);
+  const int lane = threadIdx.x & 31;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t r = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5; r < rows; r += nwarps) {
+    const int s = __ldg(sid + r);
+    if (s >= S) continue;
+    const XT* src = x + static_cast<int64_t>(s / topk) * H;
+    uint4* dst = reinterpret_cast<uint4*>(xs + r * H);
+    for (int c = lane; c < H / 8; c += 32) {
+      if constexpr (sizeof(XT) == 2) {
+        dst[c] = __ldg(reinterpret_cast<const uint4*>(src) + c);
+      } else {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(src) + 2 * c);
+        const float4 b = __ldg(reinterpret_cast<const float4*>(src) + 2 * c + 1);
+        dst[c] = make_uint4(pack2<true>(a.x, a.y), pack2<true>(a.z, a.w), pack2<true>(b.x, b.y),
+                            pack2<true>(b.z, b.w));
+      }
+    }
+  }
+  pdl_launch_dependents();
+}
+
+cudaError_t launch_gather_rows(const void* x, int x_dtype, int64_t T, int32_t H, const int32_t* sid,
+                               const int32_t* npp, int64_t max_rows, int32_t topk, int64_t S, void* xs,
+                               cudaStream_t st, bool pdl) {
+  (void)T;
+  if (max_rows == 0) return cudaSuccess;
+  const int threads = 256;
+  const int64_t warps = max_rows < 148 * 64 ? max_rows : 148 * 64;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>((warps * 32 + threads - 1) / threads));
+  cfg.blockDim = dim3(threads);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  uint16_t* out = static_cast<uint16_t*>(xs);
+  if (x_dtype == HEXMOE_F32)
+    return cudaLaunchKernelEx(&cfg, gather_rows_kernel<float>, static_cast<const float*>(x), H, sid, npp, max_rows,
+                              topk, S, out);
+  return cudaLaunchKernelEx(&cfg, gather_rows_kernel<uint16_t>, static_cast<const uint16_t*>(x), H, sid, npp,
+                            max_rows, topk, S, out);
+}
+
+// ---------------------------------------------------------------------------
 __global__ void cast_kernel(const float* __restrict__ x, uint16_t* __restrict__ out, bool bf16, int64_t n) {
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {

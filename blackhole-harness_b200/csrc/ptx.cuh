@@ -76,6 +76,26 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// The same wait for roles that are not on the critical path (producers ahead of
+// their consumers, the epilogue between tiles): after a few polls the thread
+// sleeps between polls so it does not take issue slots from the decoders.
+__device__ __forceinline__ bool mbar_wait_idle(uint64_t* bar, uint32_t parity, volatile int* abort, int* dev_err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (i > 4) __nanosleep(200);
+    if ((i & 15) == 0) {
+      if (*abort) return false;
+      if (globaltimer() - t0 > kWaitTimeoutNs) {
+        *abort = 1;
+        atomicOr(dev_err, kDevErrTimeout);
+        return false;
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -225,6 +245,13 @@ __host__ __device__ constexpr uint32_t umma_idesc(bool bf16, uint32_t M, uint32_
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Hardware tanh approximation (MUFU.TANH, max relative error about 2^-11).
+__device__ __forceinline__ float tanh_approx(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 // ---------------------------------------------------------------- byte permute

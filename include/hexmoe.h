@@ -132,6 +132,33 @@ HEXMOE_API int hexmoe_forward(const hexmoe_layer* layer, const void* x, int32_t 
                    int32_t ids_dtype, void* out, int32_t out_dtype, int32_t block_m,
                    void* workspace, size_t workspace_bytes, void* stream);
 
+/* The phases of hexmoe_forward, for callers that own the plan (or time the
+ * phases apart).  They replace the two _launch calls per tier and the sum of
+ * hex_moe_fused (hex_moe.py:286-301, 321-325); one call covers every tier.
+ *   plan      sorted_ids / expert_ids / npp from hexmoe_align with block_m
+ *   gather    x_sorted[r] = x[sorted_ids[r] / topk] for every plan row r that
+ *             holds a slot; x_sorted [max_blocks*block_m, hidden], 16-bit
+ *             (BF16 for an F32 x), padding rows untouched
+ *   gate/up   act[r, o] = silu(x_sorted[r] . Wg[e, o]) * (x_sorted[r] . Wu[e, o])
+ *             for every plan row r, rounded to x_sorted's dtype; act is
+ *             [max_blocks*block_m, inter_pad] (padding rows untouched)
+ *   down      y[slot, h] = (act[r] . Wd[e, h]) * topk_weights[slot], slot =
+ *             sorted_ids[r]; y [tokens*topk, hidden] in act's dtype
+ *   combine   out[t, h] = sum_j y[t*topk + j, h] (fp32 sum, rounded once)
+ * x / act / y dtypes: BF16 or F16. */
+HEXMOE_API int hexmoe_gather(const void* x, int32_t x_dtype, int64_t tokens, int32_t hidden, int32_t topk,
+                             int32_t num_experts, const int32_t* sorted_ids, const int32_t* npp,
+                             int32_t block_m, void* x_sorted, void* stream);
+HEXMOE_API int hexmoe_gate_up(const hexmoe_layer* layer, const void* x_sorted, int32_t x_dtype, int64_t tokens,
+                              int32_t topk, const int32_t* sorted_ids, const int32_t* expert_ids,
+                              const int32_t* npp, int32_t block_m, void* act, void* stream);
+HEXMOE_API int hexmoe_down(const hexmoe_layer* layer, const void* act, int32_t act_dtype, int64_t tokens,
+                           int32_t topk, const float* topk_weights, const int32_t* sorted_ids,
+                           const int32_t* expert_ids, const int32_t* npp, int32_t block_m, void* y,
+                           void* stream);
+HEXMOE_API int hexmoe_combine(const void* y, int32_t y_dtype, int64_t tokens, int32_t topk, int32_t hidden,
+                              void* out, int32_t out_dtype, void* stream);
+
 /* Group slots by expert, each expert's run padded to block_m (align,
  * hex_moe.py:201-222): sorted_ids int32 [max_blocks*block_m] (padding = S),
  * expert_ids int32 [max_blocks] (-1 = unused), npp int32 [1] = padded length,
