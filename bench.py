@@ -381,7 +381,7 @@ def main() -> None:
             dist.barrier()
             dist.destroy_process_group()
         return
-    launches = 4 * args.steps
+    launches = 5 * args.steps   # align, gather, gate/up, down, combine per step
     traffic = read_traffic()
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
