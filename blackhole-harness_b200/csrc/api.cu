@@ -252,6 +252,9 @@ int check_phase(const hexmoe_layer* layer, int32_t dt, int64_t tokens, int32_t t
 
 }  // namespace
 
+int hexmoe::report_error(int code, const char* msg) { return fail(code, "%s", msg); }
+int hexmoe::report_cuda_error(cudaError_t e, const char* what) { return cuda_fail(e, what); }
+
 extern "C" {
 
 int hexmoe_abi_version(void) { return HEXMOE_ABI_VERSION; }

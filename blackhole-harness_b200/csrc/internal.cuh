@@ -93,5 +93,8 @@ cudaError_t launch_route_topk(const void* logits, int dtype, int64_t T, int32_t 
 int32_t* device_error_word();  // address of this device's error word (nullptr on failure)
 cudaError_t read_device_error(int32_t* value, bool clear);   // synchronous, current device
 cudaError_t launch_build_expert_map(const hexmoe_layer_desc& d, int32_t* map, cudaStream_t st);
+// Record `msg` as the calling thread's hexmoe_last_error() and return `code`.
+int report_error(int code, const char* msg);
+int report_cuda_error(cudaError_t e, const char* what);
 
 }  // namespace hexmoe

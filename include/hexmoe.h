@@ -132,6 +132,24 @@ HEXMOE_API int hexmoe_forward(const hexmoe_layer* layer, const void* x, int32_t 
                    int32_t ids_dtype, void* out, int32_t out_dtype, int32_t block_m,
                    void* workspace, size_t workspace_bytes, void* stream);
 
+/* hexmoe_forward for callers that cannot allocate device memory and so have no
+ * workspace to pass (a serving process whose memory pool already holds nearly
+ * all of the GPU, a plugin host that owns every device allocation, a loop that
+ * must not synchronise on cudaMalloc).  No counterpart in the reference: its
+ * Triton launches take their scratch from torch's allocator.  Same arguments
+ * and result as hexmoe_forward, minus the workspace: the scratch is one fixed
+ * array of HEXMOE_NOALLOC_SCRATCH_BYTES inside the library, held by every GPU
+ * that loads it until the process exits.  Calls whose scratch need
+ * (hexmoe_forward_workspace_bytes) exceeds it fail with HEXMOE_E_ARG.  The
+ * first call on a device looks the array up on that device (make it before any
+ * stream capture).  All calls on a device share the array: calls that overlap
+ * on the GPU race and must be ordered by the caller.  Allocates nothing. */
+#define HEXMOE_NOALLOC_SCRATCH_BYTES (32u << 20)
+HEXMOE_API int hexmoe_forward_noalloc(const hexmoe_layer* layer, const void* x, int32_t x_dtype, int64_t tokens,
+                                      int32_t topk, const float* topk_weights, const void* topk_ids,
+                                      int32_t ids_dtype, void* out, int32_t out_dtype, int32_t block_m,
+                                      void* stream);
+
 /* The phases of hexmoe_forward, for callers that own the plan (or time the
  * phases apart).  They replace the two _launch calls per tier and the sum of
  * hex_moe_fused (hex_moe.py:286-301, 321-325); one call covers every tier.
