@@ -295,7 +295,7 @@ def main() -> None:
     def flush():
         flush_buf.fill_(rank & 0xFF)
 
-    bm = 16
+    bm = 16 if T <= 64 else 128     # align block height: decode batches / prefill
 
     def step_eager():
         layer.forward(x, w, ids, bm)
@@ -305,7 +305,8 @@ def main() -> None:
             step_eager()
         plan = layer.plan(ids, bm)
         xs = layer.gather(x, K_TOP, plan, bm)
-        layer.gate_up(xs, T, K_TOP, plan, bm)
+        act = layer.gate_up(xs, T, K_TOP, plan, bm)
+        layer.down(act, w, plan, bm)
         torch.cuda.synchronize()
         return
 

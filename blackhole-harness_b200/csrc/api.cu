@@ -141,6 +141,10 @@ int plan_gemm(GemmParams& p, bool glu, int bm, int k_pad, int block, int max_bit
   if (!p.di) return fail(HEXMOE_E_UNSUPPORTED, "reduction length %d / block_m %d do not fit shared memory", k_pad, bm);
   p.off_b = static_cast<uint32_t>(align_up(p.off_idx + static_cast<size_t>(p.di) * p.sz_idx, 1024));
   p.smem_bytes = std::max<uint32_t>(p.off_b + p.db * p.sz_b + 1024, 120 * 1024);
+  // gate/up: two threads issue the MMAs, one projection (accumulator) each: one
+  // tcgen05.mma of N <= 64 columns keeps its issuing thread busy longer than the
+  // tensor pipe takes to run it.
+  p.n_iss = glu ? 2 : 1;
   p.acc_stride = static_cast<uint32_t>(nproj * bm);
   p.a_stride = static_cast<uint32_t>(32 * nproj);
   p.nbuf = (2 * p.acc_stride + 2 * p.a_stride <= kTmemCols) ? 2 : 1;

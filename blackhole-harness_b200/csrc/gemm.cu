@@ -8,7 +8,7 @@
 // side (16..128 columns), so a decode step with a handful of tokens per expert
 // still streams every weight once at full width.
 //
-// Warp roles (32 x (7 + 8 x decoder groups) threads):
+// Warp roles (32 x (8 + 8 x decoder groups) threads):
 //   warp 0      producer: per tile a record (block, weight tile, tier, valid
 //               rows, level tables, expert scales, the block's slot ids and
 //               top-k weights) into a small shared ring and the tile's fp8
@@ -16,12 +16,13 @@
 //               tile, one 2-D TMA box of 128 rows x k_idx inputs (k_idx up to
 //               512, so each row moved is 144-256 bytes: TMA cost is per row),
 //               into a ring the decoders release
-//   last warp   activation producer: the block's rows of the plan-ordered
+//   warp 6+dec  activation producer: the block's rows of the plan-ordered
 //               activations, two 64-column boxes per 128 inputs, into a ring
 //               the MMA releases (its own warp, so a full activation ring never
 //               delays the next index stage)
-//   warp 1      TMEM allocation; one thread issues tcgen05.mma (A operand from
-//               TMEM, B from 128-B swizzled smem) and tcgen05.commit
+//   warp 1,     TMEM allocation (warp 1); one thread of each issues tcgen05.mma
+//   last warp   (A operand from TMEM, B from 128-B swizzled smem) and
+//               tcgen05.commit: gate and up each, or (down) warp 1 alone
 //   warps 2-5   epilogue: tcgen05.ld of the accumulators, SwiGLU (gate/up) or
 //               the top-k weight (down), 16-bit stores
 //   warps 6..   decoders, groups of 8 taking 128-input sub-blocks in turn:
@@ -33,6 +34,8 @@
 //               next half-stage is decoded, so the TMEM write latency overlaps
 // Every wait is bounded (ptx.cuh): a lost arrival ends the kernel with the
 // device error word set instead of hanging.
+#include <type_traits>
+
 #include "decode.cuh"
 #include "internal.cuh"
 
@@ -48,7 +51,7 @@ struct Ctrl {
   uint64_t t_full[2], t_empty[2];             // accumulator buffers
   uint64_t i_full[kRecs], i_empty[kRecs];     // tile records
   uint64_t tab_ready[2];                      // code tables built (per buffer)
-  uint64_t drain;
+  uint64_t drain[2];
   uint32_t tmem_base;
   int32_t abort;
 };
@@ -139,15 +142,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kMaxDI; ++i) { mbar_init(&c->x_full[i], 1); mbar_init(&c->x_empty[i], kDecWarps); }
-    for (int i = 0; i < kMaxDB; ++i) { mbar_init(&c->b_full[i], 1); mbar_init(&c->b_empty[i], 1); }
-    for (int i = 0; i < kMaxDA; ++i) { mbar_init(&c->a_full[i], GLU ? 8 : 4); mbar_init(&c->a_empty[i], 1); }
+    for (int i = 0; i < kMaxDB; ++i) { mbar_init(&c->b_full[i], 1); mbar_init(&c->b_empty[i], p.n_iss); }
+    for (int i = 0; i < kMaxDA; ++i) { mbar_init(&c->a_full[i], GLU ? 8 : 4); mbar_init(&c->a_empty[i], p.n_iss); }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&c->s_full[i], 1); mbar_init(&c->s_empty[i], kDecWarps);
-      mbar_init(&c->t_full[i], 1); mbar_init(&c->t_empty[i], 4);
+      mbar_init(&c->t_full[i], p.n_iss); mbar_init(&c->t_empty[i], 4);
       mbar_init(&c->tab_ready[i], kDecWarps);
     }
-    for (int i = 0; i < kRecs; ++i) { mbar_init(&c->i_full[i], 1); mbar_init(&c->i_empty[i], 6 + kDecWarps); }
-    mbar_init(&c->drain, 1);
+    for (int i = 0; i < kRecs; ++i) { mbar_init(&c->i_full[i], 1); mbar_init(&c->i_empty[i], 7 + kDecWarps); }
+    mbar_init(&c->drain[0], 1);
+    mbar_init(&c->drain[1], 1);
     c->abort = 0;
     fence_mbar_init();
   }
@@ -287,8 +291,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
         drain_wait(&c->b_full[q % p.db], (q / p.db) & 1);
       }
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
+  } else if (warp == 1 || warp == kMma2Warp) {
+    // ------------------------------------------------------------ MMA issuers
+    // gate/up: issuer mi owns projection mi (its own accumulator); down: warp 1
+    // issues everything and the second issuer only follows the tile records.
+    const int mi = warp == 1 ? 0 : 1;
+    const bool active = mi < p.n_iss;
     uint32_t bs = 0, bph = 0, as = 0, aph = 0;
     bool aborted = false;
     int cur = 0, acc_it = 0;
@@ -298,30 +306,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
       const int ok = recs[ri].ok, cnt = recs[ri].cnt;
       __syncwarp();
       if (lane == 0) mbar_arrive(&c->i_empty[ri]);
-      if (!ok) continue;
+      if (!ok || !active) continue;
       const uint32_t n_mma = static_cast<uint32_t>(max(16, (cnt + 15) & ~15));
       const uint32_t idesc = umma_idesc(BF16, 128, n_mma);
       const int ab = acc_it % p.nbuf;
       if (!mbar_wait(&c->t_empty[ab], ((acc_it / p.nbuf) & 1) ^ 1, abort_flag, p.dev_err)) { aborted = true; break; }
       ++acc_it;
       tc_fence_after();
-      const uint32_t d0 = tmem + ab * p.acc_stride;
-      const uint32_t d1 = d0 + p.bm;
+      const uint32_t d = tmem + ab * p.acc_stride + mi * p.bm;
+      const uint32_t h_step = static_cast<uint32_t>(p.bm * 128) >> 4;   // descriptor units per 64-input half
       for (int ks = 0; ks < ksteps && !aborted; ++ks) {
         if (!mbar_wait(&c->b_full[bs], bph, abort_flag, p.dev_err)) { aborted = true; break; }
-        const uint32_t bbase = smem_u32(bring + bs * p.sz_b);
+        const uint64_t bdesc = sw128_desc(smem_u32(bring + bs * p.sz_b));
         for (int h = 0; h < 2; ++h) {
           if (!mbar_wait(&c->a_full[as], aph, abort_flag, p.dev_err)) { aborted = true; break; }
           tc_fence_after();
           if (lane == 0) {
-            const uint32_t a0 = tmem + p.a_base + as * p.a_stride;
+            const uint32_t a0 = tmem + p.a_base + as * p.a_stride + mi * 32;
+            const uint64_t bh = bdesc + h * h_step;
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-              const uint64_t bd = sw128_desc(bbase + h * p.bm * 128 + kk * 32);
-              const uint32_t acc = (ks | h | kk) != 0;
-              umma_f16_ts(d0, a0 + kk * 8, bd, idesc, acc);
-              if (GLU) umma_f16_ts(d1, a0 + 32 + kk * 8, bd, idesc, acc);
-            }
+            for (int kk = 0; kk < 4; ++kk) umma_f16_ts(d, a0 + kk * 8, bh + kk * 2, idesc, (ks | h | kk) != 0);
             umma_commit(&c->a_empty[as]);
           }
           __syncwarp();
@@ -336,9 +340,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
       if (lane == 0) umma_commit(&c->t_full[ab]);
       __syncwarp();
     }
-    if (aborted && lane == 0) {
-      umma_commit(&c->drain);   // every MMA issued so far has finished once this arrives
-      drain_wait(&c->drain, 0);
+    if (aborted && active && lane == 0) {
+      umma_commit(&c->drain[mi]);   // every MMA this thread issued has finished once this arrives
+      drain_wait(&c->drain[mi], 0);
     }
   } else if (warp < 6) {
     // ------------------------------------------------------------ epilogue
@@ -433,6 +437,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
     bool aborted = false;
     int cur = 0, work = 0;
     int pending = -1;                        // operand stage stored to TMEM but not yet handed over
+    uint32_t ba[16], bb[16];                 // decoded 32-input blocks, alternating store buffers
+#pragma unroll
+    for (int i = 0; i < 16; ++i) ba[i] = bb[i] = 0u;
     for (int t = blockIdx.x; t < num_tiles && !aborted; t += gridDim.x, ++cur) {
       const int ri = cur % kRecs;
       if (!mbar_wait(&c->i_full[ri], (cur / kRecs) & 1, abort_flag, p.dev_err)) { aborted = true; break; }
@@ -465,75 +472,83 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
       ++work;
       const uint4* tab = tabs + (tb * NPROJ + proj) * 512;
       const uint8_t* srow = scale_buf + (sb * NPROJ + proj) * p.sz_scale + row * spr;
-      const uint32_t wst = static_cast<uint32_t>(p.k_idx / 32 * bits);
-      for (int kb = 0; kb < ksteps && !aborted; ++kb) {
-        const int sub = kb % spi;
-        const bool mine_k = (kb % kDecGroups) == group;
-        if (sub == 0) {
-          if (!mbar_wait(&c->x_full[xs], xph, abort_flag, p.dev_err)) { aborted = true; break; }
-        }
-        uint32_t w[16];
-        if (mine_k) {
-          const uint4* w4 = reinterpret_cast<const uint4*>(xring + xs * p.sz_idx + ((proj * 128 + row) * wst) * 4) +
-                            sub * bits;
-          const uint4 v0 = w4[0], v1 = w4[1], v2 = w4[2];
-          w[0] = v0.x; w[1] = v0.y; w[2] = v0.z; w[3] = v0.w;
-          w[4] = v1.x; w[5] = v1.y; w[6] = v1.z; w[7] = v1.w;
-          w[8] = v2.x; w[9] = v2.y; w[10] = v2.z; w[11] = v2.w;
-          if (bits == 4) {
-            const uint4 v3 = w4[3];
-            w[12] = v3.x; w[13] = v3.y; w[14] = v3.z; w[15] = v3.w;
-          } else {
-            w[12] = w[13] = w[14] = w[15] = 0u;
+      // the sub-block loop is specialised on the tile's index width: no per-block branch
+      auto kb_loop = [&](auto bits_c) {
+        constexpr int BITS = decltype(bits_c)::value;
+        const uint32_t wst = static_cast<uint32_t>(p.k_idx / 32 * BITS);
+        for (int kb = 0; kb < ksteps && !aborted; ++kb) {
+          const int sub = kb % spi;
+          const bool mine_k = (kb % kDecGroups) == group;
+          if (sub == 0) {
+            if (!mbar_wait(&c->x_full[xs], xph, abort_flag, p.dev_err)) { aborted = true; break; }
           }
-        }
-        if (sub == spi - 1) {
-          // every sub-block of the stage this group reads is in registers: release it
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&c->x_empty[xs]);
-          if (++xs == static_cast<uint32_t>(p.di)) { xs = 0; xph ^= 1; }
-        }
-        if (!mine_k) {
-          // another group's two half-stages
-          as += 2;
-          if (as >= static_cast<uint32_t>(p.da)) { as -= p.da; aph ^= 1; }
-          continue;
-        }
-        uint32_t sc;   // scale codes of the 4 blocks of this 128-input step, one byte each
-        if (p.block == 32) sc = *reinterpret_cast<const uint32_t*>(srow + kb * 4);
-        else sc = static_cast<uint32_t>(srow[kb]) * 0x01010101u;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const bool mine = GLU || role == h;
-          if (mine) {
-            uint32_t r[32];
-            if (h == 0) {
-              decode_block<0>(w, bits, tab, sc & 255u, r);
-              decode_block<1>(w, bits, tab, (sc >> 8) & 255u, r + 16);
+          uint32_t w[16];
+          if (mine_k) {
+            const uint4* w4 = reinterpret_cast<const uint4*>(xring + xs * p.sz_idx + ((proj * 128 + row) * wst) * 4) +
+                              sub * BITS;
+            const uint4 v0 = w4[0], v1 = w4[1], v2 = w4[2];
+            w[0] = v0.x; w[1] = v0.y; w[2] = v0.z; w[3] = v0.w;
+            w[4] = v1.x; w[5] = v1.y; w[6] = v1.z; w[7] = v1.w;
+            w[8] = v2.x; w[9] = v2.y; w[10] = v2.z; w[11] = v2.w;
+            if (BITS == 4) {
+              const uint4 v3 = w4[3];
+              w[12] = v3.x; w[13] = v3.y; w[14] = v3.z; w[15] = v3.w;
             } else {
-              decode_block<2>(w, bits, tab, (sc >> 16) & 255u, r);
-              decode_block<3>(w, bits, tab, sc >> 24, r + 16);
+              w[12] = w[13] = w[14] = w[15] = 0u;
             }
-            if (pending >= 0) {
-              // the previous half-stage's store is done: hand it to the MMA
-              // (before waiting for a free stage, which may be that one's successor in the ring)
-              tmem_st_wait();
-              tc_fence_before();
-              __syncwarp();
-              if (lane == 0) mbar_arrive(&c->a_full[pending]);
-              pending = -1;
-            }
-            if (!mbar_wait(&c->a_empty[as], aph ^ 1, abort_flag, p.dev_err)) { aborted = true; break; }
-            tc_fence_after();
-            tmem_st32(tl + p.a_base + as * p.a_stride + proj * 32, r);
-            pending = static_cast<int>(as);
           }
-          if (++as == static_cast<uint32_t>(p.da)) { as = 0; aph ^= 1; }
+          if (sub == spi - 1) {
+            // every sub-block of the stage this group reads is in registers: release it
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&c->x_empty[xs]);
+            if (++xs == static_cast<uint32_t>(p.di)) { xs = 0; xph ^= 1; }
+          }
+          if (!mine_k) {
+            // another group's two half-stages
+            as += 2;
+            if (as >= static_cast<uint32_t>(p.da)) { as -= p.da; aph ^= 1; }
+            continue;
+          }
+          uint32_t sc;   // scale codes of the 4 blocks of this 128-input step, one byte each
+          if (p.block == 32) sc = *reinterpret_cast<const uint32_t*>(srow + kb * 4);
+          else sc = static_cast<uint32_t>(srow[kb]) * 0x01010101u;
+  #pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const bool mine = GLU || role == h;
+            if (mine) {
+              // the two 32-input blocks of this half go through alternating
+              // 16-register buffers: a block is decoded while the other buffer's
+              // store is in flight, and each wait names the buffer it frees
+              const uint32_t acol = tl + p.a_base + as * p.a_stride + proj * 32;
+              if (h == 0) decode_block<0>(w, BITS, tab, sc & 255u, ba);
+              else decode_block<2>(w, BITS, tab, (sc >> 16) & 255u, ba);
+              tmem_st_wait_keep(bb);
+              if (pending >= 0) {
+                // the previous half-stage's stores are done: hand it to the MMA
+                // (before waiting for a free stage, which may be that one's successor in the ring)
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&c->a_full[pending]);
+                pending = -1;
+              }
+              if (!mbar_wait(&c->a_empty[as], aph ^ 1, abort_flag, p.dev_err)) { aborted = true; break; }
+              tc_fence_after();
+              tmem_st16(acol, ba);
+              if (h == 0) decode_block<1>(w, BITS, tab, (sc >> 8) & 255u, bb);
+              else decode_block<3>(w, BITS, tab, sc >> 24, bb);
+              tmem_st_wait_keep(ba);
+              tmem_st16(acol + 16, bb);
+              pending = static_cast<int>(as);
+            }
+            if (++as == static_cast<uint32_t>(p.da)) { as = 0; aph ^= 1; }
+          }
         }
-      }
+      };
+      if (bits == 3) kb_loop(std::integral_constant<int, 3>{});
+      else kb_loop(std::integral_constant<int, 4>{});
       if (pending >= 0 && !aborted) {
         // end of the tile: hand over the last half-stage now
-        tmem_st_wait();
+        tmem_st_wait_keep(bb);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&c->a_full[pending]);

@@ -197,6 +197,16 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       : "memory");
 }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+// tcgen05.st reads its source registers after it issues: registers handed to a
+// store must not be rewritten before tcgen05.wait::st (a rewrite stalls the warp
+// until the store completes).  This wait names the registers of the store it
+// covers, so the compiler keeps them (and nothing else) there until the wait.
+__device__ __forceinline__ void tmem_st_wait_keep(const uint32_t (&r)[16]) {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::"r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]),
+               "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+               "r"(r[15])
+               : "memory");
+}
 
 // D[tmem] (+)= A[tmem] * B[smem]^T: A (M=128 rows = lanes, K packed two 16-bit
 // values per 32-bit column) read from tensor memory, B from a smem descriptor.
