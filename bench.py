@@ -59,7 +59,8 @@ def peaks() -> dict:
 
 
 class Clocks:
-    """SM clock and throttle-reason sampling (NVML, every 2 ms) during the timed region."""
+    """SM clock and throttle-reason sampling (NVML, back to back: a few hundred µs per
+    sample) during the timed region."""
     REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
                0x80: "hw_power_brake_slowdown"}
 
@@ -90,7 +91,7 @@ class Clocks:
                 self.samples.append((sm, rs, pw))
             except Exception:  # noqa: BLE001
                 pass
-            self.stop_ev.wait(0.002)
+            self.stop_ev.wait(0.0001)
 
     def stop(self) -> dict | None:
         if self.thread is None:
@@ -282,6 +283,7 @@ def main() -> None:
     dev = torch.device("cuda", local)
     if world > 1:
         from datetime import timedelta
+        os.environ.setdefault("NCCL_DEBUG", "WARN")     # stdout carries the JSON line only
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     T = args.tokens
     L, tiers = build_layer(dev, seed=0)
@@ -374,8 +376,10 @@ def main() -> None:
     err = device_status(local)
 
     extras = {}
+    if world > 1 and not args.no_extras:
+        extras["prefill_ep"] = run_ep_prefill(dev, rank, world, flush, stream, pk)   # every rank takes part
     if not args.no_extras and rank == 0:
-        extras = run_extras(dev, L, tiers, layer, flush, stream, args, pk)
+        extras.update(run_extras(dev, L, tiers, layer, flush, stream, args, pk, cpu=world == 1))
 
     if rank != 0:
         if world > 1:
@@ -410,6 +414,39 @@ def main() -> None:
         dist.destroy_process_group()
 
 
+def run_ep_prefill(dev, rank: int, world: int, flush, stream, pk, T: int = 4096, steps: int = 5) -> dict:
+    """cfg3 prefill with expert parallelism: the 96 experts (mixed 3/4-bit) sharded
+    over the ranks, T tokens per rank routed to their owners by all-to-all
+    (blackhole_b200.ep), max-over-ranks time per step."""
+    import torch
+    import torch.distributed as dist
+
+    from blackhole_b200 import hex_data as hd
+    from blackhole_b200.ep import EPMoE, ExpertShard, shard_tiers
+    from blackhole_b200.hex_moe import HexTier
+    Lm = hd.synth_layer(E, H, I, "mixed", BLOCK, seed=0, device=dev)
+    shard = ExpertShard(E, rank, world)
+    local = [HexTier(t["bits"], t["experts"], t["gate_proj"], t["up_proj"], t["down_proj"]).prepare(E)
+             for t in shard_tiers(Lm.tiers, shard)]
+    del Lm
+    ep = EPMoE(shard, local)
+    w, ids = hd.synth_routing(T, E, K_TOP, seed=7 + 1000 * rank, device=dev)
+    x = hd.synth_x(T, H, seed=8 + 1000 * rank, device=dev)
+    for _ in range(2):
+        ep(x, w, ids)
+    torch.cuda.synchronize()
+    dist.barrier()
+    ms = time_steps(lambda: ep(x, w, ids), steps, flush, stream)
+    tt = torch.tensor([sum(ms)], device=dev)
+    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    step_ms = float(tt) / steps
+    flops = 2.0 * world * T * K_TOP * 3 * H * I
+    return {"workload": f"cfg3 prefill with expert parallelism: E={E} H={H} I={I} top-{K_TOP}, mixed 3/4-bit HEX, "
+                        f"{E // world} experts and {T} tokens per GPU, NCCL all-to-all dispatch/combine",
+            "tokens_per_s": world * T / (step_ms * 1e-3), "ms": step_ms, "TFLOPs": flops / (step_ms * 1e-3) / 1e12,
+            "bf16_frac_per_gpu": flops / world / (step_ms * 1e-3) / 1e12 / pk["bf16_tflops"], "scaling": "weak"}
+
+
 def read_traffic():
     """DRAM bytes per launch of the gate/up kernel from the committed ncu summary, if any."""
     p = ROOT / "profiles" / "traffic.json"
@@ -421,7 +458,7 @@ def read_traffic():
     return None
 
 
-def run_extras(dev, L, tiers, layer, flush, stream, args, pk) -> dict:
+def run_extras(dev, L, tiers, layer, flush, stream, args, pk, cpu: bool = True) -> dict:
     import torch
 
     from blackhole_b200 import hex_data as hd
@@ -471,10 +508,11 @@ def run_extras(dev, L, tiers, layer, flush, stream, args, pk) -> dict:
                       "gate_up_bf16_frac": gflops / g / 1e9 / pk["bf16_tflops"]}
     del lay3, t3, L3, act, xs, g3, g3u
     torch.cuda.empty_cache()
-    try:
-        out["cpu_baseline"] = cpu_baseline()
-    except Exception as e:  # noqa: BLE001  (the baseline is reported, not required)
-        out["cpu_baseline"] = {"value": None, "error": f"{type(e).__name__}: {e}"}
+    if cpu:   # rank 0 at N=1 only
+        try:
+            out["cpu_baseline"] = cpu_baseline()
+        except Exception as e:  # noqa: BLE001  (the baseline is reported, not required)
+            out["cpu_baseline"] = {"value": None, "error": f"{type(e).__name__}: {e}"}
     return out
 
 

@@ -1,0 +1,171 @@
+"""Expert parallelism for the HEX MoE layer over a torch.distributed process group.
+
+The reference plugin refuses expert and tensor parallelism
+(runtime/blackhole_runtime/vllm_hex.py:101-102) and runs one GPU; this module is
+the multi-GPU path for the prefill configs.  Experts are sharded contiguously
+over the ranks (rank r owns global experts [r * P, (r + 1) * P), P =
+ceil(E / world)) and each rank holds only its experts' HEX tiers.
+
+Forward for the T tokens of this rank (global expert ids in topk_ids):
+  1. the S = T * k slots (t, j), grouped by the rank that owns expert
+     topk_ids[t, j] (stable, so each rank's slots keep their order);
+  2. an all-to-all of the per-rank slot counts, then of the slots' token rows
+     (in the activation dtype), expert ids and top-k weights;
+  3. the local experts on the received rows: the layer at top-1, each row with
+     its own weight, so every row comes back as w * down(silu(gate x) * up x)
+     rounded to the activation dtype, exactly as the single-GPU layer rounds
+     each slot before its combine;
+  4. an all-to-all of those rows back to the ranks they came from;
+  5. out[t] = the k returned rows of token t summed in fp32 and rounded (the
+     layer's own combine kernel on the GPU).
+Each slot goes through the same arithmetic as in the single-GPU layer, so the
+result equals the single-GPU output bit for bit.  Traffic per rank: 2 x S x H
+activation rows plus 12 bytes of metadata per slot.
+
+Collectives: one all-reduce of an argument-error flag, then plain all-to-alls
+(NCCL on GPUs) with a host read of the per-rank counts (they set the split
+lists).  Every rank runs the same collectives in the same order, including ranks
+with no tokens and calls that end in an argument error.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable
+
+import torch
+import torch.distributed as dist
+
+PROJ = ("gate_proj", "up_proj", "down_proj")
+
+
+@dataclass(frozen=True)
+class ExpertShard:
+    """Which global experts a rank owns."""
+    num_experts: int
+    rank: int
+    world: int
+
+    @property
+    def per_rank(self) -> int:
+        return -(-self.num_experts // self.world)
+
+    @property
+    def local_range(self) -> tuple[int, int]:
+        lo = min(self.rank * self.per_rank, self.num_experts)
+        return lo, min(lo + self.per_rank, self.num_experts)
+
+    def owner(self, ids: torch.Tensor) -> torch.Tensor:
+        return torch.div(ids, self.per_rank, rounding_mode="floor")
+
+
+def shard_tiers(tiers: list, shard: ExpertShard) -> list:
+    """The tiers restricted to this rank's experts (tier dicts of the HEX parts, or
+    unprepared HexTier objects): every part stacked over experts keeps only the
+    local experts' slices, in the same order; tiers with none are dropped."""
+    lo, hi = shard.local_range
+    out = []
+    for t in tiers:
+        is_dict = isinstance(t, dict)
+        experts = torch.as_tensor(t["experts"] if is_dict else t.experts)
+        keep = torch.nonzero((experts >= lo) & (experts < hi)).flatten()
+        if keep.numel() == 0:
+            continue
+        projs = {p: {q: torch.as_tensor(v).index_select(0, keep.to(torch.as_tensor(v).device))
+                     for q, v in (t[p] if is_dict else getattr(t, p)).items()} for p in PROJ}
+        ex = experts.index_select(0, keep)
+        if is_dict:
+            out.append({"bits": t["bits"], "experts": ex, **projs})
+        else:
+            out.append(type(t)(t.bits, ex, projs["gate_proj"], projs["up_proj"], projs["down_proj"]))
+    return out
+
+
+ExpertFn = Callable[[torch.Tensor, torch.Tensor, torch.Tensor], torch.Tensor]
+CombineFn = Callable[[torch.Tensor, int, int], torch.Tensor]
+
+
+def _sum_combine(y: torch.Tensor, T: int, k: int) -> torch.Tensor:
+    """The combine of the CUDA layer on any device: slots added in order in fp32."""
+    yv = y.view(T, k, -1)
+    acc = yv[:, 0].float()
+    for j in range(1, k):
+        acc = acc + yv[:, j].float()
+    return acc.to(y.dtype)
+
+
+class EPMoE:
+    """The HEX MoE layer with experts sharded over `group`.
+
+    local_tiers: this rank's prepared HexTier list (from shard_tiers(...) then
+    HexTier.prepare(num_experts)); expert_fn / combine_fn replace the CUDA layer
+    (tests run the host logic on CPU ranks with the oracle as expert_fn)."""
+
+    def __init__(self, shard: ExpertShard, local_tiers: list | None = None, group=None,
+                 expert_fn: ExpertFn | None = None, combine_fn: CombineFn | None = None):
+        self.shard = shard
+        self.group = group
+        self.local_tiers = local_tiers
+        self._layer = None
+        if expert_fn is None:
+            if local_tiers is None:
+                raise ValueError("EPMoE needs the local tiers or an expert_fn")
+            from blackhole_b200.hex_moe import hex_moe, layer_for
+            self._layer = layer_for(local_tiers)
+            expert_fn = lambda xr, wr, ir: hex_moe(xr, wr[:, None], ir[:, None], local_tiers)  # noqa: E731
+            if combine_fn is None:
+                combine_fn = lambda y, T, k: self._layer.combine(y, T, k)  # noqa: E731
+        self.expert_fn = expert_fn
+        self.combine_fn = combine_fn or _sum_combine
+
+    def _a2a(self, out: torch.Tensor, inp: torch.Tensor, out_splits: list[int], in_splits: list[int]) -> None:
+        dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
+
+    def forward(self, x: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.Tensor) -> torch.Tensor:
+        if x.dim() != 2 or topk_ids.dim() != 2 or topk_weights.shape != topk_ids.shape or x.shape[0] != topk_ids.shape[0]:
+            raise ValueError("x [T, H], topk_weights and topk_ids [T, k] expected")
+        T, k = topk_ids.shape
+        H = x.shape[1]
+        dev = x.device
+        world = self.shard.world
+        ids = topk_ids.reshape(-1).to(torch.int64)
+        w = topk_weights.reshape(-1).to(torch.float32)
+        # argument errors are agreed on by every rank before any data moves, so a
+        # bad rank never leaves the others waiting inside a collective
+        bad = bool(ids.numel()) and (int(ids.min()) < 0 or int(ids.max()) >= self.shard.num_experts)
+        flag = torch.tensor([1 if bad else 0], dtype=torch.int64, device=dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MAX, group=self.group)
+        if int(flag.item()):
+            raise ValueError("topk_ids out of range" if bad else "topk_ids out of range on another rank")
+        owner = self.shard.owner(ids)
+        order = torch.argsort(owner, stable=True)
+        send_counts = torch.bincount(owner, minlength=world).to(torch.int64)
+        recv_counts = torch.empty_like(send_counts)
+        dist.all_to_all_single(recv_counts, send_counts, group=self.group)
+        sc, rc = send_counts.tolist(), recv_counts.tolist()
+        n_recv = sum(rc)
+        # 2. token rows, ids and weights of the slots, grouped by owner
+        send_x = x.index_select(0, torch.div(order, k, rounding_mode="floor"))
+        recv_x = torch.empty(n_recv, H, dtype=x.dtype, device=dev)
+        self._a2a(recv_x, send_x, rc, sc)
+        meta = torch.stack([ids.index_select(0, order), w.index_select(0, order).view(torch.int32).to(torch.int64)], 1)
+        recv_meta = torch.empty(n_recv, 2, dtype=torch.int64, device=dev)
+        self._a2a(recv_meta, meta, rc, sc)
+        recv_ids = recv_meta[:, 0].contiguous()
+        recv_w = recv_meta[:, 1].to(torch.int32).view(torch.float32).contiguous()
+        # 3. local experts, one slot per row
+        if n_recv:
+            y_recv = self.expert_fn(recv_x, recv_w, recv_ids)
+        else:
+            y_recv = torch.empty(0, H, dtype=x.dtype, device=dev)
+        # 4. rows back to their source rank, in the order they were sent
+        back = torch.empty(T * k, H, dtype=x.dtype, device=dev)
+        self._a2a(back, y_recv.to(x.dtype).contiguous(), sc, rc)
+        y = torch.empty_like(back)
+        y.index_copy_(0, order, back)
+        # 5. combine the k slots of each token
+        if T == 0:
+            return torch.empty(0, H, dtype=x.dtype, device=dev)
+        return self.combine_fn(y, T, k)
+
+    __call__ = forward

@@ -1,0 +1,157 @@
+"""Expert parallelism (blackhole_b200.ep) on CPU ranks over gloo, world size 2 and 3,
+with the C oracle standing in for each rank's local experts.
+
+The reference has no multi-GPU path (its plugin refuses expert parallelism), so
+the bar is the single-process layer: every slot is computed by its owner rank at
+top-1, rounded to the activation dtype and summed in fp32 at its source rank,
+which must reproduce the single-process per-slot computation bit for bit, and
+the oracle's moe_reference within the layer tolerance.
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+from helpers import np_tiers, rel_err, within
+
+E, H, I, K, BLOCK = 12, 256, 128, 4, 32
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _layer(seed=3):
+    from blackhole_b200 import hex_data as hd
+    return hd.synth_layer(E, H, I, "mixed", BLOCK, seed=seed)
+
+
+def _tokens(rank: int, T: int, zipf=None):
+    from blackhole_b200 import hex_data as hd
+    w, ids = hd.synth_routing(T, E, K, seed=100 + rank, zipf=zipf)
+    x = hd.synth_x(T, H, seed=200 + rank)
+    return x, w, ids
+
+
+def _per_slot_reference(x, w, ids, tiers_np):
+    """Every slot alone at top-1 (weighted, rounded to bf16), then fp32 sum: the
+    arithmetic the EP path performs, in one process."""
+    import hexoracle
+    T, k = ids.shape
+    layer = hexoracle.Layer(tiers_np, E, H, I, BLOCK)
+    xs = np.repeat(x.float().numpy(), k, axis=0)
+    y = layer.forward(xs, w.reshape(-1, 1).numpy(), ids.reshape(-1, 1).numpy())
+    y = hexoracle.round_bf16(y).reshape(T, k, H)
+    acc = y[:, 0].copy()
+    for j in range(1, k):           # slots added in order, as the layer's combine does
+        acc += y[:, j]
+    return acc
+
+
+def _worker(rank: int, world: int, port: int, T_of, zipf, out_q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import hexoracle
+
+        from blackhole_b200.ep import EPMoE, ExpertShard, shard_tiers
+        shard = ExpertShard(E, rank, world)
+        L = _layer()
+        local_np = np_tiers(shard_tiers(L.tiers, shard))
+        local = hexoracle.Layer(local_np, E, H, I, BLOCK) if local_np else None
+        lo, hi = shard.local_range
+
+        def expert_fn(xr, wr, ir):
+            assert int(ir.min()) >= lo and int(ir.max()) < hi, "slot routed to a rank that does not own it"
+            y = local.forward(xr.float().numpy(), wr.reshape(-1, 1).numpy(), ir.reshape(-1, 1).numpy())
+            return torch.from_numpy(hexoracle.round_bf16(y)).to(torch.bfloat16)
+
+        ep = EPMoE(shard, expert_fn=expert_fn)
+        x, w, ids = _tokens(rank, T_of[rank], zipf)
+        out = ep(x, w, ids)
+        out_q.put((rank, out.float().numpy()))
+    except BaseException as e:  # noqa: BLE001
+        out_q.put((rank, repr(e)))
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+def _run(world: int, T_of: list[int], zipf=None) -> dict:
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, T_of, zipf, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(world):
+        rank, val = q.get(timeout=240)
+        res[rank] = val
+    for p in procs:
+        p.join(timeout=60)
+    for r, v in res.items():
+        assert not isinstance(v, str), f"rank {r} failed: {v}"
+    return res
+
+
+@pytest.mark.parametrize("world,T_of,zipf", [
+    (2, [24, 17], None),
+    (3, [16, 0, 9], 1.2),          # a rank with no tokens; skewed routing
+])
+def test_ep_matches_single_process(oracle, world, T_of, zipf):
+    res = _run(world, T_of, zipf)
+    L = _layer()
+    full_np = np_tiers(L.tiers)
+    for r in range(world):
+        x, w, ids = _tokens(r, T_of[r], zipf)
+        got = res[r]
+        assert got.shape == (T_of[r], H)
+        if T_of[r] == 0:
+            continue
+        per_slot = hexoracle_round(_per_slot_reference(x, w, ids, full_np))
+        assert np.array_equal(got, per_slot), rel_err(got, per_slot)
+        want = oracle.moe_reference(x.float().numpy(), w.numpy(), ids.numpy(), full_np, E, BLOCK)
+        assert within(got, want), rel_err(got, want)
+
+
+def hexoracle_round(a):
+    import hexoracle
+    return hexoracle.round_bf16(a)
+
+
+def test_shard_tiers_partition_the_experts():
+    from blackhole_b200.ep import ExpertShard, shard_tiers
+    L = _layer()
+    for world in (1, 2, 3, 5):
+        seen = []
+        for r in range(world):
+            sh = ExpertShard(E, r, world)
+            lo, hi = sh.local_range
+            for t in shard_tiers(L.tiers, sh):
+                ex = t["experts"].tolist()
+                assert all(lo <= e < hi for e in ex)
+                full = next(ft for ft in L.tiers if ft["bits"] == t["bits"])
+                pos = [full["experts"].tolist().index(e) for e in ex]
+                for p in ("gate_proj", "up_proj", "down_proj"):
+                    for q in ("idx", "block_scale", "expert_scale", "levels"):
+                        assert torch.equal(t[p][q], full[p][q][pos])
+                seen += ex
+        assert sorted(seen) == list(range(E))
+
+
+def test_expert_shard_ownership():
+    from blackhole_b200.ep import ExpertShard
+    sh = ExpertShard(96, 3, 8)
+    assert sh.per_rank == 12 and sh.local_range == (36, 48)
+    assert sh.owner(torch.tensor([0, 11, 12, 95])).tolist() == [0, 0, 1, 7]
+    sh = ExpertShard(10, 3, 4)                 # uneven: 3, 3, 3, 1
+    assert sh.local_range == (9, 10)
