@@ -24,14 +24,15 @@
 //   last warp   (A operand from TMEM, B from 128-B swizzled smem) and
 //               tcgen05.commit: gate and up each, or (down) warp 1 alone
 //   warps 2-5   epilogue: tcgen05.ld of the accumulators, SwiGLU (gate/up) or
-//               the top-k weight (down), 16-bit stores
-//   warps 6..   decoders, groups of 8 taking 128-input sub-blocks in turn:
-//               once per tile, the level table scaled by every one
-//               of the 256 fp8 scale codes (one entry per thread, shared
-//               memory); per 32-input block one table load and prmt lookups of
-//               the packed codes, written to TMEM with tcgen05.st; a store is
-//               waited for (and its stage handed to the MMA) only after the
-//               next half-stage is decoded, so the TMEM write latency overlaps
+//               the top-k weight (down), 16-bit stores; one tile ahead, the
+//               code tables: the level table scaled by every one of the 256
+//               fp8 scale codes and rounded to the operand type (shared
+//               memory, two buffers)
+//   warps 6..   decoders, groups of 8 taking 128-input sub-blocks in turn: per
+//               32-input block one code-table load and prmt lookups of the
+//               packed codes into one of two 16-register buffers, written to
+//               TMEM with tcgen05.st while the other buffer's store drains; a
+//               half-stage goes to the MMA once both its stores are done
 // Every wait is bounded (ptx.cuh): a lost arrival ends the kernel with the
 // device error word set instead of hanging.
 #include <type_traits>
@@ -50,7 +51,7 @@ struct Ctrl {
   uint64_t s_full[2], s_empty[2];             // tile scale buffers
   uint64_t t_full[2], t_empty[2];             // accumulator buffers
   uint64_t i_full[kRecs], i_empty[kRecs];     // tile records
-  uint64_t tab_ready[2];                      // code tables built (per buffer)
+  uint64_t tab_ready[2], tab_empty[2];        // code tables built / released (per buffer)
   uint64_t drain[2];
   uint32_t tmem_base;
   int32_t abort;
@@ -147,7 +148,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
     for (int i = 0; i < 2; ++i) {
       mbar_init(&c->s_full[i], 1); mbar_init(&c->s_empty[i], kDecWarps);
       mbar_init(&c->t_full[i], p.n_iss); mbar_init(&c->t_empty[i], 4);
-      mbar_init(&c->tab_ready[i], kDecWarps);
+      mbar_init(&c->tab_ready[i], 4); mbar_init(&c->tab_empty[i], kDecWarps);
     }
     for (int i = 0; i < kRecs; ++i) { mbar_init(&c->i_full[i], 1); mbar_init(&c->i_empty[i], 7 + kDecWarps); }
     mbar_init(&c->drain[0], 1);
@@ -233,15 +234,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
       }
       ++s_issued;
       const int32_t wrow = ti.local * p.rows_pad + ti.m * 128;
-      for (int kb = 0; kb < ksteps; ++kb) {
-        if (kb % spi == 0) {
+      for (int kb = 0, st = 0; kb < ksteps; kb += spi, ++st) {
+        {
           if (!mbar_wait_idle(&c->x_empty[xs], xph ^ 1, abort_flag, p.dev_err)) { aborted = true; break; }
           if (lane == 0) {
             uint8_t* dst = xring + xs * p.sz_idx;
             mbar_arrive_expect_tx(&c->x_full[xs], idx_bytes);
             for (int j = 0; j < NPROJ; ++j)
               tma_load_2d_hint(dst + j * 128 * wst * 4, &p.tm_idx[ti.tier][j], &c->x_full[xs],
-                               (kb / spi) * static_cast<int>(wst), wrow, pol_stream);
+                               st * static_cast<int>(wst), wrow, pol_stream);
           }
           ++x_issued;
           if (++xs == static_cast<uint32_t>(p.di)) { xs = 0; xph ^= 1; }
@@ -349,8 +350,41 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
     const int q = warp & 3;
     const int row = q * 32 + lane;
     const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16);
-    int cur = 0, acc_it = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++cur) {
+    const int et = threadIdx.x - 64;         // 0..127: first code-table entry this thread builds
+    int cur = 0, acc_it = 0, built = 0;
+    bool aborted = false;
+    // Code tables of the tile whose record is `rc` (every thread of the 4 warps):
+    // entry (code e % 256) of projection e / 256 = levels x fp8(code) x expert scale,
+    // rounded to the operand type, as byte planes.  Built here, one tile ahead of
+    // the decoders, so the decoders only decode.
+    auto build_tables = [&](int rc) -> bool {
+      const int rr = rc % kRecs;
+      if (!mbar_wait_idle(&c->i_full[rr], (rc / kRecs) & 1, abort_flag, p.dev_err)) return false;
+      const TileRec& rec = recs[rr];
+      if (!rec.ok) return true;
+      const int tb = built & 1;
+      if (!mbar_wait_idle(&c->tab_empty[tb], ((built >> 1) & 1) ^ 1, abort_flag, p.dev_err)) return false;
+      for (int e = et; e < 256 * NPROJ; e += 128) {
+        const int j = e >> 8, code = e & 255;
+        const float s = __fmul_rn(lut[code], rec.es[j]);
+        uint4* tj = tabs + (tb * NPROJ + j) * 512;
+        if (rec.bits == 3) {
+          const Table8 t8 = make_table8<BF16>(rec.lev[j], s);
+          tj[code] = make_uint4(t8.l0, t8.l1, t8.h0, t8.h1);
+        } else {
+          const Table16 t16 = make_table16<BF16>(rec.lev[j], s);
+          tj[code] = make_uint4(t16.la0, t16.la1, t16.lb0, t16.lb1);
+          tj[256 + code] = make_uint4(t16.ha0, t16.ha1, t16.hb0, t16.hb1);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&c->tab_ready[tb]);
+      ++built;
+      return true;
+    };
+    if (static_cast<int>(blockIdx.x) < num_tiles) aborted = !build_tables(0);
+    for (int t = blockIdx.x; t < num_tiles && !aborted; t += gridDim.x, ++cur) {
+      if (t + static_cast<int>(gridDim.x) < num_tiles && !build_tables(cur + 1)) break;
       const int ri = cur % kRecs;
       if (!mbar_wait_idle(&c->i_full[ri], (cur / kRecs) & 1, abort_flag, p.dev_err)) break;
       const int ok = recs[ri].ok, cnt = recs[ri].cnt, b = recs[ri].b, m = recs[ri].m;
@@ -431,7 +465,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
     const int row = q * 32 + lane;
     const int role = (d & 7) >> 2;           // gate/up: projection; down: which half of a sub-block
     const int proj = GLU ? role : 0;
-    const int dt = threadIdx.x - 192;        // first code-table entry this thread builds
     const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16);
     uint32_t xs = 0, xph = 0, as = 0, aph = 0;
     bool aborted = false;
@@ -443,29 +476,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
     for (int t = blockIdx.x; t < num_tiles && !aborted; t += gridDim.x, ++cur) {
       const int ri = cur % kRecs;
       if (!mbar_wait(&c->i_full[ri], (cur / kRecs) & 1, abort_flag, p.dev_err)) { aborted = true; break; }
-      const TileRec& rec = recs[ri];
-      const int ok = rec.ok, bits = rec.bits;
+      const int ok = recs[ri].ok, bits = recs[ri].bits;
       const int tb = work & 1;
-      if (ok) {
-        for (int e = dt; e < 256 * NPROJ; e += kDecWarps * 32) {
-          // entry (code e % 256) of projection e / 256's code table
-          const int j = e >> 8, code = e & 255;
-          const float s = __fmul_rn(lut[code], rec.es[j]);
-          uint4* tj = tabs + (tb * NPROJ + j) * 512;
-          if (bits == 3) {
-            const Table8 t8 = make_table8<BF16>(rec.lev[j], s);
-            tj[code] = make_uint4(t8.l0, t8.l1, t8.h0, t8.h1);
-          } else {
-            const Table16 t16 = make_table16<BF16>(rec.lev[j], s);
-            tj[code] = make_uint4(t16.la0, t16.la1, t16.lb0, t16.lb1);
-            tj[256 + code] = make_uint4(t16.ha0, t16.ha1, t16.hb0, t16.hb1);
-          }
-        }
-      }
       __syncwarp();
       if (lane == 0) mbar_arrive(&c->i_empty[ri]);
       if (!ok) continue;
-      if (lane == 0) mbar_arrive(&c->tab_ready[tb]);
       if (!mbar_wait(&c->tab_ready[tb], (work >> 1) & 1, abort_flag, p.dev_err)) { aborted = true; break; }
       const int sb = work & 1;
       if (!mbar_wait(&c->s_full[sb], (work >> 1) & 1, abort_flag, p.dev_err)) { aborted = true; break; }
@@ -476,9 +491,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
       auto kb_loop = [&](auto bits_c) {
         constexpr int BITS = decltype(bits_c)::value;
         const uint32_t wst = static_cast<uint32_t>(p.k_idx / 32 * BITS);
+        int sub = -1, grp = kDecGroups - 1;     // position in the index stage / in the group rotation
         for (int kb = 0; kb < ksteps && !aborted; ++kb) {
-          const int sub = kb % spi;
-          const bool mine_k = (kb % kDecGroups) == group;
+          if (++sub == spi) sub = 0;
+          if (++grp == kDecGroups) grp = 0;
+          const bool mine_k = grp == group;
           if (sub == 0) {
             if (!mbar_wait(&c->x_full[xs], xph, abort_flag, p.dev_err)) { aborted = true; break; }
           }
@@ -512,7 +529,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
           uint32_t sc;   // scale codes of the 4 blocks of this 128-input step, one byte each
           if (p.block == 32) sc = *reinterpret_cast<const uint32_t*>(srow + kb * 4);
           else sc = static_cast<uint32_t>(srow[kb]) * 0x01010101u;
-  #pragma unroll
+#pragma unroll
           for (int h = 0; h < 2; ++h) {
             const bool mine = GLU || role == h;
             if (mine) {
@@ -555,7 +572,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
         pending = -1;
       }
       __syncwarp();
-      if (!aborted && lane == 0) mbar_arrive(&c->s_empty[sb]);
+      if (!aborted && lane == 0) {
+        mbar_arrive(&c->tab_empty[tb]);
+        mbar_arrive(&c->s_empty[sb]);
+      }
     }
     if (pending >= 0) tmem_st_wait();
   }
