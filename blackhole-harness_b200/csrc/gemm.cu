@@ -492,7 +492,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
         constexpr int BITS = decltype(bits_c)::value;
         const uint32_t wst = static_cast<uint32_t>(p.k_idx / 32 * BITS);
         int sub = -1, grp = kDecGroups - 1;     // position in the index stage / in the group rotation
+        // scale codes of the 4 blocks of a 128-input step, one byte each, loaded one step ahead
+        auto load_sc = [&](int k) -> uint32_t {
+          return p.block == 32 ? *reinterpret_cast<const uint32_t*>(srow + k * 4)
+                               : static_cast<uint32_t>(srow[k]) * 0x01010101u;
+        };
+        uint32_t sc_next = load_sc(0);
         for (int kb = 0; kb < ksteps && !aborted; ++kb) {
+          const uint32_t sc = sc_next;
+          if (kb + 1 < ksteps) sc_next = load_sc(kb + 1);
           if (++sub == spi) sub = 0;
           if (++grp == kDecGroups) grp = 0;
           const bool mine_k = grp == group;
@@ -526,9 +534,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
             if (as >= static_cast<uint32_t>(p.da)) { as -= p.da; aph ^= 1; }
             continue;
           }
-          uint32_t sc;   // scale codes of the 4 blocks of this 128-input step, one byte each
-          if (p.block == 32) sc = *reinterpret_cast<const uint32_t*>(srow + kb * 4);
-          else sc = static_cast<uint32_t>(srow[kb]) * 0x01010101u;
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             const bool mine = GLU || role == h;
