@@ -146,7 +146,7 @@ int plan_gemm(GemmParams& p, bool glu, int bm, int k_pad, int block, int max_bit
   // tensor pipe takes to run it.
   p.n_iss = glu ? 2 : 1;
   p.acc_stride = static_cast<uint32_t>(nproj * bm);
-  p.a_stride = static_cast<uint32_t>(32 * nproj);
+  p.a_stride = static_cast<uint32_t>(64 * nproj);   // one 128-input step per operand stage
   p.nbuf = (2 * p.acc_stride + 2 * p.a_stride <= kTmemCols) ? 2 : 1;
   p.a_base = p.nbuf * p.acc_stride;
   p.da = static_cast<int>(std::min<uint32_t>(kMaxDA, (kTmemCols - p.a_base) / p.a_stride));

@@ -144,7 +144,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
   if (threadIdx.x == 0) {
     for (int i = 0; i < kMaxDI; ++i) { mbar_init(&c->x_full[i], 1); mbar_init(&c->x_empty[i], kDecWarps); }
     for (int i = 0; i < kMaxDB; ++i) { mbar_init(&c->b_full[i], 1); mbar_init(&c->b_empty[i], p.n_iss); }
-    for (int i = 0; i < kMaxDA; ++i) { mbar_init(&c->a_full[i], GLU ? 8 : 4); mbar_init(&c->a_empty[i], p.n_iss); }
+    for (int i = 0; i < kMaxDA; ++i) { mbar_init(&c->a_full[i], 8); mbar_init(&c->a_empty[i], p.n_iss); }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&c->s_full[i], 1); mbar_init(&c->s_empty[i], kDecWarps);
       mbar_init(&c->t_full[i], p.n_iss); mbar_init(&c->t_empty[i], 4);
@@ -319,19 +319,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
       for (int ks = 0; ks < ksteps && !aborted; ++ks) {
         if (!mbar_wait(&c->b_full[bs], bph, abort_flag, p.dev_err)) { aborted = true; break; }
         const uint64_t bdesc = sw128_desc(smem_u32(bring + bs * p.sz_b));
-        for (int h = 0; h < 2; ++h) {
-          if (!mbar_wait(&c->a_full[as], aph, abort_flag, p.dev_err)) { aborted = true; break; }
-          tc_fence_after();
-          if (lane == 0) {
-            const uint32_t a0 = tmem + p.a_base + as * p.a_stride + mi * 32;
+        if (!mbar_wait(&c->a_full[as], aph, abort_flag, p.dev_err)) { aborted = true; break; }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t a0 = tmem + p.a_base + as * p.a_stride + mi * 64;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
             const uint64_t bh = bdesc + h * h_step;
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) umma_f16_ts(d, a0 + kk * 8, bh + kk * 2, idesc, (ks | h | kk) != 0);
-            umma_commit(&c->a_empty[as]);
+            for (int kk = 0; kk < 4; ++kk)
+              umma_f16_ts(d, a0 + h * 32 + kk * 8, bh + kk * 2, idesc, (ks | h | kk) != 0);
           }
-          __syncwarp();
-          if (++as == static_cast<uint32_t>(p.da)) { as = 0; aph ^= 1; }
+          umma_commit(&c->a_empty[as]);
         }
+        __syncwarp();
+        if (++as == static_cast<uint32_t>(p.da)) { as = 0; aph ^= 1; }
         if (aborted) break;
         if (lane == 0) umma_commit(&c->b_empty[bs]);
         __syncwarp();
@@ -529,11 +531,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
             if (++xs == static_cast<uint32_t>(p.di)) { xs = 0; xph ^= 1; }
           }
           if (!mine_k) {
-            // another group's two half-stages
-            as += 2;
+            // another group's operand stage
+            as += 1;
             if (as >= static_cast<uint32_t>(p.da)) { as -= p.da; aph ^= 1; }
             continue;
           }
+          bool have_stage = false;
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             const bool mine = GLU || role == h;
@@ -541,29 +544,32 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
               // the two 32-input blocks of this half go through alternating
               // 16-register buffers: a block is decoded while the other buffer's
               // store is in flight, and each wait names the buffer it frees
-              const uint32_t acol = tl + p.a_base + as * p.a_stride + proj * 32;
+              const uint32_t acol = tl + p.a_base + as * p.a_stride + proj * 64 + h * 32;
               if (h == 0) decode_block<0>(w, BITS, tab, sc & 255u, ba);
               else decode_block<2>(w, BITS, tab, (sc >> 16) & 255u, ba);
               tmem_st_wait_keep(bb);
-              if (pending >= 0) {
-                // the previous half-stage's stores are done: hand it to the MMA
-                // (before waiting for a free stage, which may be that one's successor in the ring)
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&c->a_full[pending]);
-                pending = -1;
+              if (!have_stage) {
+                if (pending >= 0) {
+                  // the previous step's stores are done: hand its stage to the MMA
+                  // (before waiting for a free stage, which may be that one's successor in the ring)
+                  tc_fence_before();
+                  __syncwarp();
+                  if (lane == 0) mbar_arrive(&c->a_full[pending]);
+                  pending = -1;
+                }
+                if (!mbar_wait(&c->a_empty[as], aph ^ 1, abort_flag, p.dev_err)) { aborted = true; break; }
+                tc_fence_after();
+                have_stage = true;
               }
-              if (!mbar_wait(&c->a_empty[as], aph ^ 1, abort_flag, p.dev_err)) { aborted = true; break; }
-              tc_fence_after();
               tmem_st16(acol, ba);
               if (h == 0) decode_block<1>(w, BITS, tab, (sc >> 8) & 255u, bb);
               else decode_block<3>(w, BITS, tab, sc >> 24, bb);
               tmem_st_wait_keep(ba);
               tmem_st16(acol + 16, bb);
-              pending = static_cast<int>(as);
             }
-            if (++as == static_cast<uint32_t>(p.da)) { as = 0; aph ^= 1; }
           }
+          pending = static_cast<int>(as);
+          if (++as == static_cast<uint32_t>(p.da)) { as = 0; aph ^= 1; }
         }
       };
       if (bits == 3) kb_loop(std::integral_constant<int, 3>{});
