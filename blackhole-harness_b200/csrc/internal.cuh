@@ -12,7 +12,7 @@ namespace hexmoe {
 constexpr int kMaxTiers = HEXMOE_MAX_TIERS;
 constexpr int kTileM = 128;      // weight rows per tile (UMMA M)
 constexpr int kKStep = 128;      // reduction elements per activation (B operand) stage
-constexpr int kMaxDI = 4;        // deepest index-word ring
+constexpr int kMaxDI = 8;        // deepest index-word ring
 constexpr int kMaxDB = 8;        // deepest activation ring
 constexpr int kMaxDA = 8;        // deepest TMEM operand ring
 #ifndef HEXMOE_DEC_GROUPS
