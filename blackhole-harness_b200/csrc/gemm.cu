@@ -390,20 +390,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
       const int ri = cur % kRecs;
       if (!mbar_wait_idle(&c->i_full[ri], (cur / kRecs) & 1, abort_flag, p.dev_err)) break;
       const int ok = recs[ri].ok, cnt = recs[ri].cnt, b = recs[ri].b, m = recs[ri].m;
-      // down: this warp's copy of the block's slot ids / weights (lane j holds rows j, j+32, ...)
-      int my_slot[4];
-      float my_w[4];
-      if (!GLU) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int r = lane + 32 * j;
-          my_slot[j] = r < cnt ? recs[ri].slot[r] : 0;
-          my_w[j] = r < cnt ? recs[ri].w[r] : 0.0f;
-        }
-      }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&c->i_empty[ri]);
       if (!ok) {
+        if (lane == 0) mbar_arrive(&c->i_empty[ri]);
         if (warp == 2 && lane == 0) atomicOr(p.dev_err, kDevErrNoTier);
         continue;
       }
@@ -411,53 +400,50 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
       if (!mbar_wait_idle(&c->t_full[ab], (acc_it / p.nbuf) & 1, abort_flag, p.dev_err)) break;
       ++acc_it;
       tc_fence_after();
-      const int o = m * 128 + row;
-      const bool store_row = o < p.rows_store;
+      // Lanes pair up on adjacent outputs (o, o + 1): one shuffle per two values,
+      // then each lane stores one packed pair, the even lane for token n and the
+      // odd lane for token n + 1.  Down reads the block's slot ids and top-k
+      // weights from the tile record (the same address for the whole warp).
+      const bool odd = lane & 1;
+      const int o_pair = m * 128 + row - (odd ? 1 : 0);
+      const bool store_pair = o_pair < p.rows_store;          // rows_store is even
+      uint16_t* out16 = reinterpret_cast<uint16_t*>(p.out);
       const uint32_t d0 = tl + ab * p.acc_stride;
       for (int n0 = 0; n0 < cnt; n0 += 16) {
         uint32_t g[16], u[16];
         tmem_ld16(d0 + n0, g);
         if (GLU) tmem_ld16(d0 + p.bm + n0, u);
         tmem_ld_wait();
-        if (GLU) {
-          __nv_bfloat16* out_b = reinterpret_cast<__nv_bfloat16*>(p.out);
-          __half* out_h = reinterpret_cast<__half*>(p.out);
+        if (n0 + 16 >= cnt) {
+          // every accumulator column of the tile is in registers: free the buffer now
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&c->t_empty[ab]);
+        }
+        float v[16];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int n = n0 + j;
-            if (n < cnt && store_row) {
-              const float gv = __uint_as_float(g[j]);
-              const float uv = __uint_as_float(u[j]);
-              const float hg = 0.5f * gv;                      // silu(g) = g/2 * (1 + tanh(g/2))
-              const float a = fmaf(hg, tanh_approx(hg), hg) * uv;
-              const size_t off = (static_cast<size_t>(b) * p.bm + n) * p.ld_out + o;
-              if (BF16) out_b[off] = __float2bfloat16_rn(a);
-              else out_h[off] = __float2half_rn(a);
-            }
+        for (int j = 0; j < 16; ++j) {
+          if (GLU) {
+            const float hg = 0.5f * __uint_as_float(g[j]);     // silu(g) = g/2 * (1 + tanh(g/2))
+            v[j] = fmaf(hg, tanh_approx(hg), hg) * __uint_as_float(u[j]);
+          } else {
+            v[j] = __uint_as_float(g[j]) * recs[ri].w[n0 + j];
           }
-        } else {
-          __nv_bfloat16* out_b = reinterpret_cast<__nv_bfloat16*>(p.out);
-          __half* out_h = reinterpret_cast<__half*>(p.out);
+        }
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int n = n0 + j;
-            const int src = n & 31, grp = n >> 5;             // row n of the block lives in lane n % 32
-            const int slot = __shfl_sync(0xffffffffu, grp == 0 ? my_slot[0] : grp == 1 ? my_slot[1]
-                                                      : grp == 2 ? my_slot[2] : my_slot[3], src);
-            const float wt = __shfl_sync(0xffffffffu, grp == 0 ? my_w[0] : grp == 1 ? my_w[1]
-                                                      : grp == 2 ? my_w[2] : my_w[3], src);
-            if (n < cnt && store_row) {
-              const float v = __uint_as_float(g[j]) * wt;
-              const size_t off = static_cast<size_t>(slot) * p.ld_out + o;
-              if (BF16) out_b[off] = __float2bfloat16_rn(v);
-              else out_h[off] = __float2half_rn(v);
-            }
+        for (int j = 0; j < 16; j += 2) {
+          const float keep = odd ? v[j + 1] : v[j];
+          const float other = __shfl_xor_sync(0xffffffffu, odd ? v[j] : v[j + 1], 1);
+          const int n = n0 + j + (odd ? 1 : 0);
+          if (n < cnt && store_pair) {
+            const size_t orow = GLU ? static_cast<size_t>(b) * p.bm + n : static_cast<size_t>(recs[ri].slot[n]);
+            *reinterpret_cast<uint32_t*>(out16 + orow * p.ld_out + o_pair) =
+                odd ? pack2<BF16>(other, keep) : pack2<BF16>(keep, other);
           }
         }
       }
-      tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&c->t_empty[ab]);
+      if (lane == 0) mbar_arrive(&c->i_empty[ri]);
     }
   } else {
     // ------------------------------------------------------------ decoders
