@@ -357,8 +357,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
     bool aborted = false;
     // Code tables of the tile whose record is `rc` (every thread of the 4 warps):
     // entry (code e % 256) of projection e / 256 = levels x fp8(code) x expert scale,
-    // rounded to the operand type, as byte planes.  Built here, one tile ahead of
-    // the decoders, so the decoders only decode.
+    // rounded to the operand type, as byte planes.  Built here, ahead of the
+    // decoders, so the decoders only decode: two tiles ahead with two accumulator
+    // buffers, one with a single buffer (there the index producer reaches record
+    // n+2 only after tile n's epilogue has freed the accumulator, so waiting for
+    // that record before tile n's epilogue would never end).
     auto build_tables = [&](int rc) -> bool {
       const int rr = rc % kRecs;
       if (!mbar_wait_idle(&c->i_full[rr], (rc / kRecs) & 1, abort_flag, p.dev_err)) return false;
@@ -384,9 +387,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
       ++built;
       return true;
     };
-    if (static_cast<int>(blockIdx.x) < num_tiles) aborted = !build_tables(0);
+    const int ahead = p.nbuf >= 2 ? 2 : 1;
+    for (int k = 0; k < ahead && !aborted; ++k)
+      if (static_cast<int>(blockIdx.x + k * gridDim.x) < num_tiles) aborted = !build_tables(k);
     for (int t = blockIdx.x; t < num_tiles && !aborted; t += gridDim.x, ++cur) {
-      if (t + static_cast<int>(gridDim.x) < num_tiles && !build_tables(cur + 1)) break;
+      if (t + ahead * static_cast<int>(gridDim.x) < num_tiles && !build_tables(cur + ahead)) break;
       const int ri = cur % kRecs;
       if (!mbar_wait_idle(&c->i_full[ri], (cur / kRecs) & 1, abort_flag, p.dev_err)) break;
       const int ok = recs[ri].ok, cnt = recs[ri].cnt, b = recs[ri].b, m = recs[ri].m;
