@@ -23,6 +23,7 @@ EXPORTS = (
     "hexmoe_layer_create", "hexmoe_layer_destroy", "hexmoe_forward_workspace_bytes", "hexmoe_forward",
     "hexmoe_align_workspace_bytes", "hexmoe_align", "hexmoe_dequant", "hexmoe_route_topk",
     "hexmoe_gather", "hexmoe_gate_up", "hexmoe_down", "hexmoe_combine", "hexmoe_forward_noalloc",
+    "hexmoe_tile_index",
 )
 
 
@@ -63,6 +64,7 @@ def _load() -> ctypes.CDLL:
         "hexmoe_dequant": (ctypes.c_int, [P, I32_, I32_, I32_, I32_, I32_, I32_, I32_, P, P, I32_, I64_, I64_, I64_,
                                           P]),
         "hexmoe_route_topk": (ctypes.c_int, [P, I32_, I64_, I32_, I32_, I32_, P, P, P]),
+        "hexmoe_tile_index": (ctypes.c_int, [P, I32_, I32_, I32_, I32_, P, P]),
         "hexmoe_gather": (ctypes.c_int, [P, I32_, I64_, I32_, I32_, I32_, P, P, I32_, P, P]),
         "hexmoe_gate_up": (ctypes.c_int, [P, P, I32_, I64_, I32_, P, P, P, I32_, P, P]),
         "hexmoe_down": (ctypes.c_int, [P, P, I32_, I64_, I32_, P, P, P, P, I32_, P, P]),

@@ -163,6 +163,9 @@ class _Layer:
             ct.down = _parts_struct(t.kernel_parts["down_proj"])
             self.keep.append(t)
         self.desc = d
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("the first hex_moe call on a set of tiers builds the layer (a synchronous tiled copy "
+                               "of the index streams); make it before CUDA graph capture")
         with torch.cuda.device(dev):
             self.expert_map = torch.empty(self.E, dtype=torch.int32, device=dev)
             _lib.check(_lib.lib.hexmoe_build_expert_map(ctypes.byref(d), _ptr(self.expert_map), _stream(dev)),

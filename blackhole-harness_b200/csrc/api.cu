@@ -16,10 +16,10 @@ struct hexmoe_layer {
   hexmoe_layer_desc desc;
   int device;
   int num_sms;
-  int max_bits;
-  // idx tensor maps per tier (gate, up, down) and index-stage width
-  // (k_idx = 128, 256, 384, 512 -> slot 0..3; unused where k_idx does not divide)
-  CUtensorMap tm_idx[kMaxTiers][3][4];
+  // tiled copies of the idx stacks (hexmoe_tile_index layout) per tier (gate,
+  // up, down), carved from one allocation owned by the layer
+  void* tiled_mem;
+  const uint8_t* idx_t[kMaxTiers][3];
 };
 
 namespace {
@@ -110,10 +110,10 @@ int check_dtype16(int32_t dt, const char* what) {
 }
 
 // Shared-memory and TMEM carve-up of one GEMM launch (see GemmParams).  The
-// index ring takes the widest stage (k_idx of 512, 384, 256 or 128 inputs)
-// that divides k_pad and still leaves an activation ring of useful depth:
-// TMA moves one box row per few cycles, so wide rows are what feed HBM rate.
-int plan_gemm(GemmParams& p, bool glu, int bm, int k_pad, int block, int max_bits) {
+// index ring takes the widest stage (k_idx of 512, 384, 256 or 128 inputs;
+// k_idx/128 tiled steps of 8 KB per projection) that divides k_pad and still
+// leaves an activation ring of useful depth.
+int plan_gemm(GemmParams& p, bool glu, int bm, int k_pad, int block) {
   const int nproj = glu ? 2 : 1;
   const uint32_t spr = static_cast<uint32_t>(k_pad / block);
   p.sz_scale = static_cast<uint32_t>(align_up(128u * spr, 1024));
@@ -124,12 +124,12 @@ int plan_gemm(GemmParams& p, bool glu, int bm, int k_pad, int block, int max_bit
   const int64_t budget = 232448 - 1024 - p.off_idx;
   const int db_min = bm >= 64 ? 3 : 4;
   p.di = 0;
-  // gate/up prefers 128-input stages (3-bit rows of 48 B: the decoders' 16-byte
-  // word loads are free of bank conflicts; measured faster); down, the widest
+  // gate/up prefers 128-input stages (a deeper ring in the same space; measured
+  // faster); down, the widest
   const int order[2][4] = {{512, 384, 256, 128}, {128, 512, 384, 256}};
   for (int k_idx : order[glu ? 1 : 0]) {
     if (k_pad % k_idx) continue;
-    const uint32_t sz = static_cast<uint32_t>(align_up(static_cast<size_t>(nproj) * 128 * k_idx * max_bits / 8, 1024));
+    const uint32_t sz = static_cast<uint32_t>(nproj * (k_idx / 128)) * kStepBytes;
     for (int di = kMaxDI; di >= 2; --di) {
       const int64_t rem = budget - static_cast<int64_t>(di) * sz;
       if (rem <= 0) continue;
@@ -195,10 +195,10 @@ int run_gate_up(const hexmoe_layer* layer, const void* xs, bool bf16, int64_t to
   p.out = act; p.ld_out = d.inter_pad;
   p.topk_w = nullptr;
   p.dev_err = dev_err;
-  if (int rc = plan_gemm(p, true, bm, d.hidden_pad, d.block, layer->max_bits)) return rc;
+  if (int rc = plan_gemm(p, true, bm, d.hidden_pad, d.block)) return rc;
   for (int t = 0; t < d.num_tiers; ++t) {
-    p.tm_idx[t][0] = layer->tm_idx[t][0][p.k_idx / 128 - 1];
-    p.tm_idx[t][1] = layer->tm_idx[t][1][p.k_idx / 128 - 1];
+    p.idx_t[t][0] = layer->idx_t[t][0];
+    p.idx_t[t][1] = layer->idx_t[t][1];
   }
   if (int rc = make_tmap(&p.tm_b, xs, dt16, 2, d.hidden, static_cast<uint64_t>(max_blocks) * bm, 2ull * d.hidden, 64,
                          static_cast<uint32_t>(bm), CU_TENSOR_MAP_SWIZZLE_128B, "x_sorted tensor map"))
@@ -235,8 +235,8 @@ int run_down(const hexmoe_layer* layer, const void* act, bool bf16, int64_t toke
   q.out = y; q.ld_out = d.hidden;
   q.topk_w = topk_weights;
   q.dev_err = dev_err;
-  if (int rc = plan_gemm(q, false, bm, d.inter_pad, d.block, layer->max_bits)) return rc;
-  for (int t = 0; t < d.num_tiers; ++t) q.tm_idx[t][0] = layer->tm_idx[t][2][q.k_idx / 128 - 1];
+  if (int rc = plan_gemm(q, false, bm, d.inter_pad, d.block)) return rc;
+  for (int t = 0; t < d.num_tiers; ++t) q.idx_t[t][0] = layer->idx_t[t][2];
   if (int rc = make_tmap(&q.tm_b, act, dt16, 2, d.inter_pad, static_cast<uint64_t>(max_blocks) * bm,
                          2ull * d.inter_pad, 64, static_cast<uint32_t>(bm), CU_TENSOR_MAP_SWIZZLE_128B, "act tensor map"))
     return rc;
@@ -311,46 +311,69 @@ int hexmoe_layer_create(const hexmoe_layer_desc* desc, hexmoe_layer** out) {
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (major != 10 || minor != 0)
     return fail(HEXMOE_E_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a", dev, major, minor);
+  size_t tiled_bytes = 0;
+  size_t tiled_off[kMaxTiers][3];
+  for (int t = 0; t < d.num_tiers; ++t) {
+    const hexmoe_tier& tr = d.tiers[t];
+    if (tr.bits != 3 && tr.bits != 4) return fail(HEXMOE_E_ARG, "tier %d: bits %d is not 3 or 4", t, tr.bits);
+    if (tr.n <= 0 || tr.n > 65535) return fail(HEXMOE_E_ARG, "tier %d: %d experts", t, tr.n);
+    const hexmoe_parts* parts[3] = {&tr.gate, &tr.up, &tr.down};
+    for (int j = 0; j < 3; ++j) {
+      const hexmoe_parts& pp = *parts[j];
+      if (!pp.idx || !pp.block_scale || !pp.expert_scale || !pp.levels)
+        return fail(HEXMOE_E_ARG, "tier %d projection %d: null part", t, j);
+      if (reinterpret_cast<uintptr_t>(pp.block_scale) % 16)
+        return fail(HEXMOE_E_ARG, "tier %d projection %d: block_scale not 16-byte aligned", t, j);
+      const int rows = j < 2 ? d.inter_pad : d.hidden_pad;
+      const int cols = j < 2 ? d.hidden_pad : d.inter_pad;
+      tiled_off[t][j] = tiled_bytes;
+      tiled_bytes += align_up(static_cast<size_t>(tr.n) * rows * cols / 2, 256);
+    }
+  }
+  if (!device_error_word()) return fail(HEXMOE_E_CUDA, "device error word unavailable");
+  // The tiled copies: every earlier write to the stacks (on any stream) must
+  // have landed, so wait for the device, then tile on a private stream.
+  e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "hexmoe_layer_create: device synchronize");
+  void* mem = nullptr;
+  e = cudaMalloc(&mem, tiled_bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "hexmoe_layer_create: tiled index allocation");
+  cudaStream_t st = nullptr;
+  e = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking);
+  if (e != cudaSuccess) { cudaFree(mem); return cuda_fail(e, "hexmoe_layer_create: stream"); }
   auto* L = new hexmoe_layer();
   L->desc = d;
   L->device = dev;
   L->num_sms = sms;
-  L->max_bits = 3;
-  for (int t = 0; t < d.num_tiers; ++t) {
+  L->tiled_mem = mem;
+  for (int t = 0; t < d.num_tiers && e == cudaSuccess; ++t) {
     const hexmoe_tier& tr = d.tiers[t];
-    if (tr.bits != 3 && tr.bits != 4) { delete L; return fail(HEXMOE_E_ARG, "tier %d: bits %d is not 3 or 4", t, tr.bits); }
-    if (tr.n <= 0 || tr.n > 65535) { delete L; return fail(HEXMOE_E_ARG, "tier %d: %d experts", t, tr.n); }
-    L->max_bits = std::max(L->max_bits, static_cast<int>(tr.bits));
     const hexmoe_parts* parts[3] = {&tr.gate, &tr.up, &tr.down};
-    for (int j = 0; j < 3; ++j) {
-      const hexmoe_parts& pp = *parts[j];
-      if (!pp.idx || !pp.block_scale || !pp.expert_scale || !pp.levels) {
-        delete L;
-        return fail(HEXMOE_E_ARG, "tier %d projection %d: null part", t, j);
-      }
-      if (reinterpret_cast<uintptr_t>(pp.block_scale) % 16) {
-        delete L;
-        return fail(HEXMOE_E_ARG, "tier %d projection %d: block_scale not 16-byte aligned", t, j);
-      }
+    for (int j = 0; j < 3 && e == cudaSuccess; ++j) {
       const int rows = j < 2 ? d.inter_pad : d.hidden_pad;
       const int cols = j < 2 ? d.hidden_pad : d.inter_pad;
-      const uint64_t wpr = static_cast<uint64_t>(cols) / 32 * tr.bits;
-      for (int ki = 0; ki < 4; ++ki) {
-        const int k_idx = 128 * (ki + 1);
-        if (cols % k_idx) continue;
-        int rc = make_tmap(&L->tm_idx[t][j][ki], pp.idx, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, wpr,
-                           static_cast<uint64_t>(tr.n) * rows, wpr * 4, static_cast<uint32_t>(k_idx / 32 * tr.bits), 128,
-                           CU_TENSOR_MAP_SWIZZLE_NONE, "idx tensor map");
-        if (rc != HEXMOE_OK) { delete L; return rc; }
-      }
+      uint8_t* dst = static_cast<uint8_t*>(mem) + tiled_off[t][j];
+      L->idx_t[t][j] = dst;
+      e = launch_tile_index(parts[j]->idx, tr.bits, tr.n, rows, cols, reinterpret_cast<uint32_t*>(dst), st);
     }
   }
-  if (!device_error_word()) { delete L; return fail(HEXMOE_E_CUDA, "device error word unavailable"); }
+  const cudaError_t es = cudaStreamSynchronize(st);
+  if (e == cudaSuccess) e = es;
+  cudaStreamDestroy(st);
+  if (e != cudaSuccess) {
+    hexmoe_layer_destroy(L);
+    return cuda_fail(e, "hexmoe_layer_create: tiling the index streams");
+  }
   *out = L;
   return HEXMOE_OK;
 }
 
 int hexmoe_layer_destroy(hexmoe_layer* layer) {
+  if (!layer) return HEXMOE_OK;
+  if (layer->tiled_mem) {
+    DeviceGuard g(layer->device);
+    cudaFree(layer->tiled_mem);
+  }
   delete layer;
   return HEXMOE_OK;
 }
@@ -504,6 +527,19 @@ int hexmoe_dequant(const hexmoe_parts* parts, int32_t bits, int32_t block, int32
   cudaError_t e = launch_dequant(*parts, bits, block, n, rows, cols, rows_pad, cols_pad, experts, out, out_dtype,
                                  stride_e, stride_row, row_off, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "dequant launch");
+  return HEXMOE_OK;
+}
+
+int hexmoe_tile_index(const uint32_t* idx, int32_t bits, int32_t n, int32_t rows_pad, int32_t cols_pad, uint32_t* out,
+                      void* stream) {
+  if (bits != 3 && bits != 4) return fail(HEXMOE_E_ARG, "bits %d is not 3 or 4", bits);
+  if (n < 0 || rows_pad < 0 || cols_pad < 0 || rows_pad % 128 || cols_pad % 128)
+    return fail(HEXMOE_E_ARG, "hexmoe_tile_index: n=%d rows_pad=%d cols_pad=%d (multiples of 128 expected)", n,
+                rows_pad, cols_pad);
+  if (static_cast<int64_t>(n) * rows_pad * cols_pad == 0) return HEXMOE_OK;
+  if (!idx || !out) return fail(HEXMOE_E_ARG, "hexmoe_tile_index: null pointer");
+  cudaError_t e = launch_tile_index(idx, bits, n, rows_pad, cols_pad, out, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "tile_index launch");
   return HEXMOE_OK;
 }
 

@@ -9,10 +9,11 @@
 // bytes of the 8 or 16 entries), so one `prmt` looks up one byte of four weights
 // at once; two more `prmt` interleave the planes into packed operand pairs.
 //
-// 3-bit codes (8 levels) are first spread from 3-bit to 4-bit fields (prmt
-// selectors are nibbles): three shift + lop3 steps and a mask for 8 codes.
-// 4-bit codes (16 levels) already sit in nibbles; bit 3 of each code selects
-// between the two 8-entry halves through a sign-replicating prmt mask.
+// The codes arrive one per nibble (the layer's tiled copy of the index
+// stream, hexmoe_tile_index), which is what prmt selectors are: a 3-bit code
+// (8 levels, bit 3 of its nibble clear) selects its table byte directly; for
+// a 4-bit code (16 levels) bit 3 selects between the two 8-entry halves
+// through a sign-replicating prmt mask.
 #pragma once
 
 #include "ptx.cuh"
@@ -75,16 +76,6 @@ __device__ __forceinline__ Table16 make_table16(const float* lev, float s) {
   return t;
 }
 
-// 8 codes of 3 bits at bits 0..23 of g (higher bits ignored) -> nibble j = code j.
-// The left shifts are written as multiplies so they can issue on the FMA pipe;
-// the merges and the mask are single lop3s on the integer pipe.
-__device__ __forceinline__ uint32_t spread3(uint32_t g) {
-  uint32_t x = lop3_sel(g, g * 16u, 0x0000FFFFu);   // codes 4-7 -> bits 16..27
-  x = lop3_sel(x, x * 4u, 0x00FF00FFu);             // pairs -> bytes
-  x = lop3_sel(x, x * 2u, 0x0F0F0F0Fu);             // codes -> nibbles
-  return x & 0x77777777u;                            // bit 3 of each nibble clear (prmt index mode)
-}
-
 __device__ __forceinline__ Table8 table8_from(const uint4& v) {
   Table8 t;
   t.l0 = v.x; t.l1 = v.y; t.h0 = v.z; t.h1 = v.w;
@@ -97,10 +88,12 @@ __device__ __forceinline__ Table16 table16_from(const uint4& lo, const uint4& hi
   return t;
 }
 
-// 8 consecutive weights (3-bit codes in g) -> 4 packed operand pairs, K order.
-__device__ __forceinline__ uint4 dec8_b3(uint32_t g, const Table8& t) {
-  const uint32_t s0 = spread3(g);
-  const uint32_t s1 = __umulhi(s0, 65536u);          // s0 >> 16 on the FMA pipe
+// 8 consecutive weights (3-bit codes, nibbles of w with bit 3 clear) -> 4
+// packed operand pairs, K order.  prmt reads the low 16 bits of its selector:
+// codes 0-3 from w itself, codes 4-7 from w >> 16.
+__device__ __forceinline__ uint4 dec8_n3(uint32_t w, const Table8& t) {
+  const uint32_t s0 = w;
+  const uint32_t s1 = __umulhi(w, 65536u);            // w >> 16 on the FMA pipe
   const uint32_t lo0 = prmt(t.l0, t.l1, s0), hi0 = prmt(t.h0, t.h1, s0);
   const uint32_t lo1 = prmt(t.l0, t.l1, s1), hi1 = prmt(t.h0, t.h1, s1);
   uint4 o;
@@ -130,12 +123,13 @@ __device__ __forceinline__ uint4 dec8_b4(uint32_t w, const Table16& t) {
   return o;
 }
 
-// One 32-weight block of 3-bit codes (stream words w0..w2) -> 4 chunks of 8.
-__device__ __forceinline__ void dec32_b3(uint32_t w0, uint32_t w1, uint32_t w2, const Table8& t, uint4 (&c)[4]) {
-  c[0] = dec8_b3(w0, t);
-  c[1] = dec8_b3(__funnelshift_r(w0, w1, 24), t);
-  c[2] = dec8_b3(__funnelshift_r(w1, w2, 16), t);
-  c[3] = dec8_b3(w2 >> 8, t);
+// One 32-weight block (4 tiled words, 8 codes each) -> 4 chunks of 8.
+__device__ __forceinline__ void dec32_n3(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3, const Table8& t,
+                                         uint4 (&c)[4]) {
+  c[0] = dec8_n3(w0, t);
+  c[1] = dec8_n3(w1, t);
+  c[2] = dec8_n3(w2, t);
+  c[3] = dec8_n3(w3, t);
 }
 
 __device__ __forceinline__ void dec32_b4(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3, const Table16& t,

@@ -13,9 +13,10 @@
 //               rows, level tables, expert scales, the block's slot ids and
 //               top-k weights) into a small shared ring and the tile's fp8
 //               scale codes (1-D bulk copy); the index words of the weight
-//               tile, one 2-D TMA box of 128 rows x k_idx inputs (k_idx up to
-//               512, so each row moved is 144-256 bytes: TMA cost is per row),
-//               into a ring the decoders release
+//               tile from the layer's tiled copy of the index stream, where a
+//               128-row x 128-input step is 8 KB of contiguous memory: one 1-D
+//               bulk copy per projection and stage (k_idx/128 steps) into a
+//               ring the decoders release
 //   warp 6+dec  activation producer: the block's rows of the plan-ordered
 //               activations, two 64-column boxes per 128 inputs, into a ring
 //               the MMA releases (its own warp, so a full activation ring never
@@ -29,8 +30,10 @@
 //               fp8 scale codes and rounded to the operand type (shared
 //               memory, two buffers)
 //   warps 6..   decoders, groups of 8 taking 128-input sub-blocks in turn: per
-//               32-input block one code-table load and prmt lookups of the
-//               packed codes into one of two 16-register buffers, written to
+//               32-input block one 16-byte load of its 32 codes (a nibble
+//               each; a warp's loads cover 512 contiguous bytes, free of bank
+//               conflicts), one code-table load and prmt lookups of the codes
+//               into one of two 16-register buffers, written to
 //               TMEM with tcgen05.st while the other buffer's store drains; a
 //               half-stage goes to the MMA once both its stores are done
 // Every wait is bounded (ptx.cuh): a lost arrival ends the kernel with the
@@ -107,16 +110,17 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
-// Decode the 32-input block BLK (0..3) of one stage row into 16 packed operand
-// registers (K order).  w: the row's stage words; tab: this projection's code
-// tables (plane 0, then plane 1 at +256); code: the block's fp8 scale code.
+// Decode the 32-input block BLK (0..3) of one 128-input step of a row into 16
+// packed operand registers (K order).  w: the row's 16 tiled words of the step
+// (4 per block); tab: this projection's code tables (plane 0, then plane 1 at
+// +256); code: the block's fp8 scale code.
 template <int BLK>
 __device__ __forceinline__ void decode_block(const uint32_t (&w)[16], int bits, const uint4* tab, uint32_t code,
                                              uint32_t* r) {
   uint4 ch[4];
   if (bits == 3) {
     const Table8 tb = table8_from(tab[code]);
-    dec32_b3(w[3 * BLK], w[3 * BLK + 1], w[3 * BLK + 2], tb, ch);
+    dec32_n3(w[4 * BLK], w[4 * BLK + 1], w[4 * BLK + 2], w[4 * BLK + 3], tb, ch);
   } else {
     const Table16 tb = table16_from(tab[code], tab[256 + code]);
     dec32_b4(w[4 * BLK], w[4 * BLK + 1], w[4 * BLK + 2], w[4 * BLK + 3], tb, ch);
@@ -156,11 +160,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
     c->abort = 0;
     fence_mbar_init();
   }
-  if (warp == 0 && lane == 0) {
-    for (int t = 0; t < p.num_tiers; ++t)
-      for (int j = 0; j < NPROJ; ++j) prefetch_tmap(&p.tm_idx[t][j]);
-    prefetch_tmap(&p.tm_b);
-  }
+  if (warp == 0 && lane == 0) prefetch_tmap(&p.tm_b);
   if (warp == 1) {
     tmem_alloc(&c->tmem_base, kTmemCols);
     tmem_relinquish();
@@ -220,8 +220,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
         if (lane == 0) mbar_arrive(&c->i_full[ri]);
       }
       if (!ti.ok) continue;
-      const uint32_t wst = static_cast<uint32_t>(p.k_idx / 32 * ti.bits);   // index words per row per stage
-      const uint32_t idx_bytes = NPROJ * 128u * wst * 4u;
+      const uint32_t proj_bytes = static_cast<uint32_t>(spi) * kStepBytes;   // one projection's part of a stage
+      const size_t tile_base = (static_cast<size_t>(ti.local) * p.m_tiles + ti.m) * ksteps * kStepBytes;
       const int sb = s_issued & 1;
       if (!mbar_wait_idle(&c->s_empty[sb], ((s_issued >> 1) & 1) ^ 1, abort_flag, p.dev_err)) { aborted = true; break; }
       if (lane == 0) {
@@ -233,16 +233,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
         }
       }
       ++s_issued;
-      const int32_t wrow = ti.local * p.rows_pad + ti.m * 128;
-      for (int kb = 0, st = 0; kb < ksteps; kb += spi, ++st) {
+      for (int kb = 0; kb < ksteps; kb += spi) {
         {
           if (!mbar_wait_idle(&c->x_empty[xs], xph ^ 1, abort_flag, p.dev_err)) { aborted = true; break; }
           if (lane == 0) {
             uint8_t* dst = xring + xs * p.sz_idx;
-            mbar_arrive_expect_tx(&c->x_full[xs], idx_bytes);
+            mbar_arrive_expect_tx(&c->x_full[xs], NPROJ * proj_bytes);
             for (int j = 0; j < NPROJ; ++j)
-              tma_load_2d_hint(dst + j * 128 * wst * 4, &p.tm_idx[ti.tier][j], &c->x_full[xs],
-                               st * static_cast<int>(wst), wrow, pol_stream);
+              bulk_load_hint(dst + j * proj_bytes, p.idx_t[ti.tier][j] + tile_base + static_cast<size_t>(kb) * kStepBytes,
+                             proj_bytes, &c->x_full[xs], pol_stream);
           }
           ++x_issued;
           if (++xs == static_cast<uint32_t>(p.di)) { xs = 0; xph ^= 1; }
@@ -483,7 +482,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
       // the sub-block loop is specialised on the tile's index width: no per-block branch
       auto kb_loop = [&](auto bits_c) {
         constexpr int BITS = decltype(bits_c)::value;
-        const uint32_t wst = static_cast<uint32_t>(p.k_idx / 32 * BITS);
         int sub = -1, grp = kDecGroups - 1;     // position in the index stage / in the group rotation
         // scale codes of the 4 blocks of a 128-input step, one byte each, loaded one step ahead
         auto load_sc = [&](int k) -> uint32_t {
@@ -502,18 +500,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
           }
           uint32_t w[16];
           if (mine_k) {
-            const uint4* w4 = reinterpret_cast<const uint4*>(xring + xs * p.sz_idx + ((proj * 128 + row) * wst) * 4) +
-                              sub * BITS;
-            const uint4 v0 = w4[0], v1 = w4[1], v2 = w4[2];
+            // this row's 4 words of each 32-input block: [proj][sub][block][row] x 16 B
+            const uint4* w4 = reinterpret_cast<const uint4*>(xring + xs * p.sz_idx) + (proj * spi + sub) * 512 + row;
+            const uint4 v0 = w4[0], v1 = w4[128], v2 = w4[256], v3 = w4[384];
             w[0] = v0.x; w[1] = v0.y; w[2] = v0.z; w[3] = v0.w;
             w[4] = v1.x; w[5] = v1.y; w[6] = v1.z; w[7] = v1.w;
             w[8] = v2.x; w[9] = v2.y; w[10] = v2.z; w[11] = v2.w;
-            if (BITS == 4) {
-              const uint4 v3 = w4[3];
-              w[12] = v3.x; w[13] = v3.y; w[14] = v3.z; w[15] = v3.w;
-            } else {
-              w[12] = w[13] = w[14] = w[15] = 0u;
-            }
+            w[12] = v3.x; w[13] = v3.y; w[14] = v3.z; w[15] = v3.w;
           }
           if (sub == spi - 1) {
             // every sub-block of the stage this group reads is in registers: release it

@@ -25,11 +25,13 @@ constexpr int kMma2Warp = kBWarp + 1;   // second MMA issuer (gate/up)
 constexpr int kGemmThreads = (kBWarp + 2) * 32;  // index TMA, MMA, 4 epilogue, decoders, activation TMA, MMA
 constexpr uint32_t kTmemCols = 512;
 
+constexpr uint32_t kStepBytes = 8192;   // one 128-row x 128-input step of a tiled index stream
+
 // Everything the grouped-GEMM kernel needs; passed by value as a
 // __grid_constant__ parameter (tensor maps must live in parameter space).
 struct GemmParams {
-  CUtensorMap tm_idx[kMaxTiers][2];  // idx stacks viewed as [n*rows_pad, k_pad/32*bits] u32
   CUtensorMap tm_b;                  // B rows in plan order: x_sorted [rows, H] (gate/up) or act [rows, I_pad] (down)
+  const uint8_t* idx_t[kMaxTiers][2];  // tiled index streams (hexmoe_tile_index layout)
   const uint8_t* bs[kMaxTiers][2];
   const float* es[kMaxTiers][2];
   const float* lev[kMaxTiers][2];
@@ -53,7 +55,7 @@ struct GemmParams {
   uint32_t off_scale, sz_scale;  // two tile-scale buffers
   int32_t k_idx;               // reduction elements per index stage (128..512, divides k_pad)
   int32_t di;                  // index ring depth
-  uint32_t off_idx, sz_idx;    // index stage: [nproj][128 rows][k_idx*bits/32 words]
+  uint32_t off_idx, sz_idx;    // index stage: [nproj][k_idx/128 steps][4 blocks][128 rows][4 words]
   int32_t db;                  // activation ring depth
   uint32_t off_b, sz_b;        // activation stage: [2 halves][bm rows][64 x 16-bit], 128-B swizzled
   uint32_t smem_bytes;         // dynamic shared memory to request
@@ -84,6 +86,9 @@ cudaError_t launch_dequant(const hexmoe_parts& parts, int bits, int block, int n
                            int64_t stride_row, int64_t row_off, cudaStream_t st);
 cudaError_t launch_combine(const void* y, int y_dtype, int64_t T, int32_t topk, int32_t H, int64_t ld_y, void* out,
                            int out_dtype, cudaStream_t st, bool pdl);
+// Tiled copy of one idx stack (hexmoe_tile_index layout).
+cudaError_t launch_tile_index(const uint32_t* idx, int bits, int n, int rows_pad, int cols_pad, uint32_t* out,
+                              cudaStream_t st);
 cudaError_t launch_cast_to16(const float* x, void* out, bool bf16, int64_t n, cudaStream_t st);
 // x_sorted[r] = x[sorted_ids[r] / topk] for every plan row r < npp holding a slot
 // (x in x_dtype, x_sorted 16-bit: bf16 for f32 input); padding rows untouched.

@@ -271,6 +271,53 @@ cudaError_t launch_dequant(const hexmoe_parts& parts, int bits, int block, int n
 }
 
 // ---------------------------------------------------------------------------
+// Tiled index copy (hexmoe_tile_index): one thread per output word, in output
+// order (coalesced stores).  Output word o = ((((e * m_tiles + m) * ksteps + s)
+// * 4 + b) * 128 + r) * 4 + j holds, one per nibble, the 8 codes of inputs
+// s*128 + b*32 + j*8 .. +7 of row m*128 + r of expert e.  A stored 32-input
+// block is `bits` little-endian words with code i at bits [i*bits, i*bits+bits)
+// (hex_ref.pack, hex_ref.py:49-61): 4-bit words are already nibble-packed;
+// 3-bit word j is the 24 bits from bit 24*j, which never reach past the
+// block's third word.
+__global__ void tile_index_kernel(const uint32_t* __restrict__ idx, int bits, int rows_pad, int cols_pad,
+                                  int64_t total, uint32_t* __restrict__ out) {
+  const int m_tiles = rows_pad / 128, ksteps = cols_pad / 128;
+  const int64_t wpr = static_cast<int64_t>(cols_pad) / 32 * bits;
+  for (int64_t o = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; o < total;
+       o += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int j = static_cast<int>(o & 3), r = static_cast<int>((o >> 2) & 127), b = static_cast<int>((o >> 9) & 3);
+    const int64_t rest = o >> 11;
+    const int s = static_cast<int>(rest % ksteps);
+    const int64_t em = rest / ksteps;
+    const int m = static_cast<int>(em % m_tiles);
+    const int64_t e = em / m_tiles;
+    const uint32_t* src = idx + (e * rows_pad + m * 128 + r) * wpr + static_cast<int64_t>(s * 4 + b) * bits;
+    uint32_t w;
+    if (bits == 4) {
+      w = __ldg(src + j);
+    } else {
+      const int start = 24 * j, wi = start >> 5, sh = start & 31;
+      uint32_t v = __ldg(src + wi) >> sh;
+      if (sh + 24 > 32) v |= __ldg(src + wi + 1) << (32 - sh);
+      w = 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) w |= ((v >> (3 * i)) & 7u) << (4 * i);
+    }
+    out[o] = w;
+  }
+}
+
+cudaError_t launch_tile_index(const uint32_t* idx, int bits, int n, int rows_pad, int cols_pad, uint32_t* out,
+                              cudaStream_t st) {
+  const int64_t total = static_cast<int64_t>(n) * rows_pad * cols_pad / 8;
+  if (total == 0) return cudaSuccess;
+  const int threads = 256;
+  const int grid = static_cast<int>(std::min<int64_t>((total + threads - 1) / threads, 148 * 32));
+  tile_index_kernel<<<grid, threads, 0, st>>>(idx, bits, rows_pad, cols_pad, total, out);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
 // Combine (runtime/blackhole_runtime/hex_moe.py:325, y.view(T, k, H).sum(1)):
 // out[t, h] = sum_j y[t*k + j, h], fp32 accumulation in slot order.
 template <typename YT, int OUT>

@@ -228,6 +228,16 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                : "memory");
 }
 
+// The same copy with an L2 cache policy (createpolicy) for the source lines.
+__device__ __forceinline__ void bulk_load_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                               uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
 // Shared-memory matrix descriptor of a K-major tile in the canonical 128-byte
 // swizzled layout: rows of 64 16-bit elements (128 B), 8-row groups 1024 B
 // apart (SBO), tile base 1024-B aligned.  Advancing K by 16 elements inside the

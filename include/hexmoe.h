@@ -108,12 +108,31 @@ HEXMOE_API int hexmoe_device_status(int device, int clear, int32_t* status_out);
  * for all tiers at once.  desc->expert_map is not read. */
 HEXMOE_API int hexmoe_build_expert_map(const hexmoe_layer_desc* desc, int32_t* map_out, void* stream);
 
-/* Builds the kernel-side view of a layer (tensor maps over every idx stack,
- * the global->(tier, local) expert map) on the current device.  Replaces the
- * per-call argument marshalling of _launch (hex_moe.py:286-301) and the
- * lookup built in HexTier.prepare (hex_moe.py:193-196). */
+/* Builds the kernel-side view of a layer on the current device: the
+ * global->(tier, local) expert map and a tiled copy of every idx stack
+ * (hexmoe_tile_index layout), which the grouped GEMM streams instead of the
+ * stored stacks.  Replaces the per-call argument marshalling of _launch
+ * (hex_moe.py:286-301) and the lookup built in HexTier.prepare
+ * (hex_moe.py:193-196).
+ * The copy takes n * rows_pad * cols_pad / 2 bytes of device memory per
+ * projection (one cudaMalloc, freed by hexmoe_layer_destroy) and snapshots the
+ * index streams: create waits for the device to go idle first, so it must not
+ * run inside stream capture, and later writes to the stacks are not seen.
+ * The stored stacks stay in use for hexmoe_dequant. */
 HEXMOE_API int hexmoe_layer_create(const hexmoe_layer_desc* desc, hexmoe_layer** out);
 HEXMOE_API int hexmoe_layer_destroy(hexmoe_layer* layer);
+
+/* The tiled index layout the grouped GEMM reads.  idx: [n, rows_pad,
+ * cols_pad/32*bits] u32, the stored HEX stream (hex_ref.pack,
+ * hex_ref.py:49-61: per 32-input block `bits` little-endian words).  out:
+ * [n, rows_pad/128, cols_pad/128, 4, 128, 4] u32 (n*rows_pad*cols_pad/2
+ * bytes): for weight-row tile m, 128-input step s, 32-input block b of the
+ * step and row r of the tile, 4 words whose nibble i of word j holds the code
+ * of input s*128 + b*32 + j*8 + i (3-bit codes with bit 3 clear).  One step of
+ * one tile is 8 KB of contiguous memory.  rows_pad and cols_pad: multiples of
+ * 128.  Asynchronous on `stream`. */
+HEXMOE_API int hexmoe_tile_index(const uint32_t* idx, int32_t bits, int32_t n, int32_t rows_pad,
+                                 int32_t cols_pad, uint32_t* out, void* stream);
 
 /* Scratch bytes hexmoe_forward needs for `tokens` tokens at top-`topk` with
  * tile height `block_m` (16, 32, 64 or 128; 0 = automatic, as

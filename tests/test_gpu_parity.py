@@ -35,6 +35,29 @@ def _bits(a: np.ndarray) -> np.ndarray:
     return np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
 
 
+# ----------------------------------------------------------------------------- tiled index copy
+@pytest.mark.parametrize("bits", [3, 4])
+def test_tile_index_layout_vs_oracle_codes(oracle, bits):
+    """hexmoe_tile_index (the copy the GEMM streams) holds every code of the
+    stored stream in its documented nibble position."""
+    from blackhole_b200 import _lib
+    rng = np.random.default_rng(40 + bits)
+    n, rows_pad, cols_pad = 3, 256, 384
+    codes = rng.integers(0, 1 << bits, size=(n, rows_pad, cols_pad)).astype(np.uint8)
+    words = oracle.pack(codes, bits)
+    assert np.array_equal(oracle.unpack(words, bits, cols_pad), codes)
+    idx = torch.from_numpy(np.ascontiguousarray(words).view(np.int32)).to(DEV)
+    out = torch.full((n * rows_pad * cols_pad // 8,), -1, dtype=torch.int32, device=DEV)
+    _lib.check(_lib.lib.hexmoe_tile_index(idx.data_ptr(), bits, n, rows_pad, cols_pad, out.data_ptr(), None),
+               "hexmoe_tile_index")
+    torch.cuda.synchronize()
+    got = out.cpu().numpy().view(np.uint32).reshape(n, rows_pad // 128, cols_pad // 128, 4, 128, 4)
+    # nibble i of word j of (e, m, s, b, r) = code of input s*128 + b*32 + j*8 + i of row m*128 + r
+    c = codes.reshape(n, rows_pad // 128, 128, cols_pad // 128, 4, 4, 8).transpose(0, 1, 3, 4, 2, 5, 6)
+    want = np.bitwise_or.reduce(c.astype(np.uint32) << (4 * np.arange(8, dtype=np.uint32)), axis=-1)
+    assert np.array_equal(got, want)
+
+
 # ----------------------------------------------------------------------------- dequant
 
 

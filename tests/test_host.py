@@ -43,6 +43,9 @@ def test_argument_errors_raise_valueerror_without_gpu():
     h = ctypes.c_void_p()
     assert _lib.lib.hexmoe_layer_create(ctypes.byref(d), ctypes.byref(h)) == _lib.HEXMOE_E_ARG   # 100 % 32 != 0
     assert _lib.lib.hexmoe_forward(None, None, 0, 1, 1, None, None, 0, None, 0, 0, None, 0, None) == _lib.HEXMOE_E_ARG
+    assert _lib.lib.hexmoe_tile_index(None, 3, 1, 100, 128, None, None) == _lib.HEXMOE_E_ARG    # rows_pad % 128
+    assert _lib.lib.hexmoe_tile_index(None, 5, 1, 128, 128, None, None) == _lib.HEXMOE_E_ARG    # bits
+    assert _lib.lib.hexmoe_tile_index(None, 3, 1, 128, 128, None, None) == _lib.HEXMOE_E_ARG    # null pointers
 
 
 def make_tier(E=12, H=128, I=64, bits=3, block=32, seed=0):
