@@ -144,15 +144,25 @@ int plan_gemm(GemmParams& p, bool glu, int bm, int k_pad, int block) {
   if (!p.di) return fail(HEXMOE_E_UNSUPPORTED, "reduction length %d / block_m %d do not fit shared memory", k_pad, bm);
   p.off_b = static_cast<uint32_t>(align_up(p.off_idx + static_cast<size_t>(p.di) * p.sz_idx, 1024));
   p.smem_bytes = std::max<uint32_t>(p.off_b + p.db * p.sz_b + 1024, 120 * 1024);
-  // gate/up: two threads issue the MMAs, one projection (accumulator) each: one
-  // tcgen05.mma of N <= 64 columns keeps its issuing thread busy longer than the
-  // tensor pipe takes to run it.
-  p.n_iss = glu ? 2 : 1;
-  p.acc_stride = static_cast<uint32_t>(nproj * bm);
+  // MMA issuers: one thread per projection (its own accumulator); with N <= 64
+  // columns a tcgen05.mma keeps its issuing thread busy longer than the tensor
+  // pipe takes to run it, so where an issuer warp is free (down: one
+  // projection) and tensor memory allows, two threads take alternate 128-input
+  // steps into two accumulators that the epilogue adds (ksplit 2: at least two
+  // steps, and three operand stages left).  Gate/up would need two more warps,
+  // and the registers they take from the decoders cost more than the split
+  // gains (measured).
   p.a_stride = static_cast<uint32_t>(64 * nproj);   // one 128-input step per operand stage
-  p.nbuf = (2 * p.acc_stride + 2 * p.a_stride <= kTmemCols) ? 2 : 1;
-  p.a_base = p.nbuf * p.acc_stride;
-  p.da = static_cast<int>(std::min<uint32_t>(kMaxDA, (kTmemCols - p.a_base) / p.a_stride));
+  for (int ksplit = 2; ksplit >= 1; --ksplit) {
+    if (ksplit == 2 && (k_pad / kKStep < 2 || bm > 64 || nproj * 2 > kMmaWarps)) continue;
+    p.ksplit = ksplit;
+    p.n_iss = nproj * ksplit;
+    p.acc_stride = static_cast<uint32_t>(p.n_iss * bm);
+    p.nbuf = (2 * p.acc_stride + 2 * p.a_stride <= kTmemCols) ? 2 : 1;
+    p.a_base = p.nbuf * p.acc_stride;
+    p.da = static_cast<int>(std::min<uint32_t>(kMaxDA, (kTmemCols - p.a_base) / p.a_stride));
+    if (ksplit == 1 || p.da >= 3) break;
+  }
   if (p.da < 2) return fail(HEXMOE_E_UNSUPPORTED, "block_m %d leaves no tensor memory for operands", bm);
   return HEXMOE_OK;
 }

@@ -23,7 +23,10 @@
 //               delays the next index stage)
 //   warp 1,     TMEM allocation (warp 1); one thread of each issues tcgen05.mma
 //   last warp   (A operand from TMEM, B from 128-B swizzled smem) and
-//               tcgen05.commit: gate and up each, or (down) warp 1 alone
+//               tcgen05.commit: gate and up one each; down one, or both (each
+//               over alternate 128-input steps into its own accumulator,
+//               summed by the epilogue) where an M=128 x N<=64 MMA costs its
+//               issuing thread more than the tensor pipe takes to run it
 //   warps 2-5   epilogue: tcgen05.ld of the accumulators, SwiGLU (gate/up) or
 //               the top-k weight (down), 16-bit stores; one tile ahead, the
 //               code tables: the level table scaled by every one of the 256
@@ -55,7 +58,7 @@ struct Ctrl {
   uint64_t t_full[2], t_empty[2];             // accumulator buffers
   uint64_t i_full[kRecs], i_empty[kRecs];     // tile records
   uint64_t tab_ready[2], tab_empty[2];        // code tables built / released (per buffer)
-  uint64_t drain[2];
+  uint64_t drain[kMmaWarps];   // one per MMA issuer
   uint32_t tmem_base;
   int32_t abort;
 };
@@ -134,8 +137,11 @@ __device__ __forceinline__ void decode_block(const uint32_t (&w)[16], int bits, 
   }
 }
 
-template <bool GLU, bool BF16>
+// KS: the split issue of down (p.ksplit == 2), a separate instantiation so the
+// other kernels carry none of its code.
+template <bool GLU, bool BF16, bool KS>
 __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_constant__ GemmParams p) {
+  static_assert(!(GLU && KS), "gate/up keeps one issuer per projection");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   Ctrl* c = reinterpret_cast<Ctrl*>(smem);
@@ -147,16 +153,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kMaxDI; ++i) { mbar_init(&c->x_full[i], 1); mbar_init(&c->x_empty[i], kDecWarps); }
-    for (int i = 0; i < kMaxDB; ++i) { mbar_init(&c->b_full[i], 1); mbar_init(&c->b_empty[i], p.n_iss); }
-    for (int i = 0; i < kMaxDA; ++i) { mbar_init(&c->a_full[i], 8); mbar_init(&c->a_empty[i], p.n_iss); }
+    const int stage_users = p.n_iss / p.ksplit;   // issuers reading one operand / activation stage
+    for (int i = 0; i < kMaxDB; ++i) { mbar_init(&c->b_full[i], 1); mbar_init(&c->b_empty[i], stage_users); }
+    for (int i = 0; i < kMaxDA; ++i) { mbar_init(&c->a_full[i], 8); mbar_init(&c->a_empty[i], stage_users); }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&c->s_full[i], 1); mbar_init(&c->s_empty[i], kDecWarps);
       mbar_init(&c->t_full[i], p.n_iss); mbar_init(&c->t_empty[i], 4);
       mbar_init(&c->tab_ready[i], 4); mbar_init(&c->tab_empty[i], kDecWarps);
     }
-    for (int i = 0; i < kRecs; ++i) { mbar_init(&c->i_full[i], 1); mbar_init(&c->i_empty[i], 7 + kDecWarps); }
-    mbar_init(&c->drain[0], 1);
-    mbar_init(&c->drain[1], 1);
+    for (int i = 0; i < kRecs; ++i) { mbar_init(&c->i_full[i], 1); mbar_init(&c->i_empty[i], 5 + kMmaWarps + kDecWarps); }
+    for (int i = 0; i < kMmaWarps; ++i) mbar_init(&c->drain[i], 1);
     c->abort = 0;
     fence_mbar_init();
   }
@@ -291,12 +297,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
         drain_wait(&c->b_full[q % p.db], (q / p.db) & 1);
       }
     }
-  } else if (warp == 1 || warp == kMma2Warp) {
+  } else if (warp == 1 || warp > kBWarp) {
     // ------------------------------------------------------------ MMA issuers
-    // gate/up: issuer mi owns projection mi (its own accumulator); down: warp 1
-    // issues everything and the second issuer only follows the tile records.
-    const int mi = warp == 1 ? 0 : 1;
+    // Issuer mi owns projection mi % nproj and, with ksplit 2, the 128-input
+    // steps of parity mi / nproj, into accumulator mi; issuers beyond n_iss only
+    // follow the tile records.
+    const int mi = warp == 1 ? 0 : warp - kBWarp;
     const bool active = mi < p.n_iss;
+    const int proj = mi % NPROJ, part = mi / NPROJ;
     uint32_t bs = 0, bph = 0, as = 0, aph = 0;
     bool aborted = false;
     int cur = 0, acc_it = 0;
@@ -315,19 +323,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
       tc_fence_after();
       const uint32_t d = tmem + ab * p.acc_stride + mi * p.bm;
       const uint32_t h_step = static_cast<uint32_t>(p.bm * 128) >> 4;   // descriptor units per 64-input half
-      for (int ks = 0; ks < ksteps && !aborted; ++ks) {
+      for (int ks = 0, kpar = 0; ks < ksteps && !aborted; ++ks, kpar ^= 1) {
+        if (KS && kpar != part) {
+          // the other issuer's step: only the ring positions move
+          if (++as == static_cast<uint32_t>(p.da)) { as = 0; aph ^= 1; }
+          if (++bs == static_cast<uint32_t>(p.db)) { bs = 0; bph ^= 1; }
+          continue;
+        }
         if (!mbar_wait(&c->b_full[bs], bph, abort_flag, p.dev_err)) { aborted = true; break; }
         const uint64_t bdesc = sw128_desc(smem_u32(bring + bs * p.sz_b));
         if (!mbar_wait(&c->a_full[as], aph, abort_flag, p.dev_err)) { aborted = true; break; }
         tc_fence_after();
         if (lane == 0) {
-          const uint32_t a0 = tmem + p.a_base + as * p.a_stride + mi * 64;
+          const uint32_t a0 = tmem + p.a_base + as * p.a_stride + proj * 64;
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             const uint64_t bh = bdesc + h * h_step;
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
-              umma_f16_ts(d, a0 + h * 32 + kk * 8, bh + kk * 2, idesc, (ks | h | kk) != 0);
+              umma_f16_ts(d, a0 + h * 32 + kk * 8, bh + kk * 2, idesc, (ks != (KS ? part : 0)) || (h | kk) != 0);
           }
           umma_commit(&c->a_empty[as]);
         }
@@ -418,6 +432,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
         tmem_ld16(d0 + n0, g);
         if (GLU) tmem_ld16(d0 + p.bm + n0, u);
         tmem_ld_wait();
+        if (KS) {
+          // split issue: the odd-step accumulator (columns bm on) adds in
+          uint32_t g2[16];
+          tmem_ld16(d0 + p.bm + n0, g2);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) g[j] = __float_as_uint(__uint_as_float(g[j]) + __uint_as_float(g2[j]));
+        }
         if (n0 + 16 >= cnt) {
           // every accumulator column of the tile is in registers: free the buffer now
           tc_fence_before();
@@ -581,9 +603,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
   if (warp == 1) tmem_dealloc(tmem, kTmemCols);
 }
 
-template <bool GLU, bool BF16>
+template <bool GLU, bool BF16, bool KS>
 static cudaError_t launch_one(const GemmParams& p, int grid, cudaStream_t stream, bool pdl) {
-  auto kern = hex_gemm_kernel<GLU, BF16>;
+  auto kern = hex_gemm_kernel<GLU, BF16, KS>;
   static int configured_bytes[64] = {};   // per device and instantiation; raised monotonically
   int dev = 0;
   cudaGetDevice(&dev);
@@ -608,8 +630,14 @@ static cudaError_t launch_one(const GemmParams& p, int grid, cudaStream_t stream
 }
 
 cudaError_t launch_gemm(const GemmParams& p, bool glu, bool bf16, int grid, cudaStream_t stream, bool pdl) {
-  if (glu) return bf16 ? launch_one<true, true>(p, grid, stream, pdl) : launch_one<true, false>(p, grid, stream, pdl);
-  return bf16 ? launch_one<false, true>(p, grid, stream, pdl) : launch_one<false, false>(p, grid, stream, pdl);
+  // gate/up never splits its issue (two projections already take both issuer warps)
+  if (glu) {
+    if (p.ksplit != 1) return cudaErrorInvalidValue;
+    return bf16 ? launch_one<true, true, false>(p, grid, stream, pdl) : launch_one<true, false, false>(p, grid, stream, pdl);
+  }
+  if (p.ksplit == 2)
+    return bf16 ? launch_one<false, true, true>(p, grid, stream, pdl) : launch_one<false, false, true>(p, grid, stream, pdl);
+  return bf16 ? launch_one<false, true, false>(p, grid, stream, pdl) : launch_one<false, false, false>(p, grid, stream, pdl);
 }
 
 }  // namespace hexmoe

@@ -21,8 +21,8 @@ constexpr int kMaxDA = 8;        // deepest TMEM operand ring
 constexpr int kDecGroups = HEXMOE_DEC_GROUPS;   // groups of 8 decoder warps, taking 128-input sub-blocks in turn
 constexpr int kDecWarps = 8 * kDecGroups;
 constexpr int kBWarp = 6 + kDecWarps;   // activation producer
-constexpr int kMma2Warp = kBWarp + 1;   // second MMA issuer (gate/up)
-constexpr int kGemmThreads = (kBWarp + 2) * 32;  // index TMA, MMA, 4 epilogue, decoders, activation TMA, MMA
+constexpr int kMmaWarps = 2;            // MMA issuers: warp 1 and warp kBWarp+1
+constexpr int kGemmThreads = (kBWarp + kMmaWarps) * 32;  // index TMA, MMA, 4 epilogue, decoders, activation TMA, MMA
 constexpr uint32_t kTmemCols = 512;
 
 constexpr uint32_t kStepBytes = 8192;   // one 128-row x 128-input step of a tiled index stream
@@ -61,7 +61,8 @@ struct GemmParams {
   uint32_t smem_bytes;         // dynamic shared memory to request
   // TMEM carve-up (columns)
   int32_t nbuf;                // accumulator buffers (1 or 2)
-  int32_t n_iss;               // MMA issuing threads: 2 for gate/up (one projection each), 1 for down
+  int32_t n_iss;               // MMA issuing threads: nproj x ksplit
+  int32_t ksplit;              // accumulators per projection: 2 = issuers take alternate 128-input steps
   int32_t da;                  // operand ring depth
   uint32_t acc_stride;         // columns per accumulator buffer
   uint32_t a_base, a_stride;   // operand ring: first column, columns per stage

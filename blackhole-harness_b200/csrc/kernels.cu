@@ -60,18 +60,41 @@ cudaError_t launch_build_expert_map(const hexmoe_layer_desc& d, int32_t* map, cu
 // each warp walks its segment again in order; a slot's place inside its
 // expert's run is the running count of its warp's row plus its rank among
 // equal lanes of the chunk.  Together that is the order of a stable sort.
+// When the ids fit in shared memory (as 16-bit expert ids next to the
+// histograms) all threads stage them there first, kAlignBatch loads in flight
+// per thread, and both passes read shared memory; otherwise both passes load
+// kAlignBatch chunks from global memory before working through them in order.
+// The lanes holding
+// the same expert are found with one ballot per bit of the id (7 for 96
+// experts) rather than __match_any_sync, whose cost grows with the number of
+// distinct values in the warp (here nearly 32).
 constexpr int kAlignWarps = 16;
+constexpr int kAlignBatch = 8;
 constexpr int kAlignThreads = kAlignWarps * 32;
 constexpr int kAlignMaxExperts = 2048;
+constexpr int kAlignSmemMax = 200 * 1024;   // dynamic shared memory of align_kernel
+
+// Lanes whose v equals this lane's (v < 2^nbits): the AND over the id bits of
+// the ballot of lanes that agree with this lane on that bit.
+__device__ __forceinline__ unsigned equal_lanes(uint32_t v, int nbits) {
+  unsigned m = 0xffffffffu;
+  for (int b = 0; b < nbits; ++b) {
+    const bool bit = (v >> b) & 1u;
+    const unsigned bal = __ballot_sync(0xffffffffu, bit);
+    m &= bit ? bal : ~bal;
+  }
+  return m;
+}
 
 template <bool I64>
 __global__ void __launch_bounds__(kAlignThreads, 1)
     align_kernel(const void* __restrict__ ids_raw, int64_t S, int32_t E, int32_t bm, int32_t* __restrict__ sid,
-                 int32_t* __restrict__ eid, int32_t* __restrict__ npp, int32_t* dev_err) {
+                 int32_t* __restrict__ eid, int32_t* __restrict__ npp, int32_t* dev_err, bool staged) {
   extern __shared__ int32_t sh[];
   int32_t* hist = sh;                                  // [kAlignWarps][E]
   int32_t* blk_start = sh + kAlignWarps * E;           // [E]
   int32_t* counts = blk_start + E;                     // [E]
+  int16_t* ids16 = reinterpret_cast<int16_t*>(counts + E);   // [S] when staged: expert id, -1 = out of range
   using Scan = cub::BlockScan<int32_t, kAlignThreads>;
   __shared__ typename Scan::TempStorage scan_tmp;
   __shared__ int32_t total_blocks;
@@ -79,27 +102,73 @@ __global__ void __launch_bounds__(kAlignThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   pdl_wait();
   for (int i = threadIdx.x; i < kAlignWarps * E; i += kAlignThreads) hist[i] = 0;
+  auto bad_id = [&](int64_t v) { return v < 0 || v >= E; };
+  if (staged) {
+    for (int64_t i0 = threadIdx.x; i0 < S; i0 += static_cast<int64_t>(kAlignThreads) * kAlignBatch) {
+      int64_t raw[kAlignBatch];
+#pragma unroll
+      for (int u = 0; u < kAlignBatch; ++u) {
+        const int64_t s = i0 + u * kAlignThreads;
+        raw[u] = s < S ? (I64 ? __ldg(static_cast<const int64_t*>(ids_raw) + s)
+                              : static_cast<int64_t>(__ldg(static_cast<const int32_t*>(ids_raw) + s)))
+                       : 0;
+      }
+#pragma unroll
+      for (int u = 0; u < kAlignBatch; ++u) {
+        const int64_t s = i0 + u * kAlignThreads;
+        if (s < S) {
+          if (bad_id(raw[u])) atomicOr(dev_err, kDevErrExpertId);
+          ids16[s] = bad_id(raw[u]) ? static_cast<int16_t>(-1) : static_cast<int16_t>(raw[u]);
+        }
+      }
+    }
+  }
   __syncthreads();
 
   const int64_t seg = (S + kAlignWarps - 1) / kAlignWarps;
   const int64_t s_begin = warp * seg;
   const int64_t s_end = s_begin + seg < S ? s_begin + seg : S;
-  auto load_id = [&](int64_t s) -> int32_t {
-    int64_t v = I64 ? static_cast<const int64_t*>(ids_raw)[s] : static_cast<const int32_t*>(ids_raw)[s];
-    if (v < 0 || v >= E) {
-      atomicOr(dev_err, kDevErrExpertId);
-      return -1;
+  // the expert ids of chunks c0, c0 + 32, ... (kAlignBatch of them) for this
+  // lane: every load issued before the first is used; -1 past the segment or
+  // for an out-of-range id (which also sets the error word)
+  auto load_batch = [&](int64_t c0, int32_t (&ev)[kAlignBatch]) {
+    if (staged) {
+#pragma unroll
+      for (int u = 0; u < kAlignBatch; ++u) {
+        const int64_t s = c0 + u * 32 + lane;
+        ev[u] = s < s_end ? ids16[s] : -1;
+      }
+      return;
     }
-    return static_cast<int32_t>(v);
+    int64_t raw[kAlignBatch];
+#pragma unroll
+    for (int u = 0; u < kAlignBatch; ++u) {
+      const int64_t s = c0 + u * 32 + lane;
+      raw[u] = s < s_end ? (I64 ? __ldg(static_cast<const int64_t*>(ids_raw) + s)
+                                : static_cast<int64_t>(__ldg(static_cast<const int32_t*>(ids_raw) + s)))
+                         : -1;
+    }
+#pragma unroll
+    for (int u = 0; u < kAlignBatch; ++u) {
+      const bool in_seg = c0 + u * 32 + lane < s_end;
+      const bool bad = in_seg && bad_id(raw[u]);
+      if (bad) atomicOr(dev_err, kDevErrExpertId);
+      ev[u] = (in_seg && !bad) ? static_cast<int32_t>(raw[u]) : -1;
+    }
   };
   int32_t* my_hist = hist + warp * E;
+  const int id_bits = 32 - __clz(E);   // bits of e + 1 (0 = no expert), e < E
   // pass 1
-  for (int64_t c0 = s_begin; c0 < s_end; c0 += 32) {
-    const int64_t s = c0 + lane;
-    const int32_t e = s < s_end ? load_id(s) : -1;
-    const unsigned peers = __match_any_sync(0xffffffffu, e);
-    if (e >= 0 && (peers & ((1u << lane) - 1u)) == 0) my_hist[e] += __popc(peers);
-    __syncwarp();
+  for (int64_t c0 = s_begin; c0 < s_end; c0 += 32 * kAlignBatch) {
+    int32_t ev[kAlignBatch];
+    load_batch(c0, ev);
+#pragma unroll
+    for (int u = 0; u < kAlignBatch; ++u) {
+      const int32_t e = ev[u];
+      const unsigned peers = equal_lanes(static_cast<uint32_t>(e + 1), id_bits);
+      if (e >= 0 && (peers & ((1u << lane) - 1u)) == 0) my_hist[e] += __popc(peers);
+      __syncwarp();
+    }
   }
   __syncthreads();
   // pass 2: prefix over warps, counts, block counts
@@ -152,19 +221,23 @@ __global__ void __launch_bounds__(kAlignThreads, 1)
   for (int64_t i = static_cast<int64_t>(total_blocks) * bm + threadIdx.x; i < max_blocks * bm; i += kAlignThreads)
     sid[i] = static_cast<int32_t>(S);
   // pass 3: scatter in stable order
-  for (int64_t c0 = s_begin; c0 < s_end; c0 += 32) {
-    const int64_t s = c0 + lane;
-    const int32_t e = s < s_end ? load_id(s) : -1;
-    const unsigned peers = __match_any_sync(0xffffffffu, e);
-    int32_t base = 0;
-    if (e >= 0) base = my_hist[e];
-    __syncwarp();
-    if (e >= 0) {
-      const int rank = __popc(peers & ((1u << lane) - 1u));
-      sid[static_cast<int64_t>(blk_start[e]) * bm + base + rank] = static_cast<int32_t>(s);
-      if (rank == 0) my_hist[e] = base + __popc(peers);
+  for (int64_t c0 = s_begin; c0 < s_end; c0 += 32 * kAlignBatch) {
+    int32_t ev[kAlignBatch];
+    load_batch(c0, ev);
+#pragma unroll
+    for (int u = 0; u < kAlignBatch; ++u) {
+      const int32_t e = ev[u];
+      const unsigned peers = equal_lanes(static_cast<uint32_t>(e + 1), id_bits);
+      int32_t base = 0;
+      if (e >= 0) base = my_hist[e];
+      __syncwarp();
+      if (e >= 0) {
+        const int rank = __popc(peers & ((1u << lane) - 1u));
+        sid[static_cast<int64_t>(blk_start[e]) * bm + base + rank] = static_cast<int32_t>(c0 + u * 32 + lane);
+        if (rank == 0) my_hist[e] = base + __popc(peers);
+      }
+      __syncwarp();
     }
-    __syncwarp();
   }
   pdl_launch_dependents();
 }
@@ -174,36 +247,31 @@ size_t align_scratch_bytes(int64_t, int32_t) { return 0; }
 cudaError_t launch_align(const void* ids, bool ids64, int64_t S, int32_t E, int32_t bm, int32_t* sid, int32_t* eid,
                          int32_t* npp, int32_t*, size_t, int32_t* dev_err, cudaStream_t st, bool pdl) {
   if (E > kAlignMaxExperts) return cudaErrorInvalidValue;
-  const size_t smem = static_cast<size_t>(kAlignWarps + 2) * E * sizeof(int32_t);
+  const size_t hist_bytes = static_cast<size_t>(kAlignWarps + 2) * E * sizeof(int32_t);
+  const size_t staged_bytes = hist_bytes + (static_cast<size_t>(S) * sizeof(int16_t) + 15) / 16 * 16;
+  const bool staged = staged_bytes <= static_cast<size_t>(kAlignSmemMax);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(1);
   cfg.blockDim = dim3(kAlignThreads);
-  cfg.dynamicSmemBytes = smem;
+  cfg.dynamicSmemBytes = staged ? staged_bytes : hist_bytes;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  cudaError_t e;
-  if (ids64) {
-    static bool cfgd = false;
-    if (!cfgd) {
-      e = cudaFuncSetAttribute(align_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (kAlignWarps + 2) * kAlignMaxExperts * 4);
-      if (e != cudaSuccess) return e;
-      cfgd = true;
-    }
-    return cudaLaunchKernelEx(&cfg, align_kernel<true>, ids, S, E, bm, sid, eid, npp, dev_err);
-  }
-  static bool cfgd32 = false;
-  if (!cfgd32) {
-    e = cudaFuncSetAttribute(align_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (kAlignWarps + 2) * kAlignMaxExperts * 4);
+  static bool configured[64][2] = {};   // per device and id width
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  auto kern = ids64 ? align_kernel<true> : align_kernel<false>;
+  if (!configured[dev][ids64]) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kAlignSmemMax);
     if (e != cudaSuccess) return e;
-    cfgd32 = true;
+    configured[dev][ids64] = true;
   }
-  return cudaLaunchKernelEx(&cfg, align_kernel<false>, ids, S, E, bm, sid, eid, npp, dev_err);
+  return cudaLaunchKernelEx(&cfg, kern, ids, S, E, bm, sid, eid, npp, dev_err, staged);
 }
 
 // ---------------------------------------------------------------------------
