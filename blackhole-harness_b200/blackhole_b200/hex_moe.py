@@ -293,9 +293,12 @@ def align(ids: torch.Tensor, n: int, block_m: int) -> tuple[torch.Tensor, torch.
     sid = torch.empty(max_blocks * block_m, dtype=torch.int32, device=ids.device)
     eid = torch.empty(max_blocks, dtype=torch.int32, device=ids.device)
     npp = torch.empty(1, dtype=torch.int32, device=ids.device)
+    nws = _lib.lib.hexmoe_align_workspace_bytes(S, n)
+    ws = torch.empty(nws, dtype=torch.uint8, device=ids.device) if nws else None
     with torch.cuda.device(ids.device):
         rc = _lib.lib.hexmoe_align(_ptr(ids), _lib.I64 if ids.dtype == torch.int64 else _lib.I32, S, n, block_m,
-                                   _ptr(sid), _ptr(eid), _ptr(npp), None, 0, _stream(ids.device))
+                                   _ptr(sid), _ptr(eid), _ptr(npp), _ptr(ws) if nws else None, nws,
+                                   _stream(ids.device))
     _lib.check(rc, "hexmoe_align")
     return sid, eid, npp
 

@@ -84,7 +84,7 @@ int auto_block_m(int64_t S, int32_t E) {
 }
 
 struct WsLayout {
-  size_t sid, eid, npp, xs, act, y, total;
+  size_t sid, eid, npp, align, xs, act, y, total;
   int64_t max_blocks;
 };
 
@@ -96,6 +96,7 @@ WsLayout ws_layout(const hexmoe_layer_desc& d, int64_t T, int32_t k, int32_t bm,
   w.sid = off; off = align_up(off + sizeof(int32_t) * w.max_blocks * bm, 256);
   w.eid = off; off = align_up(off + sizeof(int32_t) * w.max_blocks, 256);
   w.npp = off; off = align_up(off + 16, 256);
+  w.align = off; off = align_up(off + align_scratch_bytes(S, d.num_experts), 256);
   (void)x_dtype;
   w.xs = off; off = align_up(off + 2 * static_cast<size_t>(w.max_blocks) * bm * d.hidden, 256);
   w.act = off; off = align_up(off + 2 * static_cast<size_t>(w.max_blocks) * bm * d.inter_pad, 256);
@@ -431,7 +432,9 @@ int hexmoe_forward(const hexmoe_layer* layer, const void* x, int32_t x_dtype, in
   void* y = ws + w.y;
   const bool bf16 = x_dtype != HEXMOE_F16;     // f32 activations are computed in bf16
   void* xs = ws + w.xs;
-  cudaError_t e = launch_align(topk_ids, ids_dtype == HEXMOE_I64, S, d.num_experts, bm, sid, eid, npp, nullptr, 0, dev_err, st, true);
+  cudaError_t e = launch_align(topk_ids, ids_dtype == HEXMOE_I64, S, d.num_experts, bm, sid, eid, npp,
+                               reinterpret_cast<int32_t*>(ws + w.align), align_scratch_bytes(S, d.num_experts), dev_err,
+                               st, true);
   if (e != cudaSuccess) return cuda_fail(e, "align launch");
 
   e = launch_gather_rows(x, x_dtype, tokens, d.hidden, sid, npp, w.max_blocks * bm, topk, S, xs, st, true);
@@ -515,12 +518,12 @@ int hexmoe_align(const void* ids, int32_t ids_dtype, int64_t num_slots, int32_t 
   if (num_experts <= 0 || num_experts > 2048) return fail(HEXMOE_E_ARG, "num_experts %d outside 1..2048", num_experts);
   if (block_m <= 0) return fail(HEXMOE_E_ARG, "block_m %d", block_m);
   if (!npp || (num_slots > 0 && (!ids || !sorted_ids || !expert_ids))) return fail(HEXMOE_E_ARG, "hexmoe_align: null pointer");
-  (void)workspace;
-  (void)workspace_bytes;
+  if (workspace && reinterpret_cast<uintptr_t>(workspace) % 16) return fail(HEXMOE_E_ARG, "hexmoe_align: workspace not 16-byte aligned");
   int32_t* dev_err = device_error_word();
   if (!dev_err) return fail(HEXMOE_E_CUDA, "device error word unavailable");
   cudaError_t e = launch_align(ids, ids_dtype == HEXMOE_I64, num_slots, num_experts, block_m, sorted_ids, expert_ids,
-                               npp, nullptr, 0, dev_err, static_cast<cudaStream_t>(stream), false);
+                               npp, static_cast<int32_t*>(workspace), workspace ? workspace_bytes : 0, dev_err,
+                               static_cast<cudaStream_t>(stream), false);
   if (e != cudaSuccess) return cuda_fail(e, "align launch");
   return HEXMOE_OK;
 }

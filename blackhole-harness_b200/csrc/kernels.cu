@@ -48,31 +48,33 @@ cudaError_t launch_build_expert_map(const hexmoe_layer_desc& d, int32_t* map, cu
 }
 
 // ---------------------------------------------------------------------------
-// align (runtime/blackhole_runtime/hex_moe.py:201-222), one CTA, stable.
+// align (runtime/blackhole_runtime/hex_moe.py:201-222), stable.
 //
-// The S slots are cut into kAlignWarps contiguous segments, one per warp.
-// Pass 1: each warp counts its segment per expert (32 slots at a time, lanes
-// with the same expert grouped by __match_any_sync, the group leader adds the
-// group size) into its own row of hist[warp][E].  Pass 2: per expert, the
-// exclusive prefix of the rows over warps (so segment w starts after all
-// earlier segments' slots of that expert), the expert's count and block
-// count, and an exclusive scan of the block counts over experts.  Pass 3:
-// each warp walks its segment again in order; a slot's place inside its
-// expert's run is the running count of its warp's row plus its rank among
-// equal lanes of the chunk.  Together that is the order of a stable sort.
-// When the ids fit in shared memory (as 16-bit expert ids next to the
-// histograms) all threads stage them there first, kAlignBatch loads in flight
-// per thread, and both passes read shared memory; otherwise both passes load
-// kAlignBatch chunks from global memory before working through them in order.
-// The lanes holding
-// the same expert are found with one ballot per bit of the id (7 for 96
-// experts) rather than __match_any_sync, whose cost grows with the number of
-// distinct values in the warp (here nearly 32).
+// The slots are cut into contiguous segments, one per warp (one CTA of
+// kAlignWarps warps for up to kAlignOneCta slots; beyond that kAlignSeg slots
+// per CTA, kAlignSeg / kAlignWarps per warp).  Count: each warp counts its
+// segment per expert, 32 slots at a time: the lanes holding the same expert
+// are found with one ballot per bit of the id (7 for 96 experts; the cost of
+// __match_any_sync grows with the number of distinct values in the warp,
+// here nearly 32), and their leader adds the group size to the warp's row of
+// hist[warp][E].  Plan: per expert, exclusive prefixes of the counts over
+// warps (and CTAs), the expert's total and block count, and an exclusive scan
+// of the block counts over experts.  Scatter: each warp walks its segment
+// again in order; a slot goes to its expert's run at the warp's running
+// position plus its rank among equal lanes of the chunk.  Segments in order,
+// chunks in order, lanes in order: the order of a stable sort.  Every warp
+// loads kAlignBatch chunks of ids before working through them.
+// With several CTAs the three steps are three kernels (count, plan, scatter)
+// that hand the per-(CTA, expert) counts and then run offsets over a scratch
+// array of CTAs x E int32.
 constexpr int kAlignWarps = 16;
 constexpr int kAlignBatch = 8;
 constexpr int kAlignThreads = kAlignWarps * 32;
 constexpr int kAlignMaxExperts = 2048;
-constexpr int kAlignSmemMax = 200 * 1024;   // dynamic shared memory of align_kernel
+constexpr int64_t kAlignOneCta = 8192;   // slots one CTA aligns alone
+constexpr int kAlignSeg = 2048;          // slots per CTA beyond that
+constexpr int kAlignSmemMax = (kAlignWarps + 2) * kAlignMaxExperts * 4;
+using AlignScan = cub::BlockScan<int32_t, kAlignThreads>;
 
 // Lanes whose v equals this lane's (v < 2^nbits): the AND over the id bits of
 // the ballot of lanes that agree with this lane on that bit.
@@ -86,82 +88,36 @@ __device__ __forceinline__ unsigned equal_lanes(uint32_t v, int nbits) {
   return m;
 }
 
+// Expert ids of chunks c0, c0 + 32, ... (kAlignBatch of them) for this lane,
+// every load issued before the first is used; -1 past s_end or for an id
+// outside 0..E-1 (which also sets the error word).
 template <bool I64>
-__global__ void __launch_bounds__(kAlignThreads, 1)
-    align_kernel(const void* __restrict__ ids_raw, int64_t S, int32_t E, int32_t bm, int32_t* __restrict__ sid,
-                 int32_t* __restrict__ eid, int32_t* __restrict__ npp, int32_t* dev_err, bool staged) {
-  extern __shared__ int32_t sh[];
-  int32_t* hist = sh;                                  // [kAlignWarps][E]
-  int32_t* blk_start = sh + kAlignWarps * E;           // [E]
-  int32_t* counts = blk_start + E;                     // [E]
-  int16_t* ids16 = reinterpret_cast<int16_t*>(counts + E);   // [S] when staged: expert id, -1 = out of range
-  using Scan = cub::BlockScan<int32_t, kAlignThreads>;
-  __shared__ typename Scan::TempStorage scan_tmp;
-  __shared__ int32_t total_blocks;
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  pdl_wait();
-  for (int i = threadIdx.x; i < kAlignWarps * E; i += kAlignThreads) hist[i] = 0;
-  auto bad_id = [&](int64_t v) { return v < 0 || v >= E; };
-  if (staged) {
-    for (int64_t i0 = threadIdx.x; i0 < S; i0 += static_cast<int64_t>(kAlignThreads) * kAlignBatch) {
-      int64_t raw[kAlignBatch];
+__device__ __forceinline__ void load_ids(const void* ids, int64_t c0, int64_t s_end, int lane, int32_t E,
+                                         int32_t* dev_err, int32_t (&ev)[kAlignBatch]) {
+  int64_t raw[kAlignBatch];
 #pragma unroll
-      for (int u = 0; u < kAlignBatch; ++u) {
-        const int64_t s = i0 + u * kAlignThreads;
-        raw[u] = s < S ? (I64 ? __ldg(static_cast<const int64_t*>(ids_raw) + s)
-                              : static_cast<int64_t>(__ldg(static_cast<const int32_t*>(ids_raw) + s)))
-                       : 0;
-      }
-#pragma unroll
-      for (int u = 0; u < kAlignBatch; ++u) {
-        const int64_t s = i0 + u * kAlignThreads;
-        if (s < S) {
-          if (bad_id(raw[u])) atomicOr(dev_err, kDevErrExpertId);
-          ids16[s] = bad_id(raw[u]) ? static_cast<int16_t>(-1) : static_cast<int16_t>(raw[u]);
-        }
-      }
-    }
+  for (int u = 0; u < kAlignBatch; ++u) {
+    const int64_t s = c0 + u * 32 + lane;
+    raw[u] = s < s_end ? (I64 ? __ldg(static_cast<const int64_t*>(ids) + s)
+                              : static_cast<int64_t>(__ldg(static_cast<const int32_t*>(ids) + s)))
+                       : -1;
   }
-  __syncthreads();
+#pragma unroll
+  for (int u = 0; u < kAlignBatch; ++u) {
+    const bool in_seg = c0 + u * 32 + lane < s_end;
+    const bool bad = in_seg && (raw[u] < 0 || raw[u] >= E);
+    if (bad) atomicOr(dev_err, kDevErrExpertId);
+    ev[u] = (in_seg && !bad) ? static_cast<int32_t>(raw[u]) : -1;
+  }
+}
 
-  const int64_t seg = (S + kAlignWarps - 1) / kAlignWarps;
-  const int64_t s_begin = warp * seg;
-  const int64_t s_end = s_begin + seg < S ? s_begin + seg : S;
-  // the expert ids of chunks c0, c0 + 32, ... (kAlignBatch of them) for this
-  // lane: every load issued before the first is used; -1 past the segment or
-  // for an out-of-range id (which also sets the error word)
-  auto load_batch = [&](int64_t c0, int32_t (&ev)[kAlignBatch]) {
-    if (staged) {
-#pragma unroll
-      for (int u = 0; u < kAlignBatch; ++u) {
-        const int64_t s = c0 + u * 32 + lane;
-        ev[u] = s < s_end ? ids16[s] : -1;
-      }
-      return;
-    }
-    int64_t raw[kAlignBatch];
-#pragma unroll
-    for (int u = 0; u < kAlignBatch; ++u) {
-      const int64_t s = c0 + u * 32 + lane;
-      raw[u] = s < s_end ? (I64 ? __ldg(static_cast<const int64_t*>(ids_raw) + s)
-                                : static_cast<int64_t>(__ldg(static_cast<const int32_t*>(ids_raw) + s)))
-                         : -1;
-    }
-#pragma unroll
-    for (int u = 0; u < kAlignBatch; ++u) {
-      const bool in_seg = c0 + u * 32 + lane < s_end;
-      const bool bad = in_seg && bad_id(raw[u]);
-      if (bad) atomicOr(dev_err, kDevErrExpertId);
-      ev[u] = (in_seg && !bad) ? static_cast<int32_t>(raw[u]) : -1;
-    }
-  };
-  int32_t* my_hist = hist + warp * E;
-  const int id_bits = 32 - __clz(E);   // bits of e + 1 (0 = no expert), e < E
-  // pass 1
+// Count: my_hist[e] += slots of expert e in [s_begin, s_end).
+template <bool I64>
+__device__ void warp_count(const void* ids, int64_t s_begin, int64_t s_end, int lane, int32_t E, int id_bits,
+                           int32_t* my_hist, int32_t* dev_err) {
   for (int64_t c0 = s_begin; c0 < s_end; c0 += 32 * kAlignBatch) {
     int32_t ev[kAlignBatch];
-    load_batch(c0, ev);
+    load_ids<I64>(ids, c0, s_end, lane, E, dev_err, ev);
 #pragma unroll
     for (int u = 0; u < kAlignBatch; ++u) {
       const int32_t e = ev[u];
@@ -170,30 +126,53 @@ __global__ void __launch_bounds__(kAlignThreads, 1)
       __syncwarp();
     }
   }
-  __syncthreads();
-  // pass 2: prefix over warps, counts, block counts
-  constexpr int kPer = kAlignMaxExperts / kAlignThreads;   // experts per thread (contiguous)
+}
+
+// Scatter: slot s of expert e goes to sid[my_pos[e] + its rank in the chunk];
+// my_pos[e] advances past the chunk's slots of e.
+template <bool I64>
+__device__ void warp_scatter(const void* ids, int64_t s_begin, int64_t s_end, int lane, int32_t E, int id_bits,
+                             int32_t* my_pos, int32_t* sid, int32_t* dev_err) {
+  for (int64_t c0 = s_begin; c0 < s_end; c0 += 32 * kAlignBatch) {
+    int32_t ev[kAlignBatch];
+    load_ids<I64>(ids, c0, s_end, lane, E, dev_err, ev);
+#pragma unroll
+    for (int u = 0; u < kAlignBatch; ++u) {
+      const int32_t e = ev[u];
+      const unsigned peers = equal_lanes(static_cast<uint32_t>(e + 1), id_bits);
+      int32_t base = 0;
+      if (e >= 0) base = my_pos[e];
+      __syncwarp();
+      if (e >= 0) {
+        const int rank = __popc(peers & ((1u << lane) - 1u));
+        sid[base + rank] = static_cast<int32_t>(c0 + u * 32 + lane);
+        if (rank == 0) my_pos[e] = base + __popc(peers);
+      }
+      __syncwarp();
+    }
+  }
+}
+
+// Plan from the experts' totals counts[e] (shared memory, thread t holding
+// experts t*kPer .. t*kPer+kPer-1): block counts, their exclusive scan into
+// blk_start[e] (shared), npp, the expert of every block (-1 past the last)
+// and sorted_ids = S on every padding slot.  All threads; blk_start is
+// visible to the whole CTA on return.
+__device__ void plan_runs(const int32_t* counts, int32_t* blk_start, int64_t S, int32_t E, int32_t bm, int32_t* sid,
+                          int32_t* eid, int32_t* npp, typename AlignScan::TempStorage& scan_tmp,
+                          int32_t& total_blocks) {
+  constexpr int kPer = kAlignMaxExperts / kAlignThreads;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int32_t nblk[kPer];
   int32_t local_sum = 0;
 #pragma unroll
   for (int j = 0; j < kPer; ++j) {
     const int e = threadIdx.x * kPer + j;
-    nblk[j] = 0;
-    if (e < E) {
-      int32_t acc = 0;
-      for (int w = 0; w < kAlignWarps; ++w) {
-        const int32_t v = hist[w * E + e];
-        hist[w * E + e] = acc;
-        acc += v;
-      }
-      counts[e] = acc;
-      nblk[j] = (acc + bm - 1) / bm;
-      local_sum += nblk[j];
-    }
+    nblk[j] = e < E ? (counts[e] + bm - 1) / bm : 0;
+    local_sum += nblk[j];
   }
-  int32_t excl;
-  int32_t agg;
-  Scan(scan_tmp).ExclusiveSum(local_sum, excl, agg);
+  int32_t excl, agg;
+  AlignScan(scan_tmp).ExclusiveSum(local_sum, excl, agg);
 #pragma unroll
   for (int j = 0; j < kPer; ++j) {
     const int e = threadIdx.x * kPer + j;
@@ -208,7 +187,6 @@ __global__ void __launch_bounds__(kAlignThreads, 1)
   }
   __syncthreads();
   const int64_t max_blocks = (S + bm - 1) / bm + (E < S ? E : S);
-  // expert of every block; padding of every run and of the tail
   for (int e = warp; e < E; e += kAlignWarps) {
     const int32_t b0 = blk_start[e];
     const int32_t nb = (counts[e] + bm - 1) / bm;
@@ -220,58 +198,196 @@ __global__ void __launch_bounds__(kAlignThreads, 1)
   for (int64_t b = total_blocks + threadIdx.x; b < max_blocks; b += kAlignThreads) eid[b] = -1;
   for (int64_t i = static_cast<int64_t>(total_blocks) * bm + threadIdx.x; i < max_blocks * bm; i += kAlignThreads)
     sid[i] = static_cast<int32_t>(S);
-  // pass 3: scatter in stable order
-  for (int64_t c0 = s_begin; c0 < s_end; c0 += 32 * kAlignBatch) {
-    int32_t ev[kAlignBatch];
-    load_batch(c0, ev);
+}
+
+// One CTA: count, plan, scatter.
+template <bool I64>
+__global__ void __launch_bounds__(kAlignThreads, 1)
+    align_kernel(const void* __restrict__ ids, int64_t S, int32_t E, int32_t bm, int32_t* __restrict__ sid,
+                 int32_t* __restrict__ eid, int32_t* __restrict__ npp, int32_t* dev_err) {
+  extern __shared__ int32_t sh[];
+  int32_t* hist = sh;                                  // [kAlignWarps][E]
+  int32_t* blk_start = sh + kAlignWarps * E;           // [E]
+  int32_t* counts = blk_start + E;                     // [E]
+  __shared__ typename AlignScan::TempStorage scan_tmp;
+  __shared__ int32_t total_blocks;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int id_bits = 32 - __clz(E);   // bits of e + 1 (0 = no expert), e < E
+  pdl_wait();
+  for (int i = threadIdx.x; i < kAlignWarps * E; i += kAlignThreads) hist[i] = 0;
+  __syncthreads();
+  const int64_t seg = (S + kAlignWarps - 1) / kAlignWarps;
+  const int64_t s_begin = warp * seg;
+  const int64_t s_end = s_begin + seg < S ? s_begin + seg : S;
+  warp_count<I64>(ids, s_begin, s_end, lane, E, id_bits, hist + warp * E, dev_err);
+  __syncthreads();
+  // per expert: exclusive prefix of the warps' counts, and the total
+  constexpr int kPer = kAlignMaxExperts / kAlignThreads;
 #pragma unroll
-    for (int u = 0; u < kAlignBatch; ++u) {
-      const int32_t e = ev[u];
-      const unsigned peers = equal_lanes(static_cast<uint32_t>(e + 1), id_bits);
-      int32_t base = 0;
-      if (e >= 0) base = my_hist[e];
-      __syncwarp();
-      if (e >= 0) {
-        const int rank = __popc(peers & ((1u << lane) - 1u));
-        sid[static_cast<int64_t>(blk_start[e]) * bm + base + rank] = static_cast<int32_t>(c0 + u * 32 + lane);
-        if (rank == 0) my_hist[e] = base + __popc(peers);
+  for (int j = 0; j < kPer; ++j) {
+    const int e = threadIdx.x * kPer + j;
+    if (e < E) {
+      int32_t acc = 0;
+      for (int w = 0; w < kAlignWarps; ++w) {
+        const int32_t v = hist[w * E + e];
+        hist[w * E + e] = acc;
+        acc += v;
       }
-      __syncwarp();
+      counts[e] = acc;
     }
+  }
+  plan_runs(counts, blk_start, S, E, bm, sid, eid, npp, scan_tmp, total_blocks);
+  for (int i = threadIdx.x; i < kAlignWarps * E; i += kAlignThreads) hist[i] += blk_start[i % E] * bm;
+  __syncthreads();
+  warp_scatter<I64>(ids, s_begin, s_end, lane, E, id_bits, hist + warp * E, sid, dev_err);
+  pdl_launch_dependents();
+}
+
+// Several CTAs, step 1: cnt[g][e] = slots of expert e in CTA g's segment.
+template <bool I64>
+__global__ void __launch_bounds__(kAlignThreads, 1)
+    align_count_kernel(const void* __restrict__ ids, int64_t S, int32_t E, int32_t* __restrict__ cnt,
+                       int32_t* dev_err) {
+  extern __shared__ int32_t hist[];                    // [kAlignWarps][E]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int id_bits = 32 - __clz(E);
+  pdl_wait();
+  for (int i = threadIdx.x; i < kAlignWarps * E; i += kAlignThreads) hist[i] = 0;
+  __syncthreads();
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * kAlignSeg, r1 = r0 + kAlignSeg < S ? r0 + kAlignSeg : S;
+  const int64_t s_begin = r0 + warp * (kAlignSeg / kAlignWarps);
+  const int64_t s_end = s_begin + kAlignSeg / kAlignWarps < r1 ? s_begin + kAlignSeg / kAlignWarps : r1;
+  warp_count<I64>(ids, s_begin, s_end, lane, E, id_bits, hist + warp * E, dev_err);
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += kAlignThreads) {
+    int32_t acc = 0;
+    for (int w = 0; w < kAlignWarps; ++w) acc += hist[w * E + e];
+    cnt[static_cast<int64_t>(blockIdx.x) * E + e] = acc;
   }
   pdl_launch_dependents();
 }
 
-size_t align_scratch_bytes(int64_t, int32_t) { return 0; }
+// Step 2 (one CTA): the plan, and cnt[g][e] := sorted_ids position of CTA
+// g's first slot of expert e.
+__global__ void __launch_bounds__(kAlignThreads, 1)
+    align_plan_kernel(int32_t* __restrict__ cnt, int32_t G, int64_t S, int32_t E, int32_t bm,
+                      int32_t* __restrict__ sid, int32_t* __restrict__ eid, int32_t* __restrict__ npp) {
+  extern __shared__ int32_t sh[];
+  int32_t* blk_start = sh;                             // [E]
+  int32_t* counts = sh + E;                            // [E]
+  __shared__ typename AlignScan::TempStorage scan_tmp;
+  __shared__ int32_t total_blocks;
+  pdl_wait();
+  constexpr int kPer = kAlignMaxExperts / kAlignThreads;
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int e = threadIdx.x * kPer + j;
+    if (e < E) {
+      int32_t acc = 0;
+      for (int g = 0; g < G; ++g) {
+        const int32_t v = cnt[static_cast<int64_t>(g) * E + e];
+        cnt[static_cast<int64_t>(g) * E + e] = acc;
+        acc += v;
+      }
+      counts[e] = acc;
+    }
+  }
+  plan_runs(counts, blk_start, S, E, bm, sid, eid, npp, scan_tmp, total_blocks);
+  for (int64_t i = threadIdx.x; i < static_cast<int64_t>(G) * E; i += kAlignThreads)
+    cnt[i] += blk_start[i % E] * bm;
+  pdl_launch_dependents();
+}
+
+// Step 3: each CTA scatters its segment from its run offsets.
+template <bool I64>
+__global__ void __launch_bounds__(kAlignThreads, 1)
+    align_scatter_kernel(const void* __restrict__ ids, int64_t S, int32_t E, const int32_t* __restrict__ off,
+                         int32_t* __restrict__ sid, int32_t* dev_err) {
+  extern __shared__ int32_t hist[];                    // [kAlignWarps][E]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int id_bits = 32 - __clz(E);
+  pdl_wait();
+  for (int i = threadIdx.x; i < kAlignWarps * E; i += kAlignThreads) hist[i] = 0;
+  __syncthreads();
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * kAlignSeg, r1 = r0 + kAlignSeg < S ? r0 + kAlignSeg : S;
+  const int64_t s_begin = r0 + warp * (kAlignSeg / kAlignWarps);
+  const int64_t s_end = s_begin + kAlignSeg / kAlignWarps < r1 ? s_begin + kAlignSeg / kAlignWarps : r1;
+  warp_count<I64>(ids, s_begin, s_end, lane, E, id_bits, hist + warp * E, dev_err);
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += kAlignThreads) {
+    int32_t pos = off[static_cast<int64_t>(blockIdx.x) * E + e];
+    for (int w = 0; w < kAlignWarps; ++w) {
+      const int32_t v = hist[w * E + e];
+      hist[w * E + e] = pos;
+      pos += v;
+    }
+  }
+  __syncthreads();
+  warp_scatter<I64>(ids, s_begin, s_end, lane, E, id_bits, hist + warp * E, sid, dev_err);
+  pdl_launch_dependents();
+}
+
+size_t align_scratch_bytes(int64_t S, int32_t E) {
+  if (S <= kAlignOneCta) return 0;
+  const int64_t G = (S + kAlignSeg - 1) / kAlignSeg;
+  return static_cast<size_t>((G * E * 4 + 255) / 256 * 256);
+}
 
 cudaError_t launch_align(const void* ids, bool ids64, int64_t S, int32_t E, int32_t bm, int32_t* sid, int32_t* eid,
-                         int32_t* npp, int32_t*, size_t, int32_t* dev_err, cudaStream_t st, bool pdl) {
+                         int32_t* npp, int32_t* scratch, size_t scratch_bytes, int32_t* dev_err, cudaStream_t st,
+                         bool pdl) {
   if (E > kAlignMaxExperts) return cudaErrorInvalidValue;
-  const size_t hist_bytes = static_cast<size_t>(kAlignWarps + 2) * E * sizeof(int32_t);
-  const size_t staged_bytes = hist_bytes + (static_cast<size_t>(S) * sizeof(int16_t) + 15) / 16 * 16;
-  const bool staged = staged_bytes <= static_cast<size_t>(kAlignSmemMax);
+  static bool configured[64] = {};   // per device
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
+    const void* kerns[] = {reinterpret_cast<const void*>(align_kernel<true>),
+                           reinterpret_cast<const void*>(align_kernel<false>),
+                           reinterpret_cast<const void*>(align_count_kernel<true>),
+                           reinterpret_cast<const void*>(align_count_kernel<false>),
+                           reinterpret_cast<const void*>(align_scatter_kernel<true>),
+                           reinterpret_cast<const void*>(align_scatter_kernel<false>)};
+    for (const void* k : kerns) {
+      e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kAlignSmemMax);
+      if (e != cudaSuccess) return e;
+    }
+    configured[dev] = true;
+  }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(1);
   cfg.blockDim = dim3(kAlignThreads);
-  cfg.dynamicSmemBytes = staged ? staged_bytes : hist_bytes;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  static bool configured[64][2] = {};   // per device and id width
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  auto kern = ids64 ? align_kernel<true> : align_kernel<false>;
-  if (!configured[dev][ids64]) {
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kAlignSmemMax);
-    if (e != cudaSuccess) return e;
-    configured[dev][ids64] = true;
+  const size_t hist_bytes = static_cast<size_t>(kAlignWarps) * E * sizeof(int32_t);
+  const size_t need = align_scratch_bytes(S, E);
+  if (need == 0 || !scratch || scratch_bytes < need) {
+    cfg.gridDim = dim3(1);
+    cfg.dynamicSmemBytes = hist_bytes + 2 * E * sizeof(int32_t);
+    return ids64 ? cudaLaunchKernelEx(&cfg, align_kernel<true>, ids, S, E, bm, sid, eid, npp, dev_err)
+                 : cudaLaunchKernelEx(&cfg, align_kernel<false>, ids, S, E, bm, sid, eid, npp, dev_err);
   }
-  return cudaLaunchKernelEx(&cfg, kern, ids, S, E, bm, sid, eid, npp, dev_err, staged);
+  const int32_t G = static_cast<int32_t>((S + kAlignSeg - 1) / kAlignSeg);
+  cfg.gridDim = dim3(G);
+  cfg.dynamicSmemBytes = hist_bytes;
+  e = ids64 ? cudaLaunchKernelEx(&cfg, align_count_kernel<true>, ids, S, E, scratch, dev_err)
+            : cudaLaunchKernelEx(&cfg, align_count_kernel<false>, ids, S, E, scratch, dev_err);
+  if (e != cudaSuccess) return e;
+  cfg.numAttrs = 1;   // the next two follow kernels of this library
+  cfg.gridDim = dim3(1);
+  cfg.dynamicSmemBytes = 2 * E * sizeof(int32_t);
+  e = cudaLaunchKernelEx(&cfg, align_plan_kernel, scratch, G, S, E, bm, sid, eid, npp);
+  if (e != cudaSuccess) return e;
+  cfg.gridDim = dim3(G);
+  cfg.dynamicSmemBytes = hist_bytes;
+  return ids64 ? cudaLaunchKernelEx(&cfg, align_scatter_kernel<true>, ids, S, E, static_cast<const int32_t*>(scratch),
+                                    sid, dev_err)
+               : cudaLaunchKernelEx(&cfg, align_scatter_kernel<false>, ids, S, E,
+                                    static_cast<const int32_t*>(scratch), sid, dev_err);
 }
 
 // ---------------------------------------------------------------------------

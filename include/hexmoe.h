@@ -16,7 +16,9 @@
  * Every entry point takes plain device pointers and sizes, runs on the caller's
  * stream (a cudaStream_t passed as void*, NULL = legacy default stream), makes
  * no host synchronisation and allocates no device memory: scratch is a caller
- * buffer sized by the matching *_workspace_bytes() call.  Calls are re-entrant;
+ * buffer sized by the matching *_workspace_bytes() call.  The exceptions are
+ * hexmoe_layer_create / hexmoe_layer_destroy (load time: they synchronise and
+ * own the layer's tiled index copy) and hexmoe_device_status.  Calls are re-entrant;
  * a layer handle is immutable after creation and may be shared across streams.
  * Every call returns HEXMOE_OK or an error code; hexmoe_last_error() gives the
  * message of the calling thread's last failure.
@@ -200,7 +202,10 @@ HEXMOE_API int hexmoe_combine(const void* y, int32_t y_dtype, int64_t tokens, in
  * hex_moe.py:201-222): sorted_ids int32 [max_blocks*block_m] (padding = S),
  * expert_ids int32 [max_blocks] (-1 = unused), npp int32 [1] = padded length,
  * with max_blocks = ceil(S/block_m) + min(E, S).  Stable: slots of one expert
- * keep their order, so the output equals the reference's bit for bit. */
+ * keep their order, so the output equals the reference's bit for bit.
+ * workspace: hexmoe_align_workspace_bytes(S, E) bytes (16-byte aligned; 0 for
+ * small S, where NULL is fine).  With it, large S is aligned by many CTAs;
+ * without it (NULL or too small) by one, with the same result. */
 HEXMOE_API size_t hexmoe_align_workspace_bytes(int64_t num_slots, int32_t num_experts);
 HEXMOE_API int hexmoe_align(const void* ids, int32_t ids_dtype, int64_t num_slots, int32_t num_experts,
                  int32_t block_m, int32_t* sorted_ids, int32_t* expert_ids, int32_t* npp,

@@ -145,6 +145,33 @@ def test_align_large_vs_oracle(oracle, S, E, bm):
     assert np.array_equal(npp.cpu().numpy(), want[2])
 
 
+def test_align_without_workspace_matches_with(oracle):
+    """hexmoe_align with no workspace (one CTA) and with it (several CTAs) give
+    the same plan for a batch that takes the several-CTA path."""
+    from blackhole_b200 import _lib
+    S, E, bm = 50000, 96, 128
+    g = torch.Generator().manual_seed(7)
+    ids = torch.randint(0, E, (S,), generator=g).to(DEV)
+    assert _lib.lib.hexmoe_align_workspace_bytes(S, E) > 0
+    outs = []
+    for with_ws in (False, True):
+        max_blocks = -(-S // bm) + min(E, S)
+        sid = torch.empty(max_blocks * bm, dtype=torch.int32, device=DEV)
+        eid = torch.empty(max_blocks, dtype=torch.int32, device=DEV)
+        npp = torch.empty(1, dtype=torch.int32, device=DEV)
+        nws = _lib.lib.hexmoe_align_workspace_bytes(S, E) if with_ws else 0
+        ws = torch.empty(max(nws, 1), dtype=torch.uint8, device=DEV)
+        _lib.check(_lib.lib.hexmoe_align(ids.data_ptr(), _lib.I64, S, E, bm, sid.data_ptr(), eid.data_ptr(),
+                                         npp.data_ptr(), ws.data_ptr() if with_ws else None, nws, None),
+                   "hexmoe_align")
+        torch.cuda.synchronize()
+        outs.append((sid.cpu().numpy(), eid.cpu().numpy(), npp.cpu().numpy()))
+    want = oracle.align(ids.cpu().numpy(), E, bm)
+    for got in outs:
+        for a, b in zip(got, want):
+            assert np.array_equal(a, b)
+
+
 # ----------------------------------------------------------------------------- layer
 
 
