@@ -23,7 +23,7 @@ EXPORTS = (
     "hexmoe_layer_create", "hexmoe_layer_destroy", "hexmoe_forward_workspace_bytes", "hexmoe_forward",
     "hexmoe_align_workspace_bytes", "hexmoe_align", "hexmoe_dequant", "hexmoe_route_topk",
     "hexmoe_gather", "hexmoe_gate_up", "hexmoe_down", "hexmoe_combine", "hexmoe_forward_noalloc",
-    "hexmoe_tile_index",
+    "hexmoe_tile_index", "hexmoe_combine_rows",
 )
 
 
@@ -69,6 +69,7 @@ def _load() -> ctypes.CDLL:
         "hexmoe_gate_up": (ctypes.c_int, [P, P, I32_, I64_, I32_, P, P, P, I32_, P, P]),
         "hexmoe_down": (ctypes.c_int, [P, P, I32_, I64_, I32_, P, P, P, P, I32_, P, P]),
         "hexmoe_combine": (ctypes.c_int, [P, I32_, I64_, I32_, I32_, P, I32_, P]),
+        "hexmoe_combine_rows": (ctypes.c_int, [P, I32_, I64_, I64_, I32_, I32_, P, P, I32_, P]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)

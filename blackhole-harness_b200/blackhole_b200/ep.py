@@ -19,13 +19,17 @@ Forward for the T tokens of this rank (global expert ids in topk_ids):
   5. out[t] = the k returned rows of token t summed in fp32 and rounded (the
      layer's own combine kernel on the GPU).
 Each slot goes through the same arithmetic as in the single-GPU layer, so the
-result equals the single-GPU output bit for bit.  Traffic per rank: 2 x S x H
-activation rows plus 12 bytes of metadata per slot.
+result equals the single-GPU output bit for bit (at the same block_m).  Traffic
+per rank: 2 x S x H activation rows plus 16 bytes of metadata per slot.
 
-Collectives: one all-reduce of an argument-error flag, then plain all-to-alls
-(NCCL on GPUs) with a host read of the per-rank counts (they set the split
-lists).  Every rank runs the same collectives in the same order, including ranks
-with no tokens and calls that end in an argument error.
+Collectives: plain all-to-alls (NCCL on GPUs).  The first carries each rank's
+slot count per destination and its argument-error flag, read on the host once
+(the counts set the split lists; a bad call raises on every rank before any
+data moves).  Every rank runs the same collectives in the same order, including
+ranks with no tokens and calls that end in an argument error.  On the GPU the
+local experts run as the layer's phases without its top-1 combine, and the
+returned rows are summed in slot order through a row map (hexmoe_combine_rows)
+instead of being copied back into slot order first.
 """
 
 from __future__ import annotations
@@ -99,20 +103,24 @@ class EPMoE:
 
     local_tiers: this rank's prepared HexTier list (from shard_tiers(...) then
     HexTier.prepare(num_experts)); expert_fn / combine_fn replace the CUDA layer
-    (tests run the host logic on CPU ranks with the oracle as expert_fn)."""
+    (tests run the host logic on CPU ranks with the oracle as expert_fn).
+    block_m: tile height of the local layer (0 = by the received slot count).
+    The down GEMM's accumulation order depends on it (two accumulators for
+    block_m <= 64), so EP equals a single-GPU run bit for bit at the same block_m."""
 
     def __init__(self, shard: ExpertShard, local_tiers: list | None = None, group=None,
-                 expert_fn: ExpertFn | None = None, combine_fn: CombineFn | None = None):
+                 expert_fn: ExpertFn | None = None, combine_fn: CombineFn | None = None, block_m: int = 0):
         self.shard = shard
+        self.block_m = block_m
         self.group = group
         self.local_tiers = local_tiers
         self._layer = None
         if expert_fn is None:
             if local_tiers is None:
                 raise ValueError("EPMoE needs the local tiers or an expert_fn")
-            from blackhole_b200.hex_moe import hex_moe, layer_for
+            from blackhole_b200.hex_moe import layer_for
             self._layer = layer_for(local_tiers)
-            expert_fn = lambda xr, wr, ir: hex_moe(xr, wr[:, None], ir[:, None], local_tiers)  # noqa: E731
+            expert_fn = self._local_phases
             if combine_fn is None:
                 combine_fn = lambda y, T, k: self._layer.combine(y, T, k)  # noqa: E731
         self.expert_fn = expert_fn
@@ -121,29 +129,45 @@ class EPMoE:
     def _a2a(self, out: torch.Tensor, inp: torch.Tensor, out_splits: list[int], in_splits: list[int]) -> None:
         dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
 
+    def _local_phases(self, xr: torch.Tensor, wr: torch.Tensor, ir: torch.Tensor) -> torch.Tensor:
+        """The local experts on the received rows, one slot per row: the layer's
+        plan / gather / gate-up / down phases; the per-slot rows `y` (weighted,
+        rounded to the activation dtype) are the result, so the layer's top-1
+        combine (a copy) is skipped."""
+        from blackhole_b200.hex_moe import auto_block_m
+        L = self._layer
+        n = xr.shape[0]
+        bm = self.block_m or auto_block_m(n, L.E)
+        plan = L.plan(ir, bm)
+        xs = L.gather(xr, 1, plan, bm)
+        act = L.gate_up(xs, n, 1, plan, bm)
+        return L.down(act, wr.reshape(n, 1), plan, bm)
+
     def forward(self, x: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.Tensor) -> torch.Tensor:
         if x.dim() != 2 or topk_ids.dim() != 2 or topk_weights.shape != topk_ids.shape or x.shape[0] != topk_ids.shape[0]:
             raise ValueError("x [T, H], topk_weights and topk_ids [T, k] expected")
         T, k = topk_ids.shape
         H = x.shape[1]
         dev = x.device
-        world = self.shard.world
+        world, E = self.shard.world, self.shard.num_experts
         ids = topk_ids.reshape(-1).to(torch.int64)
         w = topk_weights.reshape(-1).to(torch.float32)
-        # argument errors are agreed on by every rank before any data moves, so a
-        # bad rank never leaves the others waiting inside a collective
-        bad = bool(ids.numel()) and (int(ids.min()) < 0 or int(ids.max()) >= self.shard.num_experts)
-        flag = torch.tensor([1 if bad else 0], dtype=torch.int64, device=dev)
-        dist.all_reduce(flag, op=dist.ReduceOp.MAX, group=self.group)
-        if int(flag.item()):
-            raise ValueError("topk_ids out of range" if bad else "topk_ids out of range on another rank")
-        owner = self.shard.owner(ids)
-        order = torch.argsort(owner, stable=True)
+        # 1. per destination rank: slot count and this rank's argument-error flag,
+        #    exchanged in one all-to-all and read on the host once, so a bad call
+        #    fails on every rank before any data moves
+        bad = ((ids < 0) | (ids >= E)).any().to(torch.int64)
+        owner = self.shard.owner(ids.clamp(0, max(E - 1, 0)))
         send_counts = torch.bincount(owner, minlength=world).to(torch.int64)
-        recv_counts = torch.empty_like(send_counts)
-        dist.all_to_all_single(recv_counts, send_counts, group=self.group)
-        sc, rc = send_counts.tolist(), recv_counts.tolist()
+        info = torch.stack([send_counts, bad.expand(world)], 1).contiguous()
+        recv_info = torch.empty_like(info)
+        dist.all_to_all_single(recv_info, info, group=self.group)
+        host = torch.cat([send_counts, recv_info.reshape(-1)]).tolist()
+        sc, rc, flags = host[:world], host[world::2], host[world + 1::2]
+        if any(flags):
+            mine = flags[dist.get_rank(self.group)]
+            raise ValueError("topk_ids out of range" if mine else "topk_ids out of range on another rank")
         n_recv = sum(rc)
+        order = torch.argsort(owner, stable=True)
         # 2. token rows, ids and weights of the slots, grouped by owner
         send_x = x.index_select(0, torch.div(order, k, rounding_mode="floor"))
         recv_x = torch.empty(n_recv, H, dtype=x.dtype, device=dev)
@@ -154,18 +178,24 @@ class EPMoE:
         recv_ids = recv_meta[:, 0].contiguous()
         recv_w = recv_meta[:, 1].to(torch.int32).view(torch.float32).contiguous()
         # 3. local experts, one slot per row
+        out_dt = x.dtype if x.dtype in (torch.bfloat16, torch.float16) else torch.bfloat16
         if n_recv:
-            y_recv = self.expert_fn(recv_x, recv_w, recv_ids)
+            y_recv = (self._local_phases(recv_x, recv_w, recv_ids) if self._layer is not None
+                      else self.expert_fn(recv_x, recv_w, recv_ids)).to(out_dt).contiguous()
         else:
-            y_recv = torch.empty(0, H, dtype=x.dtype, device=dev)
+            y_recv = torch.empty(0, H, dtype=out_dt, device=dev)
         # 4. rows back to their source rank, in the order they were sent
-        back = torch.empty(T * k, H, dtype=x.dtype, device=dev)
-        self._a2a(back, y_recv.to(x.dtype).contiguous(), sc, rc)
-        y = torch.empty_like(back)
-        y.index_copy_(0, order, back)
-        # 5. combine the k slots of each token
+        back = torch.empty(T * k, H, dtype=out_dt, device=dev)
+        self._a2a(back, y_recv, sc, rc)
         if T == 0:
             return torch.empty(0, H, dtype=x.dtype, device=dev)
-        return self.combine_fn(y, T, k)
+        # 5. combine the k slots of each token: slot order[i] came back as row i
+        if self._layer is not None:
+            rows = torch.empty(T * k, dtype=torch.int32, device=dev)
+            rows.index_copy_(0, order, torch.arange(T * k, dtype=torch.int32, device=dev))
+            return self._layer.combine_rows(back, T, k, rows, out_dtype=x.dtype)
+        y = torch.empty_like(back)
+        y.index_copy_(0, order, back)
+        return self.combine_fn(y, T, k).to(x.dtype)
 
     __call__ = forward

@@ -262,6 +262,29 @@ class _Layer:
         _lib.check(rc, "hexmoe_combine")
         return out
 
+    def combine_rows(self, y: torch.Tensor, T: int, k: int, rows: torch.Tensor, out_dtype=None) -> torch.Tensor:
+        """out[t] = sum_j y[rows[t*k + j]] (hexmoe_combine_rows): the combine of
+        per-slot rows held in another order."""
+        if rows.dtype != torch.int32 or rows.numel() != T * k:
+            raise ValueError("rows must be int32 [T * k]")
+        out = torch.empty(T, self.H, dtype=out_dtype or y.dtype, device=y.device)
+        y, rows = _aligned(y), rows.contiguous()
+        with torch.cuda.device(y.device):
+            rc = _lib.lib.hexmoe_combine_rows(_ptr(y), _DT[y.dtype], y.shape[0], T, k, self.H, _ptr(rows), _ptr(out),
+                                              _DT[out.dtype], _stream(y.device))
+        _lib.check(rc, "hexmoe_combine_rows")
+        return out
+
+
+def auto_block_m(slots: int, num_experts: int) -> int:
+    """The block_m hexmoe_forward picks when given 0 (api.cu auto_block_m): the
+    smallest of 16/32/64/128 covering the mean slots per expert."""
+    avg = -(-slots // max(num_experts, 1))
+    for bm in (16, 32, 64):
+        if avg <= bm:
+            return bm
+    return 128
+
 
 def _layer(tiers: list[HexTier]) -> _Layer:
     key = tuple((id(t), _ptr(t.kernel_parts["gate_proj"]["idx"])) for t in tiers)

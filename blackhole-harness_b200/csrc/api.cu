@@ -445,7 +445,8 @@ int hexmoe_forward(const hexmoe_layer* layer, const void* x, int32_t x_dtype, in
   if (rc) return rc;
 
   // ---- combine
-  e = launch_combine(y, bf16 ? HEXMOE_BF16 : HEXMOE_F16, tokens, topk, d.hidden, d.hidden, out, out_dtype, st, true);
+  e = launch_combine(y, bf16 ? HEXMOE_BF16 : HEXMOE_F16, tokens, topk, d.hidden, d.hidden, nullptr, S, out, out_dtype,
+                     st, true);
   if (e != cudaSuccess) return cuda_fail(e, "combine launch");
   return HEXMOE_OK;
 }
@@ -500,9 +501,24 @@ int hexmoe_combine(const void* y, int32_t y_dtype, int64_t tokens, int32_t topk,
   if (tokens == 0) return HEXMOE_OK;
   if (!y || !out || reinterpret_cast<uintptr_t>(y) % 16 || reinterpret_cast<uintptr_t>(out) % 16)
     return fail(HEXMOE_E_ARG, "combine: y / out must be non-null and 16-byte aligned");
-  cudaError_t e = launch_combine(y, y_dtype, tokens, topk, hidden, hidden, out, out_dtype,
+  cudaError_t e = launch_combine(y, y_dtype, tokens, topk, hidden, hidden, nullptr, tokens * topk, out, out_dtype,
                                  static_cast<cudaStream_t>(stream), false);
   if (e != cudaSuccess) return cuda_fail(e, "combine launch");
+  return HEXMOE_OK;
+}
+
+int hexmoe_combine_rows(const void* y, int32_t y_dtype, int64_t y_rows, int64_t tokens, int32_t topk, int32_t hidden,
+                        const int32_t* rows, void* out, int32_t out_dtype, void* stream) {
+  if (y_dtype != HEXMOE_BF16 && y_dtype != HEXMOE_F16) return fail(HEXMOE_E_DTYPE, "y dtype must be BF16 or F16");
+  if (check_dtype16(out_dtype, "out")) return HEXMOE_E_DTYPE;
+  if (tokens < 0 || topk <= 0 || hidden <= 0 || hidden % 8 || y_rows < 0)
+    return fail(HEXMOE_E_ARG, "combine_rows: tokens / topk / hidden / y_rows");
+  if (tokens == 0) return HEXMOE_OK;
+  if (!y || !out || !rows || reinterpret_cast<uintptr_t>(y) % 16 || reinterpret_cast<uintptr_t>(out) % 16)
+    return fail(HEXMOE_E_ARG, "combine_rows: y / rows / out must be non-null, y and out 16-byte aligned");
+  cudaError_t e = launch_combine(y, y_dtype, tokens, topk, hidden, hidden, rows, y_rows, out, out_dtype,
+                                 static_cast<cudaStream_t>(stream), false);
+  if (e != cudaSuccess) return cuda_fail(e, "combine_rows launch");
   return HEXMOE_OK;
 }
 

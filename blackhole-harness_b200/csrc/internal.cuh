@@ -85,8 +85,9 @@ size_t align_scratch_bytes(int64_t S, int32_t E);
 cudaError_t launch_dequant(const hexmoe_parts& parts, int bits, int block, int n, int rows, int cols, int rows_pad,
                            int cols_pad, const int32_t* experts, void* out, int out_dtype, int64_t stride_e,
                            int64_t stride_row, int64_t row_off, cudaStream_t st);
-cudaError_t launch_combine(const void* y, int y_dtype, int64_t T, int32_t topk, int32_t H, int64_t ld_y, void* out,
-                           int out_dtype, cudaStream_t st, bool pdl);
+// rows: optional [T*topk] map of y rows (nullptr: row t*topk + j), y_rows: rows of y.
+cudaError_t launch_combine(const void* y, int y_dtype, int64_t T, int32_t topk, int32_t H, int64_t ld_y,
+                           const int32_t* rows, int64_t y_rows, void* out, int out_dtype, cudaStream_t st, bool pdl);
 // Tiled copy of one idx stack (hexmoe_tile_index layout).
 cudaError_t launch_tile_index(const uint32_t* idx, int bits, int n, int rows_pad, int cols_pad, uint32_t* out,
                               cudaStream_t st);

@@ -503,10 +503,13 @@ cudaError_t launch_tile_index(const uint32_t* idx, int bits, int n, int rows_pad
 
 // ---------------------------------------------------------------------------
 // Combine (runtime/blackhole_runtime/hex_moe.py:325, y.view(T, k, H).sum(1)):
-// out[t, h] = sum_j y[t*k + j, h], fp32 accumulation in slot order.
+// out[t, h] = sum_j y[r(t, j), h], fp32 accumulation in slot order, with
+// r(t, j) = t*k + j, or rows[t*k + j] when a row map is given (the expert-
+// parallel combine, whose rows come back in dispatch order); a mapped row
+// outside 0..y_rows-1 adds nothing and sets the error word.
 template <typename YT, int OUT>
 __global__ void combine_kernel(const YT* __restrict__ y, int64_t T, int32_t k, int32_t H, int64_t ld_y,
-                               void* __restrict__ out) {
+                               const int32_t* __restrict__ rows, int64_t y_rows, void* __restrict__ out) {
   pdl_wait();
   const int hv = H / 8;
   const int64_t total = T * hv;
@@ -516,7 +519,15 @@ __global__ void combine_kernel(const YT* __restrict__ y, int64_t T, int32_t k, i
     const int h8 = static_cast<int>(i % hv) * 8;
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     for (int j = 0; j < k; ++j) {
-      const uint4 v = *reinterpret_cast<const uint4*>(y + (t * k + j) * ld_y + h8);
+      int64_t r = t * k + j;
+      if (rows) {
+        r = __ldg(rows + r);
+        if (r < 0 || r >= y_rows) {
+          if (h8 == 0) atomicOr(&g_dev_err, kDevErrExpertId);
+          continue;
+        }
+      }
+      const uint4 v = *reinterpret_cast<const uint4*>(y + r * ld_y + h8);
       const YT* e = reinterpret_cast<const YT*>(&v);
 #pragma unroll
       for (int q = 0; q < 8; ++q) acc[q] += static_cast<float>(e[q]);
@@ -537,8 +548,9 @@ __global__ void combine_kernel(const YT* __restrict__ y, int64_t T, int32_t k, i
 }
 
 template <typename YT>
-static cudaError_t combine_dispatch(const YT* y, int64_t T, int32_t k, int32_t H, int64_t ld_y, void* out,
-                                    int out_dtype, cudaStream_t st, bool pdl) {
+static cudaError_t combine_dispatch(const YT* y, int64_t T, int32_t k, int32_t H, int64_t ld_y,
+                                    const int32_t* rows, int64_t y_rows, void* out, int out_dtype, cudaStream_t st,
+                                    bool pdl) {
   const int64_t total = T * (H / 8);
   if (total == 0) return cudaSuccess;
   const int threads = 256;
@@ -552,17 +564,19 @@ static cudaError_t combine_dispatch(const YT* y, int64_t T, int32_t k, int32_t H
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  if (out_dtype == HEXMOE_F32) return cudaLaunchKernelEx(&cfg, combine_kernel<YT, HEXMOE_F32>, y, T, k, H, ld_y, out);
+  if (out_dtype == HEXMOE_F32)
+    return cudaLaunchKernelEx(&cfg, combine_kernel<YT, HEXMOE_F32>, y, T, k, H, ld_y, rows, y_rows, out);
   if (out_dtype == HEXMOE_BF16)
-    return cudaLaunchKernelEx(&cfg, combine_kernel<YT, HEXMOE_BF16>, y, T, k, H, ld_y, out);
-  return cudaLaunchKernelEx(&cfg, combine_kernel<YT, HEXMOE_F16>, y, T, k, H, ld_y, out);
+    return cudaLaunchKernelEx(&cfg, combine_kernel<YT, HEXMOE_BF16>, y, T, k, H, ld_y, rows, y_rows, out);
+  return cudaLaunchKernelEx(&cfg, combine_kernel<YT, HEXMOE_F16>, y, T, k, H, ld_y, rows, y_rows, out);
 }
 
-cudaError_t launch_combine(const void* y, int y_dtype, int64_t T, int32_t topk, int32_t H, int64_t ld_y, void* out,
-                           int out_dtype, cudaStream_t st, bool pdl) {
+cudaError_t launch_combine(const void* y, int y_dtype, int64_t T, int32_t topk, int32_t H, int64_t ld_y,
+                           const int32_t* rows, int64_t y_rows, void* out, int out_dtype, cudaStream_t st, bool pdl) {
   if (y_dtype == HEXMOE_BF16)
-    return combine_dispatch(static_cast<const __nv_bfloat16*>(y), T, topk, H, ld_y, out, out_dtype, st, pdl);
-  return combine_dispatch(static_cast<const __half*>(y), T, topk, H, ld_y, out, out_dtype, st, pdl);
+    return combine_dispatch(static_cast<const __nv_bfloat16*>(y), T, topk, H, ld_y, rows, y_rows, out, out_dtype, st,
+                            pdl);
+  return combine_dispatch(static_cast<const __half*>(y), T, topk, H, ld_y, rows, y_rows, out, out_dtype, st, pdl);
 }
 
 // ---------------------------------------------------------------------------

@@ -198,6 +198,15 @@ HEXMOE_API int hexmoe_down(const hexmoe_layer* layer, const void* act, int32_t a
 HEXMOE_API int hexmoe_combine(const void* y, int32_t y_dtype, int64_t tokens, int32_t topk, int32_t hidden,
                               void* out, int32_t out_dtype, void* stream);
 
+/* The combine with the slot rows given by a map: out[t, h] = sum_j
+ * y[rows[t*topk + j], h] (fp32 sum in j order, rounded once), for per-slot
+ * rows that come back from expert-parallel ranks in dispatch order rather than
+ * slot order.  y [y_rows, hidden]; a row index outside 0..y_rows-1 adds nothing
+ * and sets the device error word. */
+HEXMOE_API int hexmoe_combine_rows(const void* y, int32_t y_dtype, int64_t y_rows, int64_t tokens, int32_t topk,
+                                   int32_t hidden, const int32_t* rows, void* out, int32_t out_dtype,
+                                   void* stream);
+
 /* Group slots by expert, each expert's run padded to block_m (align,
  * hex_moe.py:201-222): sorted_ids int32 [max_blocks*block_m] (padding = S),
  * expert_ids int32 [max_blocks] (-1 = unused), npp int32 [1] = padded length,

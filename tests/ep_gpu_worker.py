@@ -34,13 +34,14 @@ def main() -> int:
                          for t in ts]
         full = mk(L.tiers)
         shard = ExpertShard(E, rank, world)
-        ep = EPMoE(shard, mk(shard_tiers(L.tiers, shard)))
+        ep = EPMoE(shard, mk(shard_tiers(L.tiers, shard)), block_m=16)
         for T, zipf in ((48 + 16 * rank, None), (96, 1.2), (0 if rank == world - 1 else 8, None)):
             w, ids = hd.synth_routing(T, E, K, seed=11 + rank, zipf=zipf, device=dev)
             x = hd.synth_x(T, H, seed=21 + rank, device=dev)
             got = ep(x, w, ids)
             # the single-GPU layer, one slot per row (the EP path's arithmetic), then the same combine
-            want_slots = hex_moe(x.repeat_interleave(K, 0), w.reshape(-1, 1), ids.reshape(-1, 1), full)
+            want_slots = hex_moe(x.repeat_interleave(K, 0), w.reshape(-1, 1), ids.reshape(-1, 1), full,
+                                 {"BLOCK_M": 16})
             want = ep.combine_fn(want_slots, T, K) if T else want_slots
             torch.cuda.synchronize()
             if not torch.equal(got, want):

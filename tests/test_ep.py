@@ -128,6 +128,41 @@ def hexoracle_round(a):
     return hexoracle.round_bf16(a)
 
 
+def _bad_id_worker(rank: int, world: int, port: int, out_q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from blackhole_b200.ep import EPMoE, ExpertShard
+        ep = EPMoE(ExpertShard(E, rank, world), expert_fn=lambda xr, wr, ir: xr)
+        x, w, ids = _tokens(rank, 6)
+        if rank == 1:
+            ids = ids.clone()
+            ids[2, 1] = E                      # out of range on this rank only
+        try:
+            ep(x, w, ids)
+            out_q.put((rank, "no error"))
+        except ValueError as e:
+            out_q.put((rank, str(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_out_of_range_id_raises_on_every_rank():
+    """A bad expert id on one rank ends the call with ValueError on every rank,
+    before any token row moves (the flag rides on the count exchange)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_bad_id_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=240) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+    assert res[1] == "topk_ids out of range"
+    assert res[0] == "topk_ids out of range on another rank"
+
+
 def test_shard_tiers_partition_the_experts():
     from blackhole_b200.ep import ExpertShard, shard_tiers
     L = _layer()
