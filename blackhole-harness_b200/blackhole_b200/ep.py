@@ -20,7 +20,7 @@ Forward for the T tokens of this rank (global expert ids in topk_ids):
      layer's own combine kernel on the GPU).
 Each slot goes through the same arithmetic as in the single-GPU layer, so the
 result equals the single-GPU output bit for bit (at the same block_m).  Traffic
-per rank: 2 x S x H activation rows plus 16 bytes of metadata per slot.
+per rank: 2 x S x H activation rows plus 8 bytes of metadata per slot.
 
 Collectives: plain all-to-alls (NCCL on GPUs).  The first carries each rank's
 slot count per destination and its argument-error flag, read on the host once
@@ -129,6 +129,16 @@ class EPMoE:
     def _a2a(self, out: torch.Tensor, inp: torch.Tensor, out_splits: list[int], in_splits: list[int]) -> None:
         dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
 
+    def _by_owner(self, owner: torch.Tensor) -> torch.Tensor:
+        """Slot ids ordered by owner rank, stable (slots of one rank keep their
+        order): on the GPU the layer's own align with the ranks as the experts and
+        runs of one slot, elsewhere a stable sort (the same order)."""
+        if owner.is_cuda and owner.numel():
+            from blackhole_b200.hex_moe import align
+            sid, _, _ = align(owner.to(torch.int32), self.shard.world, 1)
+            return sid[:owner.numel()].to(torch.int64)
+        return torch.argsort(owner, stable=True)
+
     def _local_phases(self, xr: torch.Tensor, wr: torch.Tensor, ir: torch.Tensor) -> torch.Tensor:
         """The local experts on the received rows, one slot per row: the layer's
         plan / gather / gate-up / down phases; the per-slot rows `y` (weighted,
@@ -157,7 +167,8 @@ class EPMoE:
         #    fails on every rank before any data moves
         bad = ((ids < 0) | (ids >= E)).any().to(torch.int64)
         owner = self.shard.owner(ids.clamp(0, max(E - 1, 0)))
-        send_counts = torch.bincount(owner, minlength=world).to(torch.int64)
+        # (torch.bincount would read its input's maximum on the host: a second sync)
+        send_counts = (owner.unsqueeze(1) == torch.arange(world, device=dev)).sum(0, dtype=torch.int64)
         info = torch.stack([send_counts, bad.expand(world)], 1).contiguous()
         recv_info = torch.empty_like(info)
         dist.all_to_all_single(recv_info, info, group=self.group)
@@ -167,16 +178,17 @@ class EPMoE:
             mine = flags[dist.get_rank(self.group)]
             raise ValueError("topk_ids out of range" if mine else "topk_ids out of range on another rank")
         n_recv = sum(rc)
-        order = torch.argsort(owner, stable=True)
+        order = self._by_owner(owner)
         # 2. token rows, ids and weights of the slots, grouped by owner
         send_x = x.index_select(0, torch.div(order, k, rounding_mode="floor"))
         recv_x = torch.empty(n_recv, H, dtype=x.dtype, device=dev)
         self._a2a(recv_x, send_x, rc, sc)
-        meta = torch.stack([ids.index_select(0, order), w.index_select(0, order).view(torch.int32).to(torch.int64)], 1)
-        recv_meta = torch.empty(n_recv, 2, dtype=torch.int64, device=dev)
+        # expert id (high word) and top-k weight bits (low word) of each slot, one int64
+        meta = ((ids << 32) | (w.view(torch.int32).to(torch.int64) & 0xFFFFFFFF)).index_select(0, order)
+        recv_meta = torch.empty(n_recv, dtype=torch.int64, device=dev)
         self._a2a(recv_meta, meta, rc, sc)
-        recv_ids = recv_meta[:, 0].contiguous()
-        recv_w = recv_meta[:, 1].to(torch.int32).view(torch.float32).contiguous()
+        recv_ids = (recv_meta >> 32).to(torch.int32)
+        recv_w = (recv_meta & 0xFFFFFFFF).to(torch.int32).view(torch.float32)
         # 3. local experts, one slot per row
         out_dt = x.dtype if x.dtype in (torch.bfloat16, torch.float16) else torch.bfloat16
         if n_recv:

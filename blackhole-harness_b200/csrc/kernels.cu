@@ -284,10 +284,16 @@ __global__ void __launch_bounds__(kAlignThreads, 1)
     const int e = threadIdx.x * kPer + j;
     if (e < E) {
       int32_t acc = 0;
-      for (int g = 0; g < G; ++g) {
-        const int32_t v = cnt[static_cast<int64_t>(g) * E + e];
-        cnt[static_cast<int64_t>(g) * E + e] = acc;
-        acc += v;
+      for (int g0 = 0; g0 < G; g0 += 16) {
+        // sixteen CTAs' counts loaded before any is rewritten: loads in flight, not one at a time
+        int32_t v[16];
+#pragma unroll
+        for (int u = 0; u < 16; ++u) v[u] = g0 + u < G ? cnt[static_cast<int64_t>(g0 + u) * E + e] : 0;
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+          if (g0 + u < G) cnt[static_cast<int64_t>(g0 + u) * E + e] = acc;
+          acc += v[u];
+        }
       }
       counts[e] = acc;
     }
