@@ -23,7 +23,7 @@ EXPORTS = (
     "hexmoe_layer_create", "hexmoe_layer_destroy", "hexmoe_forward_workspace_bytes", "hexmoe_forward",
     "hexmoe_align_workspace_bytes", "hexmoe_align", "hexmoe_dequant", "hexmoe_route_topk",
     "hexmoe_gather", "hexmoe_gate_up", "hexmoe_down", "hexmoe_combine", "hexmoe_forward_noalloc",
-    "hexmoe_tile_index", "hexmoe_combine_rows",
+    "hexmoe_tile_index", "hexmoe_combine_rows", "hexmoe_forward_slots",
 )
 
 
@@ -59,6 +59,7 @@ def _load() -> ctypes.CDLL:
         "hexmoe_forward_workspace_bytes": (SZ, [P, I64_, I32_, I32_, I32_]),
         "hexmoe_forward": (ctypes.c_int, [P, P, I32_, I64_, I32_, P, P, I32_, P, I32_, I32_, P, SZ, P]),
         "hexmoe_forward_noalloc": (ctypes.c_int, [P, P, I32_, I64_, I32_, P, P, I32_, P, I32_, I32_, P]),
+        "hexmoe_forward_slots": (ctypes.c_int, [P, P, I32_, I64_, I32_, P, P, I32_, P, I32_, P, SZ, P]),
         "hexmoe_align_workspace_bytes": (SZ, [I64_, I32_]),
         "hexmoe_align": (ctypes.c_int, [P, I32_, I64_, I32_, I32_, P, P, P, P, SZ, P]),
         "hexmoe_dequant": (ctypes.c_int, [P, I32_, I32_, I32_, I32_, I32_, I32_, I32_, P, P, I32_, I64_, I64_, I64_,

@@ -140,18 +140,11 @@ class EPMoE:
         return torch.argsort(owner, stable=True)
 
     def _local_phases(self, xr: torch.Tensor, wr: torch.Tensor, ir: torch.Tensor) -> torch.Tensor:
-        """The local experts on the received rows, one slot per row: the layer's
-        plan / gather / gate-up / down phases; the per-slot rows `y` (weighted,
-        rounded to the activation dtype) are the result, so the layer's top-1
-        combine (a copy) is skipped."""
-        from blackhole_b200.hex_moe import auto_block_m
-        L = self._layer
+        """The local experts on the received rows, one slot per row: the layer
+        forward up to the per-slot rows (weighted, rounded to the activation
+        dtype) in one call, so the layer's top-1 combine (a copy) is skipped."""
         n = xr.shape[0]
-        bm = self.block_m or auto_block_m(n, L.E)
-        plan = L.plan(ir, bm)
-        xs = L.gather(xr, 1, plan, bm)
-        act = L.gate_up(xs, n, 1, plan, bm)
-        return L.down(act, wr.reshape(n, 1), plan, bm)
+        return self._layer.forward_slots(xr, wr.reshape(n, 1), ir.reshape(n, 1), self.block_m)
 
     def forward(self, x: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.Tensor) -> torch.Tensor:
         if x.dim() != 2 or topk_ids.dim() != 2 or topk_weights.shape != topk_ids.shape or x.shape[0] != topk_ids.shape[0]:

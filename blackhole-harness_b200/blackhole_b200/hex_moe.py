@@ -210,6 +210,32 @@ class _Layer:
         return out
 
 
+    def forward_slots(self, x: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.Tensor,
+                      block_m: int = 0) -> torch.Tensor:
+        """forward() without the combine: the weighted per-slot rows [T * k, H]
+        (16-bit: x's dtype, bf16 for fp32 x), in slot order (hexmoe_forward_slots)."""
+        T, k = topk_ids.shape
+        if x.device != self.device or x.dim() != 2 or x.shape != (T, self.H) or topk_weights.shape != (T, k):
+            raise ValueError("x [T, H] on the layer's device, topk_weights / topk_ids [T, k] expected")
+        if x.dtype not in _DT:
+            raise ValueError(f"unsupported activation dtype {x.dtype}")
+        x = _aligned(x)
+        w = _aligned(topk_weights.to(torch.float32))
+        ids = _aligned(topk_ids if topk_ids.dtype in (torch.int32, torch.int64) else topk_ids.long())
+        y = torch.empty(T * k, self.H, dtype=torch.float16 if x.dtype == torch.float16 else torch.bfloat16,
+                        device=x.device)
+        if T == 0:
+            return y
+        xdt = _DT[x.dtype]
+        nbytes = _lib.lib.hexmoe_forward_workspace_bytes(self.handle, T, k, block_m, xdt)
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
+        with torch.cuda.device(x.device):
+            rc = _lib.lib.hexmoe_forward_slots(self.handle, _ptr(x), xdt, T, k, _ptr(w), _ptr(ids),
+                                               _lib.I64 if ids.dtype == torch.int64 else _lib.I32, _ptr(y), block_m,
+                                               _ptr(ws), nbytes, _stream(x.device))
+        _lib.check(rc, "hexmoe_forward_slots")
+        return y
+
     # -- the phases of forward(), for callers that time or drive them apart
     def plan(self, topk_ids: torch.Tensor, block_m: int):
         return align(topk_ids.reshape(-1), self.E, block_m)

@@ -396,18 +396,25 @@ size_t hexmoe_forward_workspace_bytes(const hexmoe_layer* layer, int64_t tokens,
   return ws_layout(layer->desc, tokens, topk, bm, x_dtype).total;
 }
 
-int hexmoe_forward(const hexmoe_layer* layer, const void* x, int32_t x_dtype, int64_t tokens, int32_t topk,
-                   const float* topk_weights, const void* topk_ids, int32_t ids_dtype, void* out, int32_t out_dtype,
-                   int32_t block_m, void* workspace, size_t workspace_bytes, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// hexmoe_forward, or with slots_out its per-slot rows instead of the combine.
+int forward_impl(const hexmoe_layer* layer, const void* x, int32_t x_dtype, int64_t tokens, int32_t topk,
+                 const float* topk_weights, const void* topk_ids, int32_t ids_dtype, void* out, int32_t out_dtype,
+                 void* slots_out, int32_t block_m, void* workspace, size_t workspace_bytes, void* stream) {
   if (!layer) return fail(HEXMOE_E_ARG, "hexmoe_forward: null layer");
   const hexmoe_layer_desc& d = layer->desc;
   if (tokens < 0 || topk <= 0 || topk > d.num_experts) return fail(HEXMOE_E_ARG, "tokens %lld / topk %d", static_cast<long long>(tokens), topk);
   if (int rc = check_dtype16(x_dtype, "x")) return rc;
   if (int rc = check_dtype16(out_dtype, "out")) return rc;
-  if (out_dtype != x_dtype && out_dtype != HEXMOE_F32) return fail(HEXMOE_E_DTYPE, "out dtype must be x dtype or f32");
+  if (!slots_out && out_dtype != x_dtype && out_dtype != HEXMOE_F32)
+    return fail(HEXMOE_E_DTYPE, "out dtype must be x dtype or f32");
   if (ids_dtype != HEXMOE_I32 && ids_dtype != HEXMOE_I64) return fail(HEXMOE_E_DTYPE, "ids dtype %d", ids_dtype);
   if (tokens == 0) return HEXMOE_OK;
   if (!x || !topk_weights || !topk_ids || !out || !workspace) return fail(HEXMOE_E_ARG, "hexmoe_forward: null pointer");
+  if (slots_out && reinterpret_cast<uintptr_t>(slots_out) % 16) return fail(HEXMOE_E_ARG, "y must be 16-byte aligned");
   if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(out) % 16 ||
       reinterpret_cast<uintptr_t>(workspace) % 256)
     return fail(HEXMOE_E_ARG, "x / out must be 16-byte and workspace 256-byte aligned");
@@ -429,7 +436,7 @@ int hexmoe_forward(const hexmoe_layer* layer, const void* x, int32_t x_dtype, in
   int32_t* eid = reinterpret_cast<int32_t*>(ws + w.eid);
   int32_t* npp = reinterpret_cast<int32_t*>(ws + w.npp);
   void* act = ws + w.act;
-  void* y = ws + w.y;
+  void* y = slots_out ? slots_out : ws + w.y;
   const bool bf16 = x_dtype != HEXMOE_F16;     // f32 activations are computed in bf16
   void* xs = ws + w.xs;
   cudaError_t e = launch_align(topk_ids, ids_dtype == HEXMOE_I64, S, d.num_experts, bm, sid, eid, npp,
@@ -443,12 +450,32 @@ int hexmoe_forward(const hexmoe_layer* layer, const void* x, int32_t x_dtype, in
   if (rc) return rc;
   rc = run_down(layer, act, bf16, tokens, topk, topk_weights, sid, eid, npp, bm, y, dev_err, st, true);
   if (rc) return rc;
+  if (slots_out) return HEXMOE_OK;
 
   // ---- combine
   e = launch_combine(y, bf16 ? HEXMOE_BF16 : HEXMOE_F16, tokens, topk, d.hidden, d.hidden, nullptr, S, out, out_dtype,
                      st, true);
   if (e != cudaSuccess) return cuda_fail(e, "combine launch");
   return HEXMOE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int hexmoe_forward(const hexmoe_layer* layer, const void* x, int32_t x_dtype, int64_t tokens, int32_t topk,
+                   const float* topk_weights, const void* topk_ids, int32_t ids_dtype, void* out, int32_t out_dtype,
+                   int32_t block_m, void* workspace, size_t workspace_bytes, void* stream) {
+  return forward_impl(layer, x, x_dtype, tokens, topk, topk_weights, topk_ids, ids_dtype, out, out_dtype, nullptr,
+                      block_m, workspace, workspace_bytes, stream);
+}
+
+int hexmoe_forward_slots(const hexmoe_layer* layer, const void* x, int32_t x_dtype, int64_t tokens, int32_t topk,
+                         const float* topk_weights, const void* topk_ids, int32_t ids_dtype, void* y,
+                         int32_t block_m, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!y && tokens > 0) return fail(HEXMOE_E_ARG, "hexmoe_forward_slots: null y");
+  return forward_impl(layer, x, x_dtype, tokens, topk, topk_weights, topk_ids, ids_dtype, y,
+                      x_dtype == HEXMOE_F16 ? HEXMOE_F16 : HEXMOE_BF16, y, block_m, workspace, workspace_bytes, stream);
 }
 
 int hexmoe_gather(const void* x, int32_t x_dtype, int64_t tokens, int32_t hidden, int32_t topk, int32_t num_experts,

@@ -153,6 +153,17 @@ HEXMOE_API int hexmoe_forward(const hexmoe_layer* layer, const void* x, int32_t 
                    int32_t ids_dtype, void* out, int32_t out_dtype, int32_t block_m,
                    void* workspace, size_t workspace_bytes, void* stream);
 
+/* hexmoe_forward up to, not including, the combine: y[t*topk + j, :] =
+ * w[t, j] * down_e(silu(gate_e x_t) * up_e x_t) rounded to the 16-bit compute
+ * type (x_dtype, BF16 for F32 x), one row per slot in slot order.  The
+ * expert-parallel path (blackhole_b200.ep) runs its received rows through this
+ * at topk = 1 and sums them on their source rank.  Same workspace as
+ * hexmoe_forward. */
+HEXMOE_API int hexmoe_forward_slots(const hexmoe_layer* layer, const void* x, int32_t x_dtype, int64_t tokens,
+                                    int32_t topk, const float* topk_weights, const void* topk_ids,
+                                    int32_t ids_dtype, void* y, int32_t block_m, void* workspace,
+                                    size_t workspace_bytes, void* stream);
+
 /* hexmoe_forward for callers that cannot allocate device memory and so have no
  * workspace to pass (a serving process whose memory pool already holds nearly
  * all of the GPU, a plugin host that owns every device allocation, a loop that

@@ -277,6 +277,28 @@ def test_layer_empty_batch():
     assert out.shape == (0, 128)
 
 
+def test_forward_slots_then_combine_equals_forward():
+    """hexmoe_forward_slots (the per-slot rows the expert-parallel path sends
+    back) summed by the combine, directly and through a row map, equals
+    hexmoe_forward bit for bit."""
+    from blackhole_b200.hex_moe import HexTier, layer_for
+    L = hd.synth_layer(16, 512, 256, "mixed", 128, seed=13, device=DEV)
+    tiers = [HexTier(t["bits"], t["experts"], t["gate_proj"], t["up_proj"], t["down_proj"]).prepare(16)
+             for t in L.tiers]
+    layer = layer_for(tiers)
+    T, K = 70, 4
+    w, ids = hd.synth_routing(T, 16, K, seed=14, device=DEV)
+    x = hd.synth_x(T, 512, seed=15, device=DEV)
+    want = layer.forward(x, w, ids)
+    y = layer.forward_slots(x, w, ids)
+    assert y.shape == (T * K, 512)
+    assert torch.equal(layer.combine(y, T, K), want)
+    perm = torch.randperm(T * K, generator=torch.Generator().manual_seed(1)).to(DEV)
+    rows = torch.empty(T * K, dtype=torch.int32, device=DEV)
+    rows[perm] = torch.arange(T * K, dtype=torch.int32, device=DEV)      # slot perm[i] sits in row i
+    assert torch.equal(layer.combine_rows(y[perm], T, K, rows), want)
+
+
 def test_layer_deterministic_and_graph_capturable(oracle):
     from blackhole_b200.hex_moe import hex_moe
     E, H, I, k, T = 16, 256, 256, 4, 32
