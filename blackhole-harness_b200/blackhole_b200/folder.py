@@ -21,7 +21,7 @@ convert.py:32-56); every other tensor of the folder is ignored here.
     save_folder(folder, ...)    writes a folder in the same layout (synthetic
                                 checkpoints for tests and benchmarks)
 
-    python -m blackhole_b200.folder <folder> [--device cuda] [--layers N]
+    python -m blackhole_b200.folder <folder> [--device cuda] [--layers N] [--no-kernel]
 
 prints the check as one JSON line and exits 1 on any problem.
 """
@@ -225,8 +225,9 @@ def main(argv: list[str] | None = None) -> int:
     ap.add_argument("--device", default="cuda")
     ap.add_argument("--layers", type=int, default=0, help="layers to run the kernel on (0 = all)")
     ap.add_argument("--tokens", type=int, default=5)
+    ap.add_argument("--no-kernel", action="store_true", help="structural checks only (no GPU needed)")
     a = ap.parse_args(argv)
-    r = check_folder(a.folder, a.device, a.layers, a.tokens)
+    r = check_folder(a.folder, a.device, a.layers, a.tokens, run_kernel=not a.no_kernel)
     print(json.dumps(r))
     return 0 if r["ok"] else 1
 

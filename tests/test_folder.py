@@ -88,6 +88,16 @@ def test_missing_part_is_reported(tmp_path):
     assert any("missing down_proj.levels" in p for p in r["problems"]), r
 
 
+def test_command_line_structural_check(tmp_path, capsys):
+    from blackhole_b200.folder import main
+    _write(tmp_path, n_layers=1)
+    assert main([str(tmp_path), "--no-kernel"]) == 0
+    r = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert r["ok"] and r["layers"] == 1
+    (tmp_path / "config.json").write_text(json.dumps({"quantization_config": {"quant_method": "awq"}}))
+    assert main([str(tmp_path), "--no-kernel"]) == 1
+
+
 @pytest.mark.gpu
 def test_check_folder_runs_the_kernel(tmp_path):
     _write(tmp_path)

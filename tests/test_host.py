@@ -46,6 +46,11 @@ def test_argument_errors_raise_valueerror_without_gpu():
     assert _lib.lib.hexmoe_tile_index(None, 3, 1, 100, 128, None, None) == _lib.HEXMOE_E_ARG    # rows_pad % 128
     assert _lib.lib.hexmoe_tile_index(None, 5, 1, 128, 128, None, None) == _lib.HEXMOE_E_ARG    # bits
     assert _lib.lib.hexmoe_tile_index(None, 3, 1, 128, 128, None, None) == _lib.HEXMOE_E_ARG    # null pointers
+    # per-slot forward and row-mapped combine: argument errors before any device work
+    assert _lib.lib.hexmoe_forward_slots(None, None, 1, 4, 2, None, None, 0, None, 0, None, 0, None) == _lib.HEXMOE_E_ARG
+    assert _lib.lib.hexmoe_combine_rows(None, _lib.BF16, 8, 4, 2, 128, None, None, _lib.BF16, None) == _lib.HEXMOE_E_ARG
+    assert _lib.lib.hexmoe_combine_rows(None, _lib.F32, 8, 4, 2, 128, None, None, _lib.BF16, None) == _lib.HEXMOE_E_DTYPE
+    assert _lib.lib.hexmoe_align(None, _lib.I32, 100, 0, 16, None, None, None, None, 0, None) == _lib.HEXMOE_E_ARG
 
 
 def make_tier(E=12, H=128, I=64, bits=3, block=32, seed=0):
