@@ -28,7 +28,7 @@
 //               summed by the epilogue) where an M=128 x N<=64 MMA costs its
 //               issuing thread more than the tensor pipe takes to run it
 //   warps 2-5   epilogue: tcgen05.ld of the accumulators, SwiGLU (gate/up) or
-//               the top-k weight (down), 16-bit stores; one tile ahead, the
+//               the top-k weight (down), 16-bit stores; ahead of the decoders, the
 //               code tables: the level table scaled by every one of the 256
 //               fp8 scale codes and rounded to the operand type (shared
 //               memory, two buffers)
