@@ -115,14 +115,15 @@ class EPMoE:
         self.group = group
         self.local_tiers = local_tiers
         self._layer = None
+        self._cuda = expert_fn is None        # the CUDA layer (else injected functions, e.g. on CPU ranks)
         if expert_fn is None:
             if local_tiers is None:
                 raise ValueError("EPMoE needs the local tiers or an expert_fn")
             from blackhole_b200.hex_moe import layer_for
-            self._layer = layer_for(local_tiers)
+            # a rank may own no experts (more ranks than experts allow): it only
+            # sends its tokens out and combines what comes back
+            self._layer = layer_for(local_tiers) if local_tiers else None
             expert_fn = self._local_phases
-            if combine_fn is None:
-                combine_fn = lambda y, T, k: self._layer.combine(y, T, k)  # noqa: E731
         self.expert_fn = expert_fn
         self.combine_fn = combine_fn or _sum_combine
 
@@ -185,8 +186,9 @@ class EPMoE:
         # 3. local experts, one slot per row
         out_dt = x.dtype if x.dtype in (torch.bfloat16, torch.float16) else torch.bfloat16
         if n_recv:
-            y_recv = (self._local_phases(recv_x, recv_w, recv_ids) if self._layer is not None
-                      else self.expert_fn(recv_x, recv_w, recv_ids)).to(out_dt).contiguous()
+            if self._cuda and self._layer is None:
+                raise RuntimeError("slots were routed to a rank that holds no experts")
+            y_recv = self.expert_fn(recv_x, recv_w, recv_ids).to(out_dt).contiguous()
         else:
             y_recv = torch.empty(0, H, dtype=out_dt, device=dev)
         # 4. rows back to their source rank, in the order they were sent
@@ -195,10 +197,11 @@ class EPMoE:
         if T == 0:
             return torch.empty(0, H, dtype=x.dtype, device=dev)
         # 5. combine the k slots of each token: slot order[i] came back as row i
-        if self._layer is not None:
+        if self._cuda:
+            from blackhole_b200.hex_moe import combine_rows
             rows = torch.empty(T * k, dtype=torch.int32, device=dev)
             rows.index_copy_(0, order, torch.arange(T * k, dtype=torch.int32, device=dev))
-            return self._layer.combine_rows(back, T, k, rows, out_dtype=x.dtype)
+            return combine_rows(back, T, k, rows, out_dtype=x.dtype)
         y = torch.empty_like(back)
         y.index_copy_(0, order, back)
         return self.combine_fn(y, T, k).to(x.dtype)

@@ -289,17 +289,27 @@ class _Layer:
         return out
 
     def combine_rows(self, y: torch.Tensor, T: int, k: int, rows: torch.Tensor, out_dtype=None) -> torch.Tensor:
-        """out[t] = sum_j y[rows[t*k + j]] (hexmoe_combine_rows): the combine of
-        per-slot rows held in another order."""
-        if rows.dtype != torch.int32 or rows.numel() != T * k:
-            raise ValueError("rows must be int32 [T * k]")
-        out = torch.empty(T, self.H, dtype=out_dtype or y.dtype, device=y.device)
-        y, rows = _aligned(y), rows.contiguous()
-        with torch.cuda.device(y.device):
-            rc = _lib.lib.hexmoe_combine_rows(_ptr(y), _DT[y.dtype], y.shape[0], T, k, self.H, _ptr(rows), _ptr(out),
-                                              _DT[out.dtype], _stream(y.device))
-        _lib.check(rc, "hexmoe_combine_rows")
-        return out
+        """out[t] = sum_j y[rows[t*k + j]]: see combine_rows()."""
+        return combine_rows(y, T, k, rows, out_dtype)
+
+
+def combine_rows(y: torch.Tensor, T: int, k: int, rows: torch.Tensor, out_dtype=None) -> torch.Tensor:
+    """out[t] = sum_j y[rows[t*k + j]] (hexmoe_combine_rows): the layer's combine
+    of per-slot rows held in another order; needs no layer.  y [R, H] 16-bit,
+    rows int32 [T * k]."""
+    if not y.is_cuda:
+        raise ValueError("combine_rows runs on CUDA only")
+    if rows.dtype != torch.int32 or rows.numel() != T * k:
+        raise ValueError("rows must be int32 [T * k]")
+    if y.dtype not in (torch.bfloat16, torch.float16) or y.dim() != 2:
+        raise ValueError("y must be a bf16 / fp16 [rows, H] tensor")
+    out = torch.empty(T, y.shape[1], dtype=out_dtype or y.dtype, device=y.device)
+    y, rows = _aligned(y), rows.contiguous()
+    with torch.cuda.device(y.device):
+        rc = _lib.lib.hexmoe_combine_rows(_ptr(y), _DT[y.dtype], y.shape[0], T, k, y.shape[1], _ptr(rows), _ptr(out),
+                                          _DT[out.dtype], _stream(y.device))
+    _lib.check(rc, "hexmoe_combine_rows")
+    return out
 
 
 def auto_block_m(slots: int, num_experts: int) -> int:

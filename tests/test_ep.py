@@ -106,6 +106,7 @@ def _run(world: int, T_of: list[int], zipf=None) -> dict:
 @pytest.mark.parametrize("world,T_of,zipf", [
     (2, [24, 17], None),
     (3, [16, 0, 9], 1.2),          # a rank with no tokens; skewed routing
+    (5, [7, 5, 0, 3, 6], None),    # E=12 over 5 ranks: rank 4 owns no experts
 ])
 def test_ep_matches_single_process(oracle, world, T_of, zipf):
     res = _run(world, T_of, zipf)
