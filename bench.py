@@ -83,12 +83,15 @@ class Clocks:
 
     def _run(self):
         nv = self.nv
+        pw, i = 0.0, 0
         while not self.stop_ev.is_set():
             try:
                 sm = nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)
                 rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
-                pw = nv.nvmlDeviceGetPowerUsage(self.h) / 1000.0
+                if i % 10 == 0:     # the power query is the slow one: every tenth sample
+                    pw = nv.nvmlDeviceGetPowerUsage(self.h) / 1000.0
                 self.samples.append((sm, rs, pw))
+                i += 1
             except Exception:  # noqa: BLE001
                 pass
             self.stop_ev.wait(0.0001)
