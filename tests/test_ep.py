@@ -107,6 +107,7 @@ def _run(world: int, T_of: list[int], zipf=None) -> dict:
     (2, [24, 17], None),
     (3, [16, 0, 9], 1.2),          # a rank with no tokens; skewed routing
     (5, [7, 5, 0, 3, 6], None),    # E=12 over 5 ranks: rank 4 owns no experts
+    (8, [4, 3, 5, 0, 2, 6, 1, 3], 1.2),   # eight ranks, as on one B200 node: ranks 6 and 7 own none
 ])
 def test_ep_matches_single_process(oracle, world, T_of, zipf):
     res = _run(world, T_of, zipf)
