@@ -17,6 +17,7 @@ HEXMOE_OK, HEXMOE_E_ARG, HEXMOE_E_DTYPE, HEXMOE_E_CUDA, HEXMOE_E_UNSUPPORTED, HE
 F32, BF16, F16 = 0, 1, 2
 I32, I64 = 0, 1
 MAX_TIERS = 4
+NOALLOC_SCRATCH_BYTES = 32 << 20   # HEXMOE_NOALLOC_SCRATCH_BYTES in include/hexmoe.h
 
 EXPORTS = (
     "hexmoe_abi_version", "hexmoe_last_error", "hexmoe_device_status", "hexmoe_build_expert_map",

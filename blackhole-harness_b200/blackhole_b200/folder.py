@@ -16,8 +16,10 @@ convert.py:32-56); every other tensor of the folder is ignored here.
     layer_tiers(tiers, E, dev)  the prepared HexTier list of one MoE layer
     check_folder(folder, ...)   the checks of check_folder.py:47-93 on this build:
                                 every expert held by exactly one tier, consistent
-                                shapes, and the fused layer against a torch fp32
-                                MoE over the weights hexmoe_dequant produces
+                                shapes, and the fused layer against
+                                reference_moe (hex_ref.moe_reference restated in
+                                torch over format_dequant, which decodes the
+                                stored parts itself), as check_folder.py:86-90
     save_folder(folder, ...)    writes a folder in the same layout (synthetic
                                 checkpoints for tests and benchmarks)
 
@@ -117,18 +119,61 @@ def layer_tiers(tiers: dict[int, dict], num_experts: int, device) -> list:
     return out
 
 
-def _torch_moe(x: torch.Tensor, w: torch.Tensor, ids: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor,
-               act_dtype: torch.dtype) -> torch.Tensor:
-    """fp32 SwiGLU MoE over dequantized weights, h rounded to the activation
-    dtype before down (the reference arithmetic, hex_ref.py:77-94)."""
-    I = w2.shape[2]
+def _fp8_values(device) -> torch.Tensor:
+    """The 256 fp8 e4m3 scale codes as HEX reads them (blackhole/anatomy/hex.py:199-203):
+    exponent field 0 is m/8 * 2^-6, every other field (1 + m/8) * 2^(e-7), the
+    all-ones codes included (+-480, not NaN)."""
+    c = torch.arange(256, device=device)
+    e, m = (c >> 3) & 15, (c & 7).to(torch.float32)
+    v = torch.where(e == 0, m * 2.0 ** -9, (1.0 + m / 8.0) * torch.exp2((e - 7).to(torch.float32)))
+    return torch.where(c >= 128, -v, v)
+
+
+def format_dequant(parts: dict, bits: int, experts: torch.Tensor) -> torch.Tensor:
+    """fp32 weights [len(experts), rows, cols] of local experts `experts` of one
+    stacked projection, decoded from the stored parts by the format's own rule
+    (blackhole/anatomy/hex.py:180-204): per 32-input block `bits` little-endian
+    words, code j at bits [j*bits, j*bits + bits); W = levels[code] * (fp8(scale)
+    * expert_scale), fp32 products.  The folder check's reference arithmetic: it
+    shares no code with the kernels it checks."""
+    idx = parts["idx"].index_select(0, experts)
+    n, rows, nw = idx.shape
+    words = idx.view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+    nblk = nw // bits
+    words = words.reshape(n, rows, nblk, bits)
+    lo = torch.arange(32, device=idx.device) * bits
+    wi, sh = lo // 32, lo % 32
+    v = words[..., wi] >> sh
+    spill = (sh + bits > 32)
+    nxt = words[..., torch.clamp(wi + 1, max=bits - 1)] << (32 - sh)
+    v = torch.where(spill, v | nxt, v)
+    codes = (v & ((1 << bits) - 1)).reshape(n, rows, nblk * 32)
+    lev = parts["levels"].index_select(0, experts).float()
+    vals = torch.gather(lev, 1, codes.reshape(n, -1)).reshape(n, rows, -1)
+    bs = parts["block_scale"].index_select(0, experts).to(torch.int64)
+    block = nblk * 32 // bs.shape[2]
+    s = _fp8_values(idx.device)[bs] * parts["expert_scale"].float().reshape(-1).index_select(0, experts)[:, None, None]
+    return vals * s.repeat_interleave(block, dim=2)
+
+
+def reference_moe(x: torch.Tensor, w: torch.Tensor, ids: torch.Tensor, tiers: dict[int, dict]) -> torch.Tensor:
+    """moe_reference (runtime/blackhole_runtime/hex_ref.py:77-94) over a folder
+    layer's tiers: per routed expert its weights by format_dequant, h = silu(x Wg^T)
+    * (x Wu^T) in fp32 rounded to x's dtype, out += w * (h Wd^T) in fp32."""
     xf = x.float()
-    out = torch.zeros(x.shape[0], w2.shape[1], dtype=torch.float32, device=x.device)
-    for j in range(ids.shape[1]):
-        e = ids[:, j].long()
-        gu = torch.bmm(w13[e], xf.unsqueeze(2)).squeeze(2)
-        h = (torch.nn.functional.silu(gu[:, :I]) * gu[:, I:]).to(act_dtype).float()
-        out += w[:, j:j + 1].float() * torch.bmm(w2[e], h.unsqueeze(2)).squeeze(2)
+    out = torch.zeros(x.shape[0], x.shape[1], dtype=torch.float32, device=x.device)
+    for L, t in tiers.items():
+        bits = _bits(L)
+        ex = t["experts"].reshape(-1).to(x.device).long()
+        for local in range(ex.numel()):
+            tok, slot = torch.nonzero(ids == ex[local], as_tuple=True)
+            if tok.numel() == 0:
+                continue
+            li = torch.tensor([local], device=x.device)
+            g, u, d = (format_dequant({q: v.to(x.device) for q, v in t[p].items()}, bits, li)[0] for p in PROJ)
+            a = xf[tok]
+            h = (torch.nn.functional.silu(a @ g.T) * (a @ u.T)).to(x.dtype).float()
+            out.index_add_(0, tok, (h @ d.T) * w[tok, slot].float()[:, None])
     return out
 
 
@@ -140,8 +185,8 @@ def check_folder(folder: str | Path, device: str = "cuda", layers: int = 0, toke
                  run_kernel: bool = True) -> dict:
     """The folder check: config, every layer's tiers, and (run_kernel) the fused
     layer on `tokens` random tokens and routings per layer (the first `layers`
-    layers; 0 = all) against the fp32 MoE of its dequantized experts, relative
-    max error within 2e-2 (bf16 activations)."""
+    layers; 0 = all) against reference_moe, relative max error within 2e-2
+    (bf16 activations; check_folder.py:86-90)."""
     folder = Path(folder)
     problems: list[str] = []
     cfg_path = folder / "config.json"
@@ -165,7 +210,7 @@ def check_folder(folder: str | Path, device: str = "cuda", layers: int = 0, toke
         problems += p
         if p or not run_kernel or (layers and checked >= layers):
             continue
-        from blackhole_b200.hex_moe import dequant_all, hex_moe
+        from blackhole_b200.hex_moe import hex_moe
         n = E or int(torch.cat([t["experts"].reshape(-1) for t in tiers.values()]).max()) + 1
         run = layer_tiers(tiers, n, device)
         I, H = run[0].dims()
@@ -175,13 +220,12 @@ def check_folder(folder: str | Path, device: str = "cuda", layers: int = 0, toke
         w = torch.softmax(torch.randn(tokens, kk, generator=g), -1).to(device)
         x = torch.randn(tokens, H, generator=g).to(torch.bfloat16).to(device)
         got = hex_moe(x, w, ids, run).float()
-        w13, w2 = dequant_all(run, torch.float32)
-        want = _torch_moe(x, w, ids, w13, w2, torch.bfloat16)
+        want = reference_moe(x, w, ids, tiers)
         worst = max(worst, float((got - want).abs().max() / (want.abs().max() + 1e-12)))
         checked += 1
     if checked and worst >= 2e-2:
-        problems.append(f"the fused layer differs from the fp32 MoE of its dequantized experts by {worst:.1e} "
-                        "(tolerance 2e-2)")
+        problems.append(f"the fused layer differs from moe_reference over the format's dequantization by "
+                        f"{worst:.1e} (tolerance 2e-2)")
     return {"layers": len(all_tiers), "checked": checked, "kernel_rel": worst, "problems": problems,
             "ok": not problems}
 

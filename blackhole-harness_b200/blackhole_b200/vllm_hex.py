@@ -88,21 +88,35 @@ def register() -> None:
     from vllm.model_executor.layers.vocab_parallel_embedding import ParallelLMHead, UnquantizedEmbeddingMethod
 
     class HexHeadMethod(UnquantizedEmbeddingMethod):
-        """bf16 LM head; logits of tokens outside the kept ids are HEAD_FILL."""
+        """Output-trimmed LM head: only the kept vocabulary rows are multiplied.
+
+        The reference computes every logit and then adds a -1e4 mask outside the
+        kept ids (vllm_hex.py:78-93).  Here the kept rows of the weight are
+        gathered once after loading into a [K, hidden] matrix; apply() runs that
+        K-row GEMM and scatters its columns into logits pre-filled with HEAD_FILL,
+        so the head reads and multiplies K of the V rows.  Kept logits are the
+        same GEMM values; a dropped token's logit is HEAD_FILL itself (the
+        reference's is its true logit - 1e4): either way it is never sampled."""
 
         def __init__(self, ids):
             super().__init__()
-            self.ids = list(ids)
+            self.keep = sorted({int(i) for i in ids})
 
         def process_weights_after_loading(self, layer) -> None:
             super().process_weights_after_loading(layer)
             w = layer.weight
-            mask = torch.full((w.shape[0],), HEAD_FILL, dtype=w.dtype, device=w.device)
-            mask[torch.as_tensor(self.ids, dtype=torch.long, device=w.device)] = 0
-            layer.register_buffer("hex_head_mask", mask, persistent=False)
+            keep = torch.as_tensor(self.keep, dtype=torch.long, device=w.device)
+            if keep.numel() and (int(keep.min()) < 0 or int(keep.max()) >= w.shape[0]):
+                raise ValueError(f"{NAME}: head_ids outside the vocabulary of {w.shape[0]} rows")
+            layer.register_buffer("hex_head_keep", keep, persistent=False)
+            layer.register_buffer("hex_head_rows", w.index_select(0, keep).contiguous(), persistent=False)
 
         def apply(self, layer, x, bias=None):
-            return super().apply(layer, x, bias) + layer.hex_head_mask
+            kept = torch.nn.functional.linear(x, layer.hex_head_rows,
+                                              None if bias is None else bias.index_select(0, layer.hex_head_keep))
+            out = torch.full((*x.shape[:-1], layer.weight.shape[0]), HEAD_FILL, dtype=kept.dtype, device=x.device)
+            out.index_copy_(-1, layer.hex_head_keep, kept)
+            return out
 
     class HexMoEMethod(FusedMoEMethodBase):
         """Routed experts of one MoE layer as HEX tiers on the sm_100a layer."""

@@ -41,6 +41,8 @@
 //               half-stage goes to the MMA once both its stores are done
 // Every wait is bounded (ptx.cuh): a lost arrival ends the kernel with the
 // device error word set instead of hanging.
+#include <atomic>
+#include <mutex>
 #include <type_traits>
 
 #include "decode.cuh"
@@ -450,8 +452,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           if (GLU) {
-            const float hg = 0.5f * __uint_as_float(g[j]);     // silu(g) = g/2 * (1 + tanh(g/2))
-            v[j] = fmaf(hg, tanh_approx(hg), hg) * __uint_as_float(u[j]);
+            // silu(g) = g / (1 + e^-g) with CUDA's expf and an IEEE division, as
+            // the reference's fp32 torch silu; a large negative g gives -0
+            const float gg = __uint_as_float(g[j]);
+            v[j] = __fdiv_rn(gg, 1.0f + expf(-gg)) * __uint_as_float(u[j]);
           } else {
             v[j] = __uint_as_float(g[j]) * recs[ri].w[n0 + j];
           }
@@ -606,15 +610,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
 template <bool GLU, bool BF16, bool KS>
 static cudaError_t launch_one(const GemmParams& p, int grid, cudaStream_t stream, bool pdl) {
   auto kern = hex_gemm_kernel<GLU, BF16, KS>;
-  static int configured_bytes[64] = {};   // per device and instantiation; raised monotonically
+  // per device and instantiation, raised monotonically; the mutex keeps two
+  // host threads from racing on the first launches
+  static std::atomic<int> configured_bytes[64] = {};
+  static std::mutex mu;
   int dev = 0;
   cudaGetDevice(&dev);
   const int bytes = static_cast<int>(p.smem_bytes);
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (bytes > configured_bytes[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-    if (e != cudaSuccess) return e;
-    configured_bytes[dev] = bytes;
+  if (bytes > configured_bytes[dev].load(std::memory_order_acquire)) {
+    std::lock_guard<std::mutex> lock(mu);
+    if (bytes > configured_bytes[dev].load(std::memory_order_relaxed)) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+      if (e != cudaSuccess) return e;
+      configured_bytes[dev].store(bytes, std::memory_order_release);
+    }
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);

@@ -1,6 +1,9 @@
 // kernels.cu — the small kernels around the grouped GEMM: the align plan, the
 // bit-exact dequantization, the top-k combine, the fp32 -> 16-bit cast and
 // the router.
+#include <atomic>
+#include <mutex>
+
 #include <cub/block/block_scan.cuh>
 
 #include "decode.cuh"
@@ -12,15 +15,23 @@ namespace hexmoe {
 __device__ int32_t g_dev_err;
 
 int32_t* device_error_word() {
-  static int32_t* addr[64] = {};
+  // per-device cache of the symbol's address; first calls from several host
+  // threads serialise on the mutex, later ones read the atomic slot only
+  static std::atomic<int32_t*> addr[64] = {};
+  static std::mutex mu;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  if (!addr[dev]) {
+  int32_t* a = addr[dev].load(std::memory_order_acquire);
+  if (a) return a;
+  std::lock_guard<std::mutex> lock(mu);
+  a = addr[dev].load(std::memory_order_relaxed);
+  if (!a) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_dev_err) != cudaSuccess) return nullptr;
-    addr[dev] = static_cast<int32_t*>(p);
+    a = static_cast<int32_t*>(p);
+    addr[dev].store(a, std::memory_order_release);
   }
-  return addr[dev];
+  return a;
 }
 
 cudaError_t read_device_error(int32_t* value, bool clear) {
@@ -343,23 +354,27 @@ cudaError_t launch_align(const void* ids, bool ids64, int64_t S, int32_t E, int3
                          int32_t* npp, int32_t* scratch, size_t scratch_bytes, int32_t* dev_err, cudaStream_t st,
                          bool pdl) {
   if (E > kAlignMaxExperts) return cudaErrorInvalidValue;
-  static bool configured[64] = {};   // per device
+  static std::atomic<bool> configured[64] = {};   // per device
+  static std::mutex mu;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (!configured[dev]) {
-    const void* kerns[] = {reinterpret_cast<const void*>(align_kernel<true>),
-                           reinterpret_cast<const void*>(align_kernel<false>),
-                           reinterpret_cast<const void*>(align_count_kernel<true>),
-                           reinterpret_cast<const void*>(align_count_kernel<false>),
-                           reinterpret_cast<const void*>(align_scatter_kernel<true>),
-                           reinterpret_cast<const void*>(align_scatter_kernel<false>)};
-    for (const void* k : kerns) {
-      e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kAlignSmemMax);
-      if (e != cudaSuccess) return e;
+  if (!configured[dev].load(std::memory_order_acquire)) {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!configured[dev].load(std::memory_order_relaxed)) {
+      const void* kerns[] = {reinterpret_cast<const void*>(align_kernel<true>),
+                             reinterpret_cast<const void*>(align_kernel<false>),
+                             reinterpret_cast<const void*>(align_count_kernel<true>),
+                             reinterpret_cast<const void*>(align_count_kernel<false>),
+                             reinterpret_cast<const void*>(align_scatter_kernel<true>),
+                             reinterpret_cast<const void*>(align_scatter_kernel<false>)};
+      for (const void* k : kerns) {
+        e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kAlignSmemMax);
+        if (e != cudaSuccess) return e;
+      }
+      configured[dev].store(true, std::memory_order_release);
     }
-    configured[dev] = true;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.blockDim = dim3(kAlignThreads);

@@ -30,7 +30,9 @@ import sys
 from pathlib import Path
 
 os.environ.setdefault("TRITON_INTERPRET", "1")
-REF = Path(os.environ.get("REF", "/root/reference"))
+if "REF" not in os.environ:
+    sys.exit("make_golden.py: set REF to the root of a BlackHole-Harness checkout (the reference implementation)")
+REF = Path(os.environ["REF"])
 sys.path[:0] = [str(REF / "runtime"), str(REF)]
 HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE.parents[1] / "blackhole-harness_b200"))

@@ -103,3 +103,27 @@ def test_check_folder_runs_the_kernel(tmp_path):
     _write(tmp_path)
     r = check_folder(tmp_path, device="cuda")
     assert r["ok"] and r["checked"] == 2 and r["kernel_rel"] < 2e-2, r
+
+
+@pytest.mark.parametrize("bits,block", [("3", 32), ("4", 128), ("mixed", 32)])
+def test_checker_arithmetic_matches_oracle(oracle, bits, block):
+    """The folder check's own reference (format_dequant, reference_moe) equals
+    the pinned oracle: dequantization bit for bit, the layer within 1e-5."""
+    import numpy as np
+    from helpers import np_tiers
+
+    from blackhole_b200.folder import format_dequant, reference_moe
+    Hq, Iq = 256, 128          # multiples of the 128-input scale block
+    L = hd.synth_layer(E, Hq, Iq, bits, block, seed=70)
+    for t, nt in zip(L.tiers, np_tiers(L.tiers)):
+        ex = torch.arange(len(t["experts"]))
+        for p in ("gate_proj", "up_proj", "down_proj"):
+            got = format_dequant(t[p], t["bits"], ex).numpy()
+            want = oracle.dequant(nt[p], t["bits"], block)
+            assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), p
+    w, ids = hd.synth_routing(9, E, K, seed=71)
+    x = hd.synth_x(9, Hq, seed=72)
+    tiers = {1 << t["bits"]: t for t in L.tiers}
+    got = reference_moe(x, w, ids, tiers).numpy()
+    want = oracle.moe_reference(x.float().numpy(), w.numpy(), ids.numpy(), np_tiers(L.tiers), E, block=block)
+    assert np.abs(got - want).max() <= 1e-5 * np.abs(want).max()

@@ -223,7 +223,7 @@ def test_layer_cfg1_tiny_config(oracle):
     assert within(got, z["out_bf16"]), rel_err(got, z["out_bf16"])
 
 
-@pytest.mark.parametrize("T", [1, 8, 64])
+@pytest.mark.parametrize("T", [1, 8, 32, 64])
 def test_layer_decode_cfg2_shape(oracle, T):
     c = hd.CONFIGS["cfg2"]
     L = hd.synth_layer(c["E"], c["H"], c["I"], "3", c["block"], seed=7)
@@ -240,6 +240,39 @@ def test_layer_prefill_mixed_tiers(oracle, bits, block, bm):
     w, ids = hd.synth_routing(T, E, k, seed=32)
     x = hd.synth_x(T, H, seed=33)
     got, want = _run_layer(oracle, L, w, ids, x, block_m=bm or None)
+    assert within(got, want), rel_err(got, want)
+
+
+def _sampled_parity(oracle, L, w, ids, x, block_m: int, sample: int, seed: int):
+    """The full batch through the CUDA layer; the oracle on a seeded sample of its
+    tokens (each token's output depends on its own row and routing only)."""
+    from blackhole_b200.hex_moe import hex_moe
+    tiers = hex_tiers(L.tiers, L.E, DEV)
+    got = hex_moe(x.to(DEV), w.to(DEV), ids.to(DEV), tiers, {"BLOCK_M": block_m}).float().cpu().numpy()
+    pick = torch.randperm(x.shape[0], generator=torch.Generator().manual_seed(seed))[:sample].sort().values
+    want = oracle.moe_reference(x[pick].float().numpy(), w[pick].numpy(), ids[pick].numpy(), np_tiers(L.tiers), L.E,
+                                block=L.block)
+    return got[pick.numpy()], want
+
+
+def test_layer_prefill_cfg3_bench_shape(oracle):
+    """The bench's prefill workload exactly: cfg3, E=96 H=2048 I=768 top-8, mixed
+    3/4-bit, block-128 scales, T=4096, tile height 128."""
+    c = hd.CONFIGS["cfg3"]
+    L = hd.synth_layer(c["E"], c["H"], c["I"], c["bits"], c["block"], seed=3)
+    w, ids = hd.synth_routing(4096, c["E"], c["k"], seed=5)
+    x = hd.synth_x(4096, c["H"], seed=6)
+    got, want = _sampled_parity(oracle, L, w, ids, x, 128, sample=96, seed=1)
+    assert within(got, want), rel_err(got, want)
+
+
+def test_layer_cfg4_one_gpu_slice(oracle):
+    """cfg4's per-GPU slice at 8 GPUs: 16 experts of H=4096, I=1536, mixed 3/4-bit,
+    block-128 scales, 1024 tokens at top-8 (512 slots per expert)."""
+    L = hd.synth_layer(16, 4096, 1536, "mixed", 128, seed=44)
+    w, ids = hd.synth_routing(1024, 16, 8, seed=45)
+    x = hd.synth_x(1024, 4096, seed=46)
+    got, want = _sampled_parity(oracle, L, w, ids, x, 128, sample=48, seed=2)
     assert within(got, want), rel_err(got, want)
 
 

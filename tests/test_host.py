@@ -32,6 +32,15 @@ def test_library_exports_every_header_symbol():
     assert _lib.lib.hexmoe_abi_version() == 1
 
 
+def test_noalloc_scratch_constant_matches_header():
+    """_lib.NOALLOC_SCRATCH_BYTES mirrors HEXMOE_NOALLOC_SCRATCH_BYTES (the tests probe that limit)."""
+    from blackhole_b200 import _lib
+    src = (ROOT / "include" / "hexmoe.h").read_text()
+    m = re.search(r"#define\s+HEXMOE_NOALLOC_SCRATCH_BYTES\s+\((\d+)u\s*<<\s*(\d+)\)", src)
+    assert m, "HEXMOE_NOALLOC_SCRATCH_BYTES not found"
+    assert int(m.group(1)) << int(m.group(2)) == _lib.NOALLOC_SCRATCH_BYTES
+
+
 def test_argument_errors_raise_valueerror_without_gpu():
     from blackhole_b200 import _lib
     rc = _lib.lib.hexmoe_layer_create(None, None)

@@ -55,6 +55,32 @@ def test_registered_with_vllm():
     vh.register()                                   # idempotent
 
 
+def test_trimmed_head_matches_full_head_on_kept_ids():
+    """The output-trimmed LM head (HexHeadMethod, for a config with head_ids):
+    kept logits equal the full head's, every other logit is HEAD_FILL."""
+    vh, _ = _method()
+    V, D = 50, 16
+    g = torch.Generator().manual_seed(4)
+    layer = torch.nn.Module()
+    layer.weight = torch.nn.Parameter(torch.randn(V, D, generator=g), requires_grad=False)
+    keep = [3, 7, 7, 41, 0]
+    head = vh._registered["head"](keep)
+    head.process_weights_after_loading(layer)
+    x = torch.randn(5, D, generator=g)
+    bias = torch.randn(V, generator=g)
+    for b in (None, bias):
+        got = head.apply(layer, x, b)
+        full = torch.nn.functional.linear(x, layer.weight, b)
+        kept = sorted(set(keep))
+        assert got.shape == full.shape
+        assert torch.allclose(got[:, kept], full[:, kept], rtol=1e-5, atol=1e-5)
+        mask = torch.ones(V, dtype=torch.bool)
+        mask[kept] = False
+        assert bool((got[:, mask] == vh.HEAD_FILL).all())
+    with pytest.raises(ValueError):
+        vh._registered["head"]([V]).process_weights_after_loading(layer)
+
+
 def test_names_load_into_tiers():
     vh, m = _method()
     L, ck = _checkpoint()

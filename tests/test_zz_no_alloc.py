@@ -60,11 +60,20 @@ def _no_alloc(layer, x, w, ids, out: torch.Tensor) -> None:
 
 
 def test_noalloc_matches_workspace_forward_two_calls():
+    """Two calls in a row, each bit-equal to hexmoe_forward with a workspace on
+    the same inputs.  A first call at a larger batch with NaN / Inf activations
+    leaves poisoned rows all over the shared array; the second, smaller call must
+    not see any of them (padding rows of its plan hold whatever the first call
+    left, and must never reach `out`)."""
     from blackhole_b200.hex_moe import device_status
     device_status(0, clear=True)
     layer = _layer()
-    # two calls in a row on different batches: the second runs over the scratch
-    # the first left behind
+    poison = _inputs(96, 3)[0]
+    poison[::3] = float("nan")
+    poison[1::3] = float("inf")
+    x0, w0, ids0 = poison, *_inputs(96, 3)[1:]
+    out0 = torch.empty(96, H, dtype=torch.float32, device=DEV)
+    _no_alloc(layer, x0, w0, ids0, out0)
     for T, seed in ((48, 5), (20, 9)):
         x, w, ids = _inputs(T, seed)
         want = _with_workspace(layer, x, w, ids).cpu().numpy()
@@ -72,16 +81,29 @@ def test_noalloc_matches_workspace_forward_two_calls():
         _no_alloc(layer, x, w, ids, out)
         got = out.cpu().numpy()
         assert np.isfinite(got).all()
-        assert within(got, want), rel_err(got, want)
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), rel_err(got, want)
+        assert within(got, want)
     assert device_status(0, clear=True) == 0
 
 
 def test_noalloc_rejects_batches_beyond_its_scratch():
+    """The largest batch whose scratch fits runs; one token more is rejected
+    with HEXMOE_E_ARG before anything is launched."""
     layer = _layer()
-    limit = 32 << 20
-    T = 1
-    while _lib.lib.hexmoe_forward_workspace_bytes(layer.handle, T, K, 0, _lib.BF16) <= limit:
-        T *= 2
+    limit = _lib.NOALLOC_SCRATCH_BYTES
+    need = lambda t: _lib.lib.hexmoe_forward_workspace_bytes(layer.handle, t, K, 0, _lib.BF16)   # noqa: E731
+    lo, hi = 1, 2
+    while need(hi) <= limit:
+        lo, hi = hi, hi * 2
+    while hi - lo > 1:                      # largest T with need(T) <= limit
+        mid = (lo + hi) // 2
+        lo, hi = (mid, hi) if need(mid) <= limit else (lo, mid)
+    x, w, ids = _inputs(lo, 13)
+    out = torch.empty(lo, H, dtype=torch.float32, device=DEV)
+    _no_alloc(layer, x, w, ids, out)
+    want = _with_workspace(layer, x, w, ids)
+    assert torch.equal(out, want)
+    T = hi
     x = torch.zeros(T, H, dtype=torch.bfloat16, device=DEV)
     w = torch.zeros(T, K, dtype=torch.float32, device=DEV)
     ids = torch.zeros(T, K, dtype=torch.int32, device=DEV)
