@@ -25,7 +25,11 @@ EXPORTS = (
     "hexmoe_align_workspace_bytes", "hexmoe_align", "hexmoe_dequant", "hexmoe_route_topk",
     "hexmoe_gather", "hexmoe_gate_up", "hexmoe_down", "hexmoe_combine", "hexmoe_forward_noalloc",
     "hexmoe_tile_index", "hexmoe_combine_rows", "hexmoe_forward_slots",
+    "hexmoe_ep_init", "hexmoe_ep_handle", "hexmoe_ep_connect", "hexmoe_ep_workspace_bytes", "hexmoe_ep_dispatch",
+    "hexmoe_ep_experts", "hexmoe_ep_combine", "hexmoe_ep_forward", "hexmoe_ep_destroy",
 )
+EP_MAX_WORLD = 8          # HEXMOE_EP_MAX_WORLD
+EP_HANDLE_BYTES = 64      # HEXMOE_EP_HANDLE_BYTES
 
 
 class Parts(ctypes.Structure):
@@ -72,6 +76,15 @@ def _load() -> ctypes.CDLL:
         "hexmoe_down": (ctypes.c_int, [P, P, I32_, I64_, I32_, P, P, P, P, I32_, P, P]),
         "hexmoe_combine": (ctypes.c_int, [P, I32_, I64_, I32_, I32_, P, I32_, P]),
         "hexmoe_combine_rows": (ctypes.c_int, [P, I32_, I64_, I64_, I32_, I32_, P, P, I32_, P]),
+        "hexmoe_ep_init": (ctypes.c_int, [I32_, I32_, I32_, I32_, I32_, I64_, I32_, P]),
+        "hexmoe_ep_handle": (ctypes.c_int, [P, P]),
+        "hexmoe_ep_connect": (ctypes.c_int, [P, P]),
+        "hexmoe_ep_workspace_bytes": (SZ, [P, P, I32_]),
+        "hexmoe_ep_dispatch": (ctypes.c_int, [P, P, I32_, I64_, P, P, I32_, P]),
+        "hexmoe_ep_experts": (ctypes.c_int, [P, P, I32_, P, SZ, P]),
+        "hexmoe_ep_combine": (ctypes.c_int, [P, I64_, P, I32_, P]),
+        "hexmoe_ep_forward": (ctypes.c_int, [P, P, P, I32_, I64_, P, P, I32_, P, I32_, I32_, P, SZ, P]),
+        "hexmoe_ep_destroy": (ctypes.c_int, [P]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)

@@ -1,4 +1,4 @@
-"""Expert parallelism for the HEX MoE layer over a torch.distributed process group.
+"""Expert parallelism for the HEX MoE layer: experts sharded over the ranks of one node.
 
 The reference plugin refuses expert and tensor parallelism
 (runtime/blackhole_runtime/vllm_hex.py:101-102) and runs one GPU; this module is
@@ -7,29 +7,29 @@ over the ranks (rank r owns global experts [r * P, (r + 1) * P), P =
 ceil(E / world)) and each rank holds only its experts' HEX tiers.
 
 Forward for the T tokens of this rank (global expert ids in topk_ids):
-  1. the S = T * k slots (t, j), grouped by the rank that owns expert
-     topk_ids[t, j] (stable, so each rank's slots keep their order);
-  2. an all-to-all of the per-rank slot counts, then of the slots' token rows
-     (in the activation dtype), expert ids and top-k weights;
-  3. the local experts on the received rows: the layer at top-1, each row with
-     its own weight, so every row comes back as w * down(silu(gate x) * up x)
-     rounded to the activation dtype, exactly as the single-GPU layer rounds
-     each slot before its combine;
-  4. an all-to-all of those rows back to the ranks they came from;
-  5. out[t] = the k returned rows of token t summed in fp32 and rounded (the
-     layer's own combine kernel on the GPU).
-Each slot goes through the same arithmetic as in the single-GPU layer, so the
-result equals the single-GPU output bit for bit (at the same block_m).  Traffic
-per rank: 2 x S x H activation rows plus 8 bytes of metadata per slot.
+  1. dispatch: each token row goes once to every rank that owns at least one
+     of its k experts (not once per slot), with one record per slot (row,
+     expert, top-k weight) in the token's j order;
+  2. experts: each rank runs its experts on the received slots, one slot per
+     row at top-1, giving w * down(silu(gate x) * up x) rounded to the row
+     dtype per slot, exactly as the single-GPU layer rounds each slot;
+  3. return: per received row, the fp32 sum of its slots in j order, rounded
+     once to the row dtype, goes back to the row's source rank;
+  4. combine: out[t] = the returned partials of token t summed in rank order in
+     fp32, rounded once.
+With one rank this is the single-GPU layer bit for bit; with several it
+differs from it only in the rounding of the per-rank partial sums.
 
-Collectives: plain all-to-alls (NCCL on GPUs).  The first carries each rank's
-slot count per destination and its argument-error flag, read on the host once
-(the counts set the split lists; a bad call raises on every rank before any
-data moves).  Every rank runs the same collectives in the same order, including
-ranks with no tokens and calls that end in an argument error.  On the GPU the
-local experts run as the layer's phases without its top-1 combine, and the
-returned rows are summed in slot order through a row map (hexmoe_combine_rows)
-instead of being copied back into slot order first.
+On GPUs (EPMoE with local tiers) the four steps are the library's hexmoe_ep_*
+kernels over CUDA-IPC peer memory: stores straight into the owner's region over
+NVLink, epoch flags instead of host synchronisation, so a forward can be
+captured in a CUDA graph.  The only collective on the host is the one-time
+exchange of the IPC handles at construction.  An expert id outside 0..E-1 is
+dropped and sets the device error word (hexmoe_device_status) on the GPU path.
+
+On CPU ranks (EPMoE with an expert_fn, e.g. the oracle over gloo in the tests)
+the same protocol runs over torch all-to-alls with the counts read on the host;
+there a bad expert id raises ValueError on every rank before any row moves.
 """
 
 from __future__ import annotations
@@ -86,124 +86,268 @@ def shard_tiers(tiers: list, shard: ExpertShard) -> list:
 
 
 ExpertFn = Callable[[torch.Tensor, torch.Tensor, torch.Tensor], torch.Tensor]
-CombineFn = Callable[[torch.Tensor, int, int], torch.Tensor]
 
 
-def _sum_combine(y: torch.Tensor, T: int, k: int) -> torch.Tensor:
-    """The combine of the CUDA layer on any device: slots added in order in fp32."""
-    yv = y.view(T, k, -1)
-    acc = yv[:, 0].float()
-    for j in range(1, k):
-        acc = acc + yv[:, j].float()
-    return acc.to(y.dtype)
+@dataclass
+class DispatchPlan:
+    """Where this rank's tokens go (the host form of the device plan).
+
+    pos[t, d]   row position of token t in the list sent to rank d, -1 = none
+    rows[d]     tokens sent to rank d, in token order
+    slots[d]    (token, j) of the slots sent to rank d, ordered by (token, j)
+    """
+    pos: torch.Tensor
+    rows: list
+    slots: list
+
+
+def plan_dispatch(ids: torch.Tensor, shard: ExpertShard) -> DispatchPlan:
+    """Rows and slots per destination rank, stable in token order and j order
+    (what ep_plan_kernel computes on the device).  ids: valid global ids [T, k]."""
+    T, k = ids.shape
+    owner = shard.owner(ids)                                          # [T, k]
+    pos = torch.full((T, shard.world), -1, dtype=torch.int64)
+    rows, slots = [], []
+    for d in range(shard.world):
+        mine = owner == d                                             # [T, k]
+        has = mine.any(1)
+        tok = torch.nonzero(has).flatten()
+        pos[tok, d] = torch.arange(tok.numel())
+        rows.append(tok)
+        t_idx, j_idx = torch.nonzero(mine, as_tuple=True)             # row-major: (t, j) order
+        slots.append((t_idx, j_idx))
+    return DispatchPlan(pos, rows, slots)
+
+
+def _row_dtype(dt: torch.dtype) -> torch.dtype:
+    return dt if dt in (torch.bfloat16, torch.float16) else torch.bfloat16
 
 
 class EPMoE:
-    """The HEX MoE layer with experts sharded over `group`.
+    """The HEX MoE layer with experts sharded over `group` (one rank per GPU).
 
-    local_tiers: this rank's prepared HexTier list (from shard_tiers(...) then
-    HexTier.prepare(num_experts)); expert_fn / combine_fn replace the CUDA layer
-    (tests run the host logic on CPU ranks with the oracle as expert_fn).
-    block_m: tile height of the local layer (0 = by the received slot count).
-    The down GEMM's accumulation order depends on it (two accumulators for
-    block_m <= 64), so EP equals a single-GPU run bit for bit at the same block_m."""
+    GPU path: local_tiers is this rank's prepared HexTier list (from
+    shard_tiers(...) then HexTier.prepare(num_experts)); an empty list on a rank
+    that owns no experts.  max_tokens, topk and hidden fix the shared buffers at
+    construction (every rank must pass the same values: the buffers of all
+    ranks have one layout); construction exchanges the IPC handles over `group`
+    and so is collective.  Then every rank must make the same sequence of
+    forward calls.  close() (collective) frees the buffers.
+
+    CPU path: expert_fn(x_rows, weights, ids) -> per-slot rows (rounded to the
+    row dtype) replaces the local layer; the protocol runs over torch
+    all-to-alls (the tests run it on gloo ranks with the oracle as expert_fn).
+    block_m: tile height of the local layer (0 = automatic)."""
 
     def __init__(self, shard: ExpertShard, local_tiers: list | None = None, group=None,
-                 expert_fn: ExpertFn | None = None, combine_fn: CombineFn | None = None, block_m: int = 0):
+                 expert_fn: ExpertFn | None = None, block_m: int = 0, max_tokens: int = 4096, topk: int = 8,
+                 hidden: int | None = None, row_dtype: torch.dtype = torch.bfloat16):
         self.shard = shard
         self.block_m = block_m
         self.group = group
-        self.local_tiers = local_tiers
-        self._layer = None
-        self._cuda = expert_fn is None        # the CUDA layer (else injected functions, e.g. on CPU ranks)
-        if expert_fn is None:
-            if local_tiers is None:
-                raise ValueError("EPMoE needs the local tiers or an expert_fn")
-            from blackhole_b200.hex_moe import layer_for
-            # a rank may own no experts (more ranks than experts allow): it only
-            # sends its tokens out and combines what comes back
-            self._layer = layer_for(local_tiers) if local_tiers else None
-            expert_fn = self._local_phases
         self.expert_fn = expert_fn
-        self.combine_fn = combine_fn or _sum_combine
+        self.local_tiers = local_tiers
+        self._ctx = None
+        self._ws = {}
+        self._layer = None
+        if expert_fn is not None:
+            return
+        if local_tiers is None:
+            raise ValueError("EPMoE needs the local tiers (possibly empty) or an expert_fn")
+        from blackhole_b200 import _lib
+        from blackhole_b200.hex_moe import layer_for
+        self._lib = _lib
+        if local_tiers:
+            self._layer = layer_for(local_tiers)
+            if hidden is not None and hidden != self._layer.H:
+                raise ValueError(f"hidden {hidden} differs from the local tiers' {self._layer.H}")
+            hidden = self._layer.H
+            self.device = self._layer.device
+        else:
+            if hidden is None:
+                raise ValueError("a rank without experts must be given `hidden`")
+            self.device = torch.device("cuda", torch.cuda.current_device())
+        self.hidden, self.topk, self.max_tokens = int(hidden), int(topk), int(max_tokens)
+        if row_dtype not in (torch.bfloat16, torch.float16):
+            raise ValueError("rows travel as bf16 or fp16")
+        self.row_dtype = row_dtype
+        import ctypes
+        h = ctypes.c_void_p()
+        rdt = _lib.BF16 if row_dtype == torch.bfloat16 else _lib.F16
+        with torch.cuda.device(self.device):
+            _lib.check(_lib.lib.hexmoe_ep_init(shard.rank, shard.world, shard.num_experts, self.hidden, self.topk,
+                                               self.max_tokens, rdt, ctypes.byref(h)), "hexmoe_ep_init")
+            self._ctx = h
+            if shard.world > 1:
+                mine = torch.empty(_lib.EP_HANDLE_BYTES, dtype=torch.uint8)
+                _lib.check(_lib.lib.hexmoe_ep_handle(h, mine.data_ptr()), "hexmoe_ep_handle")
+                on_dev = dist.get_backend(group) == "nccl"
+                t = mine.to(self.device) if on_dev else mine
+                got = [torch.empty_like(t) for _ in range(shard.world)]
+                dist.all_gather(got, t, group=group)
+                allh = torch.cat([g.cpu() for g in got]).contiguous()
+                _lib.check(_lib.lib.hexmoe_ep_connect(h, allh.data_ptr()), "hexmoe_ep_connect")
 
+    # ------------------------------------------------------------------ GPU
+    def _workspace(self, bm: int) -> torch.Tensor | None:
+        if self._layer is None:
+            return None
+        ws = self._ws.get(bm)
+        if ws is None:
+            n = self._lib.lib.hexmoe_ep_workspace_bytes(self._ctx, self._layer.handle, bm)
+            ws = self._ws[bm] = torch.empty(n, dtype=torch.uint8, device=self.device)
+        return ws
+
+    def _forward_device(self, x: torch.Tensor, w: torch.Tensor, ids: torch.Tensor, events=None) -> torch.Tensor:
+        _lib = self._lib
+        T, k = ids.shape
+        if k != self.topk or x.shape[1] != self.hidden:
+            raise ValueError(f"this context was built for top-{self.topk} and hidden {self.hidden}")
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens exceed the context's max_tokens {self.max_tokens}")
+        if x.dtype == torch.float32 and self.row_dtype != torch.bfloat16:
+            raise ValueError("fp32 activations need bf16 rows")
+        if x.dtype not in (torch.float32, self.row_dtype):
+            raise ValueError(f"activations {x.dtype} do not match the rows' {self.row_dtype}")
+        from blackhole_b200.hex_moe import _DT, _aligned, _stream
+        x = _aligned(x)
+        w = _aligned(w.to(torch.float32))
+        ids = _aligned(ids if ids.dtype in (torch.int32, torch.int64) else ids.long())
+        out = torch.empty(T, self.hidden, dtype=x.dtype, device=x.device)
+        ws = self._workspace(self.block_m)
+        st = _stream(self.device)
+        ids_dt = _lib.I64 if ids.dtype == torch.int64 else _lib.I32
+        wsp, wsn = (ws.data_ptr(), ws.numel()) if ws is not None else (None, 0)
+        lay = self._layer.handle if self._layer else None
+        with torch.cuda.device(self.device):
+            if events is None:
+                rc = _lib.lib.hexmoe_ep_forward(self._ctx, lay, x.data_ptr(), _DT[x.dtype], T, w.data_ptr(),
+                                                ids.data_ptr(), ids_dt, out.data_ptr(), _DT[out.dtype], self.block_m,
+                                                wsp, wsn, st)
+                _lib.check(rc, "hexmoe_ep_forward")
+                return out
+            # the three phases apart, with events[0..3] recorded around them
+            cur = torch.cuda.current_stream(self.device)
+            events[0].record(cur)
+            _lib.check(_lib.lib.hexmoe_ep_dispatch(self._ctx, x.data_ptr(), _DT[x.dtype], T, w.data_ptr(),
+                                                   ids.data_ptr(), ids_dt, st), "hexmoe_ep_dispatch")
+            events[1].record(cur)
+            _lib.check(_lib.lib.hexmoe_ep_experts(self._ctx, lay, self.block_m, wsp, wsn, st), "hexmoe_ep_experts")
+            events[2].record(cur)
+            _lib.check(_lib.lib.hexmoe_ep_combine(self._ctx, T, out.data_ptr(), _DT[out.dtype], st),
+                       "hexmoe_ep_combine")
+            events[3].record(cur)
+        return out
+
+    def close(self) -> None:
+        """Collective: waits for every rank, then frees this rank's buffers."""
+        if self._ctx is None:
+            return
+        torch.cuda.synchronize(self.device)
+        if self.shard.world > 1:
+            dist.barrier(group=self.group)
+        self._lib.lib.hexmoe_ep_destroy(self._ctx)
+        self._ctx = None
+        self._ws.clear()
+
+    def __del__(self):
+        ctx = getattr(self, "_ctx", None)
+        if ctx is not None and self.shard.world == 1:
+            self._lib.lib.hexmoe_ep_destroy(ctx)
+            self._ctx = None
+
+    # ------------------------------------------------------------------ CPU ranks
     def _a2a(self, out: torch.Tensor, inp: torch.Tensor, out_splits: list[int], in_splits: list[int]) -> None:
         dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
 
-    def _by_owner(self, owner: torch.Tensor) -> torch.Tensor:
-        """Slot ids ordered by owner rank, stable (slots of one rank keep their
-        order): on the GPU the layer's own align with the ranks as the experts and
-        runs of one slot, elsewhere a stable sort (the same order)."""
-        if owner.is_cuda and owner.numel():
-            from blackhole_b200.hex_moe import align
-            sid, _, _ = align(owner.to(torch.int32), self.shard.world, 1)
-            return sid[:owner.numel()].to(torch.int64)
-        return torch.argsort(owner, stable=True)
-
-    def _local_phases(self, xr: torch.Tensor, wr: torch.Tensor, ir: torch.Tensor) -> torch.Tensor:
-        """The local experts on the received rows, one slot per row: the layer
-        forward up to the per-slot rows (weighted, rounded to the activation
-        dtype) in one call, so the layer's top-1 combine (a copy) is skipped."""
-        n = xr.shape[0]
-        return self._layer.forward_slots(xr, wr.reshape(n, 1), ir.reshape(n, 1), self.block_m)
-
-    def forward(self, x: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.Tensor) -> torch.Tensor:
-        if x.dim() != 2 or topk_ids.dim() != 2 or topk_weights.shape != topk_ids.shape or x.shape[0] != topk_ids.shape[0]:
-            raise ValueError("x [T, H], topk_weights and topk_ids [T, k] expected")
-        T, k = topk_ids.shape
+    def _forward_host(self, x: torch.Tensor, w: torch.Tensor, ids: torch.Tensor) -> torch.Tensor:
+        T, k = ids.shape
         H = x.shape[1]
-        dev = x.device
         world, E = self.shard.world, self.shard.num_experts
-        ids = topk_ids.reshape(-1).to(torch.int64)
-        w = topk_weights.reshape(-1).to(torch.float32)
-        # 1. per destination rank: slot count and this rank's argument-error flag,
-        #    exchanged in one all-to-all and read on the host once, so a bad call
-        #    fails on every rank before any data moves
-        bad = ((ids < 0) | (ids >= E)).any().to(torch.int64)
-        owner = self.shard.owner(ids.clamp(0, max(E - 1, 0)))
-        # (torch.bincount would read its input's maximum on the host: a second sync)
-        send_counts = (owner.unsqueeze(1) == torch.arange(world, device=dev)).sum(0, dtype=torch.int64)
-        info = torch.stack([send_counts, bad.expand(world)], 1).contiguous()
+        rdt = _row_dtype(x.dtype)
+        ids = ids.to(torch.int64)
+        w = w.to(torch.float32)
+        bad = bool(((ids < 0) | (ids >= E)).any())
+        plan = plan_dispatch(ids.clamp(0, max(E - 1, 0)), self.shard)
+        # 1. rows, slots and this rank's error flag per destination, read on the host
+        info = torch.tensor([[len(plan.rows[d]), len(plan.slots[d][0]), int(bad)] for d in range(world)],
+                            dtype=torch.int64)
         recv_info = torch.empty_like(info)
         dist.all_to_all_single(recv_info, info, group=self.group)
-        host = torch.cat([send_counts, recv_info.reshape(-1)]).tolist()
-        sc, rc, flags = host[:world], host[world::2], host[world + 1::2]
-        if any(flags):
-            mine = flags[dist.get_rank(self.group)]
-            raise ValueError("topk_ids out of range" if mine else "topk_ids out of range on another rank")
-        n_recv = sum(rc)
-        order = self._by_owner(owner)
-        # 2. token rows, ids and weights of the slots, grouped by owner
-        send_x = x.index_select(0, torch.div(order, k, rounding_mode="floor"))
-        recv_x = torch.empty(n_recv, H, dtype=x.dtype, device=dev)
-        self._a2a(recv_x, send_x, rc, sc)
-        # expert id (high word) and top-k weight bits (low word) of each slot, one int64
-        meta = ((ids << 32) | (w.view(torch.int32).to(torch.int64) & 0xFFFFFFFF)).index_select(0, order)
-        recv_meta = torch.empty(n_recv, dtype=torch.int64, device=dev)
-        self._a2a(recv_meta, meta, rc, sc)
-        recv_ids = (recv_meta >> 32).to(torch.int32)
-        recv_w = (recv_meta & 0xFFFFFFFF).to(torch.int32).view(torch.float32)
-        # 3. local experts, one slot per row
-        out_dt = x.dtype if x.dtype in (torch.bfloat16, torch.float16) else torch.bfloat16
-        if n_recv:
-            if self._cuda and self._layer is None:
-                raise RuntimeError("slots were routed to a rank that holds no experts")
-            y_recv = self.expert_fn(recv_x, recv_w, recv_ids).to(out_dt).contiguous()
-        else:
-            y_recv = torch.empty(0, H, dtype=out_dt, device=dev)
-        # 4. rows back to their source rank, in the order they were sent
-        back = torch.empty(T * k, H, dtype=out_dt, device=dev)
-        self._a2a(back, y_recv, sc, rc)
-        if T == 0:
-            return torch.empty(0, H, dtype=x.dtype, device=dev)
-        # 5. combine the k slots of each token: slot order[i] came back as row i
-        if self._cuda:
-            from blackhole_b200.hex_moe import combine_rows
-            rows = torch.empty(T * k, dtype=torch.int32, device=dev)
-            rows.index_copy_(0, order, torch.arange(T * k, dtype=torch.int32, device=dev))
-            return combine_rows(back, T, k, rows, out_dtype=x.dtype)
-        y = torch.empty_like(back)
-        y.index_copy_(0, order, back)
-        return self.combine_fn(y, T, k).to(x.dtype)
+        if bool(recv_info[:, 2].any()) or bad:
+            raise ValueError("topk_ids out of range" if bad else "topk_ids out of range on another rank")
+        sent_rows = [len(r) for r in plan.rows]
+        sent_slots = [len(s[0]) for s in plan.slots]
+        got_rows, got_slots = recv_info[:, 0].tolist(), recv_info[:, 1].tolist()
+        # 2. one row per (token, destination); one record per slot: (row at the destination, expert, weight bits)
+        send_x = torch.cat([x[r].to(rdt) for r in plan.rows]) if T else x.new_zeros(0, H, dtype=rdt)
+        recv_x = torch.empty(sum(got_rows), H, dtype=rdt)
+        self._a2a(recv_x, send_x, got_rows, sent_rows)
+        recs = []
+        for d, (t_idx, j_idx) in enumerate(plan.slots):
+            wbits = w[t_idx, j_idx].view(torch.int32).to(torch.int64)
+            recs.append(torch.stack([plan.pos[t_idx, d], ids[t_idx, j_idx], wbits], 1))
+        send_rec = torch.cat(recs) if recs else torch.zeros(0, 3, dtype=torch.int64)
+        recv_rec = torch.empty(sum(got_slots), 3, dtype=torch.int64)
+        self._a2a(recv_rec, send_rec, got_slots, sent_slots)
+        # 3. the local experts, one slot per row
+        row_base = torch.tensor([0] + got_rows[:-1], dtype=torch.int64).cumsum(0)
+        src_of_slot = torch.repeat_interleave(torch.arange(world), torch.tensor(got_slots))
+        row = row_base[src_of_slot] + recv_rec[:, 0]
+        e = recv_rec[:, 1]
+        wr = recv_rec[:, 2].to(torch.int32).view(torch.float32)
+        n_rows = recv_x.shape[0]
+        part = torch.zeros(n_rows, H, dtype=torch.float32)
+        if row.numel():
+            y = self.expert_fn(recv_x[row], wr, e).to(rdt).float()
+            # 4. per received row, its slots in j order (contiguous, in order): level by level
+            first = torch.ones_like(row, dtype=torch.bool)
+            first[1:] = row[1:] != row[:-1]
+            start = torch.nonzero(first).flatten()
+            level = torch.arange(row.numel()) - torch.repeat_interleave(start, torch.diff(
+                torch.cat([start, torch.tensor([row.numel()])])))
+            for lv in range(int(level.max()) + 1):
+                sel = level == lv
+                part[row[sel]] += y[sel]
+        back_rows = part.to(rdt)
+        ret = torch.empty(sum(sent_rows), H, dtype=rdt)
+        self._a2a(ret, back_rows, sent_rows, got_rows)
+        # 5. combine in rank order
+        out = torch.zeros(T, H, dtype=torch.float32)
+        base = 0
+        for d in range(world):
+            tok = plan.rows[d]
+            out[tok] += ret[base:base + len(tok)].float()
+            base += len(tok)
+        return out.to(x.dtype)
+
+    # ------------------------------------------------------------------ entry
+    def forward(self, x: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.Tensor,
+                events=None) -> torch.Tensor:
+        """events (GPU path, optional): four torch.cuda.Event recorded before
+        dispatch, before experts, before combine and after it."""
+        if x.dim() != 2 or topk_ids.dim() != 2 or topk_weights.shape != topk_ids.shape or x.shape[0] != topk_ids.shape[0]:
+            raise ValueError("x [T, H], topk_weights and topk_ids [T, k] expected")
+        if self.expert_fn is not None:
+            return self._forward_host(x, topk_weights, topk_ids)
+        return self._forward_device(x, topk_weights, topk_ids, events)
 
     __call__ = forward
+
+
+def reference_combine(y_slots: torch.Tensor, ids: torch.Tensor, shard: ExpertShard, out_dtype) -> torch.Tensor:
+    """What EPMoE returns, from the single-GPU layer's per-slot rows y [T * k, H]
+    (hexmoe_forward_slots): per rank (in rank order) the fp32 sum of the token's
+    slots it owns in j order, rounded to y's dtype, then the fp32 sum of those
+    partials, rounded to out_dtype.  Any device."""
+    T, k = ids.shape
+    yv = y_slots.view(T, k, -1).float()
+    owner = shard.owner(ids.to(torch.int64))
+    out = torch.zeros(T, yv.shape[2], dtype=torch.float32, device=y_slots.device)
+    for d in range(shard.world):
+        part = torch.zeros_like(out)
+        for j in range(k):
+            m = (owner[:, j] == d).to(torch.float32)[:, None]
+            part = torch.where(m > 0, part + yv[:, j], part)
+        out = out + part.to(y_slots.dtype).float()
+    return out.to(out_dtype)

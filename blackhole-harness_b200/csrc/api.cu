@@ -401,9 +401,13 @@ size_t hexmoe_forward_workspace_bytes(const hexmoe_layer* layer, int64_t tokens,
 namespace {
 
 // hexmoe_forward, or with slots_out its per-slot rows instead of the combine.
+// slot_row (optional): the x row of every slot (else slot / topk); seg_counts /
+// seg_len (optional): a ragged slot space, of which only the first
+// seg_counts[g] slots of every seg_len-slot segment exist (expert parallelism).
 int forward_impl(const hexmoe_layer* layer, const void* x, int32_t x_dtype, int64_t tokens, int32_t topk,
                  const float* topk_weights, const void* topk_ids, int32_t ids_dtype, void* out, int32_t out_dtype,
-                 void* slots_out, int32_t block_m, void* workspace, size_t workspace_bytes, void* stream) {
+                 void* slots_out, int32_t block_m, void* workspace, size_t workspace_bytes, void* stream,
+                 const int32_t* slot_row = nullptr, const int32_t* seg_counts = nullptr, int64_t seg_len = 0) {
   if (!layer) return fail(HEXMOE_E_ARG, "hexmoe_forward: null layer");
   const hexmoe_layer_desc& d = layer->desc;
   if (tokens < 0 || topk <= 0 || topk > d.num_experts) return fail(HEXMOE_E_ARG, "tokens %lld / topk %d", static_cast<long long>(tokens), topk);
@@ -441,10 +445,10 @@ int forward_impl(const hexmoe_layer* layer, const void* x, int32_t x_dtype, int6
   void* xs = ws + w.xs;
   cudaError_t e = launch_align(topk_ids, ids_dtype == HEXMOE_I64, S, d.num_experts, bm, sid, eid, npp,
                                reinterpret_cast<int32_t*>(ws + w.align), align_scratch_bytes(S, d.num_experts), dev_err,
-                               st, true);
+                               st, true, seg_counts, seg_len);
   if (e != cudaSuccess) return cuda_fail(e, "align launch");
 
-  e = launch_gather_rows(x, x_dtype, tokens, d.hidden, sid, npp, w.max_blocks * bm, topk, S, xs, st, true);
+  e = launch_gather_rows(x, x_dtype, tokens, d.hidden, sid, npp, w.max_blocks * bm, topk, S, xs, st, true, slot_row);
   if (e != cudaSuccess) return cuda_fail(e, "gather launch");
   int rc = run_gate_up(layer, xs, bf16, tokens, topk, sid, eid, npp, bm, act, dev_err, st, true);
   if (rc) return rc;
@@ -460,6 +464,32 @@ int forward_impl(const hexmoe_layer* layer, const void* x, int32_t x_dtype, int6
 }
 
 }  // namespace
+
+const hexmoe_layer_desc* hexmoe::layer_desc(const hexmoe_layer* layer) { return layer ? &layer->desc : nullptr; }
+
+size_t hexmoe::slots_workspace_bytes(const hexmoe_layer* layer, int64_t num_slots, int32_t block_m) {
+  if (!layer || num_slots < 0) return 0;
+  const int bm = block_m > 0 ? block_m : auto_block_m(num_slots, layer->desc.num_experts);
+  return ws_layout(layer->desc, num_slots, 1, bm, HEXMOE_BF16).total;
+}
+
+int hexmoe::forward_slot_space(const hexmoe_layer* layer, const void* x, int32_t x_dtype, int64_t num_slots,
+                               const int32_t* slot_expert, const float* slot_weight, const int32_t* slot_row,
+                               const int32_t* seg_counts, int64_t seg_len, void* y, int32_t block_m, void* workspace,
+                               size_t workspace_bytes, cudaStream_t st, void** y_used) {
+  if (!layer) return fail(HEXMOE_E_ARG, "forward_slot_space: null layer");
+  if (!y) {
+    // the per-slot rows go to the workspace's own y region
+    const int bm = block_m > 0 ? block_m : auto_block_m(num_slots, layer->desc.num_experts);
+    const WsLayout w = ws_layout(layer->desc, num_slots, 1, bm, x_dtype);
+    if (!workspace || workspace_bytes < w.total) return fail(HEXMOE_E_ARG, "forward_slot_space: workspace too small");
+    y = static_cast<char*>(workspace) + w.y;
+  }
+  if (y_used) *y_used = y;
+  return forward_impl(layer, x, x_dtype, num_slots, 1, slot_weight, slot_expert, HEXMOE_I32, y,
+                      x_dtype == HEXMOE_F16 ? HEXMOE_F16 : HEXMOE_BF16, y, block_m, workspace, workspace_bytes, st,
+                      slot_row, seg_counts, seg_len);
+}
 
 extern "C" {
 

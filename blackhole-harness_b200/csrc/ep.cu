@@ -1,0 +1,668 @@
+// ep.cu — expert parallelism for the HEX MoE layer over peer memory
+// (hexmoe_ep_*).  The reference runs one GPU and refuses expert parallelism
+// (runtime/blackhole_runtime/vllm_hex.py:101-102); this is new work.
+//
+// Experts are sharded contiguously: rank r owns global experts [r*P, (r+1)*P),
+// P = ceil(E / world).  Every rank owns one region of device memory that it
+// exports by CUDA IPC and every other rank maps, so kernels on any rank store
+// straight into any rank's region over NVLink (plain stores, no multicast):
+//
+//   flags      disp[world], ret[world] (uint64): the epoch a source's dispatch /
+//              a destination's return has completed, written with release
+//              stores at system scope, polled with acquire loads
+//   counts     rows[world], slots[world]: what each source sent this epoch
+//   recv_x     [world][cap][H] 16-bit: one row per (token, this rank) pair of
+//              each source, in the source's token order
+//   rec_row    [world][seg_len] int32: per received slot, its row (src*cap + pos)
+//   rec_exp    [world][seg_len] int32: per received slot, its global expert
+//   rec_w      [world][seg_len] f32:   per received slot, its top-k weight
+//   rowslot    [world][cap+1] int32: first slot of every received row (the
+//              slots of one row are contiguous, in the token's j order)
+//   ret        [world][cap][H] 16-bit: the partial sums each destination rank
+//              returns for this rank's tokens, in the order they were sent
+//
+// One forward, all on the caller's stream, no host synchronisation:
+//   plan      (1 CTA) epoch += 1; per token and destination rank, the row
+//             position and the first slot offset (stable scans over tokens)
+//   send      (all SMs) each token row read once and stored to every rank that
+//             owns one of its experts, with its slot records; the last CTA
+//             writes the counts and raises disp[me] = epoch on every rank
+//   wait      (1 CTA) disp[src] >= epoch for every source (bounded)
+//   experts   the layer over the received slots (align over the ragged slot
+//             space, gather through rec_row, gate/up, down) -> per-slot rows
+//   return    (all SMs) per received row, its slots summed in j order in fp32,
+//             rounded once, stored into the source's ret; the last CTA raises
+//             ret[me] = epoch on every rank
+//   wait      ret[d] >= epoch for every destination (bounded)
+//   combine   out[t] = sum over ranks d in rank order of ret[d][pos(t, d)],
+//             fp32, rounded once
+//
+// Buffers are single: a source writes rank d's receive rows for epoch e only
+// after its own combine of epoch e-1 saw d's return of e-1, which d raised
+// after its experts and return had read everything of e-1; and d writes a
+// source's ret for epoch e only after it saw that source's dispatch of e,
+// issued after the source's combine of e-1 had read ret.  So every rank must
+// run every forward (the same sequence of calls on every rank).  Every wait is
+// bounded (2 s): a missing peer sets the device error word (timeout) instead of
+// hanging the GPU.
+#include <algorithm>
+#include <cstring>
+#include <type_traits>
+
+#include "decode.cuh"
+#include "internal.cuh"
+
+namespace hexmoe {
+
+constexpr int kEpMaxWorld = HEXMOE_EP_MAX_WORLD;
+constexpr uint64_t kEpWaitNs = 2000000000ull;
+
+struct EpArgs {
+  uint8_t* peer[kEpMaxWorld];   // every rank's region base (own included)
+  uint8_t* self;
+  int32_t rank, world, E, P, H, topk;
+  int64_t cap, seg_len;
+  // region offsets
+  uint64_t o_disp, o_ret_flag, o_rows, o_slots, o_x, o_row, o_exp, o_w, o_rowslot, o_ret;
+  // this rank's private state
+  int64_t* epoch;
+  uint32_t* done;               // [2]: CTAs finished in send / return
+  int32_t* tot;                 // [world][2]: rows and slots sent to every rank
+  int32_t* pos;                 // [cap][world]: row position of token t at rank d, -1 = none
+  int32_t* soff;                // [cap][world]: first slot offset of token t at rank d
+  int32_t* dev_err;
+};
+
+__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+template <typename T>
+__device__ __forceinline__ T* at(uint8_t* base, uint64_t off) {
+  return reinterpret_cast<T*>(base + off);
+}
+
+// ---------------------------------------------------------------- plan
+// Counts of token t per destination, packed rows << 32 | slots.
+template <bool I64>
+__device__ __forceinline__ void token_counts(const EpArgs& a, const void* ids, int64_t t, int64_t (&c)[kEpMaxWorld],
+                                             bool report) {
+#pragma unroll
+  for (int d = 0; d < kEpMaxWorld; ++d) c[d] = 0;
+  for (int j = 0; j < a.topk; ++j) {
+    const int64_t e = I64 ? static_cast<const int64_t*>(ids)[t * a.topk + j]
+                          : static_cast<const int32_t*>(ids)[t * a.topk + j];
+    if (e < 0 || e >= a.E) {
+      if (report) atomicOr(a.dev_err, kDevErrExpertId);
+      continue;
+    }
+    const int d = static_cast<int>(e / a.P);
+#pragma unroll
+    for (int q = 0; q < kEpMaxWorld; ++q)
+      if (q == d) c[q] += 1;
+  }
+#pragma unroll
+  for (int d = 0; d < kEpMaxWorld; ++d)
+    if (c[d]) c[d] += 1ll << 32;
+}
+
+constexpr int kPlanThreads = 1024;
+
+template <bool I64>
+__global__ void __launch_bounds__(kPlanThreads, 1) ep_plan_kernel(EpArgs a, const void* __restrict__ ids, int64_t T) {
+  __shared__ int64_t wtot[32][kEpMaxWorld];
+  __shared__ int64_t wbase[32][kEpMaxWorld];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) *a.epoch = *a.epoch + 1;
+  const int64_t per = (T + kPlanThreads - 1) / kPlanThreads;
+  const int64_t t0 = min(static_cast<int64_t>(tid) * per, T), t1 = min(t0 + per, T);
+  int64_t run[kEpMaxWorld];
+#pragma unroll
+  for (int d = 0; d < kEpMaxWorld; ++d) run[d] = 0;
+  for (int64_t t = t0; t < t1; ++t) {
+    int64_t c[kEpMaxWorld];
+    token_counts<I64>(a, ids, t, c, true);
+#pragma unroll
+    for (int d = 0; d < kEpMaxWorld; ++d) run[d] += c[d];
+  }
+  // exclusive scan over threads (token ranges are in thread order)
+  int64_t incl[kEpMaxWorld];
+#pragma unroll
+  for (int d = 0; d < kEpMaxWorld; ++d) {
+    int64_t v = run[d];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int64_t u = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v += u;
+    }
+    incl[d] = v;
+    if (lane == 31) wtot[warp][d] = v;
+  }
+  __syncthreads();
+  if (warp == 0) {
+#pragma unroll
+    for (int d = 0; d < kEpMaxWorld; ++d) {
+      const int64_t own = wtot[lane][d];
+      int64_t v = own;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int64_t u = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += u;
+      }
+      wbase[lane][d] = v - own;
+      if (lane == 31 && d < a.world) {
+        a.tot[2 * d] = static_cast<int32_t>(v >> 32);
+        a.tot[2 * d + 1] = static_cast<int32_t>(v & 0xffffffffll);
+      }
+    }
+  }
+  __syncthreads();
+  int64_t base[kEpMaxWorld];
+#pragma unroll
+  for (int d = 0; d < kEpMaxWorld; ++d) base[d] = wbase[warp][d] + incl[d] - run[d];
+  for (int64_t t = t0; t < t1; ++t) {
+    int64_t c[kEpMaxWorld];
+    token_counts<I64>(a, ids, t, c, false);
+#pragma unroll
+    for (int d = 0; d < kEpMaxWorld; ++d) {
+      if (d >= a.world) break;
+      a.pos[t * a.world + d] = c[d] ? static_cast<int32_t>(base[d] >> 32) : -1;
+      a.soff[t * a.world + d] = static_cast<int32_t>(base[d] & 0xffffffffll);
+      base[d] += c[d];
+    }
+  }
+}
+
+// ---------------------------------------------------------------- send
+// A warp per token: its row is read once (8 x 16 B per lane per 2048 inputs)
+// and stored to every destination rank; lanes j < topk write the slot records.
+constexpr int kSendThreads = 256;
+
+template <typename XT, bool I64>
+__global__ void __launch_bounds__(kSendThreads) ep_send_kernel(EpArgs a, const XT* __restrict__ x,
+                                                                const void* __restrict__ ids,
+                                                                const float* __restrict__ w, int64_t T) {
+  const int lane = threadIdx.x & 31;
+  const int64_t epoch = *a.epoch;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * kSendThreads) >> 5;
+  const int hv = a.H / 8;                         // 16-byte vectors of 8 16-bit values per row
+  for (int64_t t = (blockIdx.x * static_cast<int64_t>(kSendThreads) + threadIdx.x) >> 5; t < T; t += nwarps) {
+    int32_t pos[kEpMaxWorld], so[kEpMaxWorld];
+#pragma unroll
+    for (int d = 0; d < kEpMaxWorld; ++d) {
+      pos[d] = d < a.world ? __ldg(a.pos + t * a.world + d) : -1;
+      so[d] = d < a.world ? __ldg(a.soff + t * a.world + d) : 0;
+    }
+    for (int c0 = 0; c0 < hv; c0 += 8 * 32) {
+      uint4 v[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int c = c0 + i * 32 + lane;
+        if (c < hv) {
+          if constexpr (sizeof(XT) == 2) {
+            v[i] = __ldg(reinterpret_cast<const uint4*>(x + t * a.H) + c);
+          } else {
+            const float4 p0 = __ldg(reinterpret_cast<const float4*>(x + t * a.H) + 2 * c);
+            const float4 p1 = __ldg(reinterpret_cast<const float4*>(x + t * a.H) + 2 * c + 1);
+            v[i] = make_uint4(pack2<true>(p0.x, p0.y), pack2<true>(p0.z, p0.w), pack2<true>(p1.x, p1.y),
+                              pack2<true>(p1.z, p1.w));
+          }
+        }
+      }
+#pragma unroll
+      for (int d = 0; d < kEpMaxWorld; ++d) {
+        if (pos[d] < 0) continue;
+        uint4* dst = at<uint4>(a.peer[d], a.o_x) + (static_cast<int64_t>(a.rank) * a.cap + pos[d]) * hv;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int c = c0 + i * 32 + lane;
+          if (c < hv) dst[c] = v[i];
+        }
+      }
+    }
+    // slot records (topk <= 32): the j-th slot of token t at its owner rank d
+    int64_t e = -1;
+    if (lane < a.topk)
+      e = I64 ? __ldg(static_cast<const int64_t*>(ids) + t * a.topk + lane)
+              : static_cast<int64_t>(__ldg(static_cast<const int32_t*>(ids) + t * a.topk + lane));
+    const bool ok = lane < a.topk && e >= 0 && e < a.E;
+    const int d = ok ? static_cast<int>(e / a.P) : -1 - lane;
+    const unsigned same = __match_any_sync(0xffffffffu, d);
+    if (ok) {
+      const int rk = __popc(same & ((1u << lane) - 1u));
+      int32_t my_pos = 0, my_so = 0;
+#pragma unroll
+      for (int q = 0; q < kEpMaxWorld; ++q)
+        if (q == d) { my_pos = pos[q]; my_so = so[q]; }
+      uint8_t* R = a.peer[d];
+      const int64_t seg = static_cast<int64_t>(a.rank) * a.seg_len;
+      at<int32_t>(R, a.o_row)[seg + my_so + rk] = static_cast<int32_t>(a.rank * a.cap + my_pos);
+      at<int32_t>(R, a.o_exp)[seg + my_so + rk] = static_cast<int32_t>(e);
+      at<float>(R, a.o_w)[seg + my_so + rk] = __ldg(w + t * a.topk + lane);
+      if (rk == 0) at<int32_t>(R, a.o_rowslot)[static_cast<int64_t>(a.rank) * (a.cap + 1) + my_pos] = my_so;
+    }
+  }
+  // the last CTA to finish publishes the counts and raises the dispatch flags
+  __shared__ bool last;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    last = atomicAdd(a.done, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (last && threadIdx.x < a.world) {
+    __threadfence_system();
+    const int d = threadIdx.x;
+    uint8_t* R = a.peer[d];
+    const int32_t rows = a.tot[2 * d], slots = a.tot[2 * d + 1];
+    at<int32_t>(R, a.o_rows)[a.rank] = rows;
+    at<int32_t>(R, a.o_slots)[a.rank] = slots;
+    at<int32_t>(R, a.o_rowslot)[static_cast<int64_t>(a.rank) * (a.cap + 1) + rows] = slots;
+    __threadfence_system();
+    st_release_sys(at<uint64_t>(R, a.o_disp) + a.rank, static_cast<uint64_t>(epoch));
+  }
+  if (last && threadIdx.x == 0) *a.done = 0;
+}
+
+// ---------------------------------------------------------------- wait
+// Thread d polls flag[d] of this rank's region until it reaches the epoch;
+// gives up after kEpWaitNs with the timeout bit in the device error word.
+__global__ void ep_wait_kernel(EpArgs a, uint64_t o_flags) {
+  const int d = threadIdx.x;
+  if (d < a.world) {
+    const uint64_t want = static_cast<uint64_t>(*a.epoch);
+    const uint64_t* f = at<uint64_t>(a.self, o_flags) + d;
+    if (ld_acquire_sys(f) < want) {
+      const uint64_t t0 = globaltimer();
+      while (ld_acquire_sys(f) < want) {
+        if (globaltimer() - t0 > kEpWaitNs) {
+          atomicOr(a.dev_err, kDevErrTimeout);
+          break;
+        }
+        __nanosleep(100);
+      }
+    }
+  }
+  __syncthreads();
+}
+
+// ---------------------------------------------------------------- return
+// A warp per received row: its slots' rows of y summed in slot (j) order in
+// fp32, rounded once to the row type and stored into the source's ret.
+template <typename YT>
+__global__ void __launch_bounds__(kSendThreads) ep_return_kernel(EpArgs a, const YT* __restrict__ y) {
+  const int lane = threadIdx.x & 31;
+  const int64_t epoch = *a.epoch;
+  int64_t start[kEpMaxWorld + 1];
+  start[0] = 0;
+#pragma unroll
+  for (int d = 0; d < kEpMaxWorld; ++d)
+    start[d + 1] = start[d] + (d < a.world ? __ldg(at<int32_t>(a.self, a.o_rows) + d) : 0);
+  const int64_t total = start[kEpMaxWorld];
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * kSendThreads) >> 5;
+  const int hv = a.H / 8;
+  for (int64_t g = (blockIdx.x * static_cast<int64_t>(kSendThreads) + threadIdx.x) >> 5; g < total; g += nwarps) {
+    int src = 0;
+#pragma unroll
+    for (int d = 1; d < kEpMaxWorld; ++d)
+      if (g >= start[d]) src = d;
+    const int64_t rho = g - start[src];
+    const int32_t* rs = at<int32_t>(a.self, a.o_rowslot) + static_cast<int64_t>(src) * (a.cap + 1);
+    const int32_t s0 = __ldg(rs + rho), s1 = __ldg(rs + rho + 1);
+    const YT* ybase = y + (static_cast<int64_t>(src) * a.seg_len) * a.H;
+    uint4* dst = at<uint4>(a.peer[src], a.o_ret) + (static_cast<int64_t>(a.rank) * a.cap + rho) * hv;
+    for (int c0 = 0; c0 < hv; c0 += 4 * 32) {
+      float acc[4][8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc[i][q] = 0.f;
+      for (int s = s0; s < s1; ++s) {
+        const uint4* row = reinterpret_cast<const uint4*>(ybase + static_cast<int64_t>(s) * a.H);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int c = c0 + i * 32 + lane;
+          if (c < hv) {
+            const uint4 v = __ldg(row + c);
+            const YT* e = reinterpret_cast<const YT*>(&v);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) acc[i][q] += static_cast<float>(e[q]);
+          }
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int c = c0 + i * 32 + lane;
+        if (c < hv) {
+          constexpr bool kBf16 = std::is_same<YT, __nv_bfloat16>::value;
+          dst[c] = make_uint4(pack2<kBf16>(acc[i][0], acc[i][1]), pack2<kBf16>(acc[i][2], acc[i][3]),
+                              pack2<kBf16>(acc[i][4], acc[i][5]), pack2<kBf16>(acc[i][6], acc[i][7]));
+        }
+      }
+    }
+  }
+  __shared__ bool last;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    last = atomicAdd(a.done + 1, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (last && threadIdx.x < a.world) {
+    __threadfence_system();
+    st_release_sys(at<uint64_t>(a.peer[threadIdx.x], a.o_ret_flag) + a.rank, static_cast<uint64_t>(epoch));
+  }
+  if (last && threadIdx.x == 0) a.done[1] = 0;
+}
+
+// ---------------------------------------------------------------- combine
+// out[t, h] = sum over ranks d (in rank order) holding a row of t of ret[d][pos],
+// fp32, rounded once.
+template <typename YT, int OUT>
+__global__ void ep_combine_kernel(EpArgs a, int64_t T, void* __restrict__ out) {
+  const int hv = a.H / 8;
+  const int64_t total = T * hv;
+  const YT* ret = at<const YT>(a.self, a.o_ret);
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t t = i / hv;
+    const int c = static_cast<int>(i % hv);
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int d = 0; d < a.world; ++d) {
+      const int32_t p = __ldg(a.pos + t * a.world + d);
+      if (p < 0) continue;
+      const uint4 v = *(reinterpret_cast<const uint4*>(ret + (static_cast<int64_t>(d) * a.cap + p) * a.H) + c);
+      const YT* e = reinterpret_cast<const YT*>(&v);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) acc[q] += static_cast<float>(e[q]);
+    }
+    const int64_t o = t * a.H + c * 8;
+    if (OUT == HEXMOE_F32) {
+      float4* dd = reinterpret_cast<float4*>(static_cast<float*>(out) + o);
+      dd[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      dd[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    } else {
+      uint4 r;
+      uint32_t* rr = reinterpret_cast<uint32_t*>(&r);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) rr[q] = pack2<OUT == HEXMOE_BF16>(acc[2 * q], acc[2 * q + 1]);
+      *reinterpret_cast<uint4*>(static_cast<uint16_t*>(out) + o) = r;
+    }
+  }
+}
+
+}  // namespace hexmoe
+
+using namespace hexmoe;
+
+struct hexmoe_ep {
+  int device, rank, world, E, P, H, topk, row_dtype;
+  int64_t cap, seg_len;
+  uint64_t o_disp, o_ret_flag, o_rows, o_slots, o_x, o_row, o_exp, o_w, o_rowslot, o_ret;
+  size_t region_bytes;
+  uint8_t* region;
+  uint8_t* peer[kEpMaxWorld];
+  bool opened[kEpMaxWorld];
+  bool connected;
+  uint8_t* local;
+  int64_t* epoch;
+  uint32_t* done;
+  int32_t *tot, *pos, *soff;
+  int64_t last_tokens;
+};
+
+namespace {
+
+size_t up256(size_t v) { return (v + 255) / 256 * 256; }
+
+EpArgs ep_args(const hexmoe_ep* ep, int32_t* dev_err) {
+  EpArgs a{};
+  for (int d = 0; d < kEpMaxWorld; ++d) a.peer[d] = d < ep->world ? ep->peer[d] : nullptr;
+  a.self = ep->region;
+  a.rank = ep->rank; a.world = ep->world; a.E = ep->E; a.P = ep->P; a.H = ep->H; a.topk = ep->topk;
+  a.cap = ep->cap; a.seg_len = ep->seg_len;
+  a.o_disp = ep->o_disp; a.o_ret_flag = ep->o_ret_flag; a.o_rows = ep->o_rows; a.o_slots = ep->o_slots;
+  a.o_x = ep->o_x; a.o_row = ep->o_row; a.o_exp = ep->o_exp; a.o_w = ep->o_w; a.o_rowslot = ep->o_rowslot;
+  a.o_ret = ep->o_ret;
+  a.epoch = ep->epoch; a.done = ep->done; a.tot = ep->tot; a.pos = ep->pos; a.soff = ep->soff;
+  a.dev_err = dev_err;
+  return a;
+}
+
+int ep_check(const hexmoe_ep* ep, const char* what) {
+  if (!ep) return report_error(HEXMOE_E_ARG, what);
+  if (!ep->connected) return report_error(HEXMOE_E_ARG, "expert parallel context is not connected (hexmoe_ep_connect)");
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev != ep->device) return report_error(HEXMOE_E_ARG, "expert parallel context belongs to another device");
+  return HEXMOE_OK;
+}
+
+int grid_for(int64_t work_warps, int per_cta_warps) {
+  int sms = 148;
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t want = (work_warps + per_cta_warps - 1) / per_cta_warps;
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, static_cast<int64_t>(sms) * 8)));
+}
+
+}  // namespace
+
+extern "C" {
+
+int hexmoe_ep_init(int32_t rank, int32_t world, int32_t num_experts, int32_t hidden, int32_t topk,
+                   int64_t max_tokens, int32_t row_dtype, hexmoe_ep** out) {
+  if (!out) return report_error(HEXMOE_E_ARG, "hexmoe_ep_init: null out");
+  *out = nullptr;
+  if (world < 1 || world > kEpMaxWorld || rank < 0 || rank >= world)
+    return report_error(HEXMOE_E_ARG, "hexmoe_ep_init: rank / world outside 0 <= rank < world <= 8");
+  if (num_experts <= 0 || hidden <= 0 || hidden % 8 || topk <= 0 || topk > 32 || topk > num_experts || max_tokens <= 0)
+    return report_error(HEXMOE_E_ARG, "hexmoe_ep_init: bad experts / hidden / topk / max_tokens");
+  if (row_dtype != HEXMOE_BF16 && row_dtype != HEXMOE_F16)
+    return report_error(HEXMOE_E_DTYPE, "hexmoe_ep_init: rows are BF16 or F16");
+  if (max_tokens * topk >= (1ll << 31) / world) return report_error(HEXMOE_E_ARG, "hexmoe_ep_init: max_tokens too large");
+  auto* ep = new hexmoe_ep();
+  cudaGetDevice(&ep->device);
+  ep->rank = rank; ep->world = world; ep->E = num_experts; ep->P = (num_experts + world - 1) / world;
+  ep->H = hidden; ep->topk = topk; ep->row_dtype = row_dtype; ep->cap = max_tokens;
+  ep->seg_len = (max_tokens * topk + 2047) / 2048 * 2048;
+  const size_t W = static_cast<size_t>(world);
+  size_t off = 0;
+  ep->o_disp = off; off += 8 * kEpMaxWorld;
+  ep->o_ret_flag = off; off += 8 * kEpMaxWorld;
+  ep->o_rows = off; off += 4 * kEpMaxWorld;
+  ep->o_slots = off; off += 4 * kEpMaxWorld;
+  off = up256(off);
+  const size_t header = off;
+  ep->o_x = off; off = up256(off + W * ep->cap * hidden * 2);
+  ep->o_row = off; off = up256(off + W * ep->seg_len * 4);
+  ep->o_exp = off; off = up256(off + W * ep->seg_len * 4);
+  ep->o_w = off; off = up256(off + W * ep->seg_len * 4);
+  ep->o_rowslot = off; off = up256(off + W * (ep->cap + 1) * 4);
+  ep->o_ret = off; off = up256(off + W * ep->cap * hidden * 2);
+  ep->region_bytes = off;
+  cudaError_t e = cudaMalloc(&ep->region, ep->region_bytes);
+  if (e != cudaSuccess) { delete ep; return report_cuda_error(e, "hexmoe_ep_init: region allocation"); }
+  const size_t local_bytes = up256(8 + 8) + up256(W * 2 * 4) + 2 * up256(ep->cap * W * 4);
+  e = cudaMalloc(&ep->local, local_bytes);
+  if (e == cudaSuccess) e = cudaMemset(ep->region, 0, header);
+  if (e == cudaSuccess) e = cudaMemset(ep->local, 0, local_bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    cudaFree(ep->region);
+    if (ep->local) cudaFree(ep->local);
+    delete ep;
+    return report_cuda_error(e, "hexmoe_ep_init: local state");
+  }
+  ep->epoch = reinterpret_cast<int64_t*>(ep->local);
+  ep->done = reinterpret_cast<uint32_t*>(ep->local + 8);
+  ep->tot = reinterpret_cast<int32_t*>(ep->local + up256(16));
+  ep->pos = reinterpret_cast<int32_t*>(ep->local + up256(16) + up256(W * 8));
+  ep->soff = reinterpret_cast<int32_t*>(ep->local + up256(16) + up256(W * 8) + up256(ep->cap * W * 4));
+  for (int d = 0; d < kEpMaxWorld; ++d) { ep->peer[d] = nullptr; ep->opened[d] = false; }
+  ep->peer[rank] = ep->region;
+  ep->connected = world == 1;
+  *out = ep;
+  return HEXMOE_OK;
+}
+
+int hexmoe_ep_handle(const hexmoe_ep* ep, void* handle_out) {
+  if (!ep || !handle_out) return report_error(HEXMOE_E_ARG, "hexmoe_ep_handle: null argument");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, ep->region);
+  if (e != cudaSuccess) return report_cuda_error(e, "hexmoe_ep_handle: cudaIpcGetMemHandle");
+  static_assert(sizeof(h) == HEXMOE_EP_HANDLE_BYTES, "IPC handle size");
+  std::memcpy(handle_out, &h, sizeof(h));
+  return HEXMOE_OK;
+}
+
+int hexmoe_ep_connect(hexmoe_ep* ep, const void* handles) {
+  if (!ep || (!handles && ep->world > 1)) return report_error(HEXMOE_E_ARG, "hexmoe_ep_connect: null argument");
+  if (ep->connected) return HEXMOE_OK;
+  const uint8_t* hb = static_cast<const uint8_t*>(handles);
+  for (int r = 0; r < ep->world; ++r) {
+    if (r == ep->rank) continue;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, hb + static_cast<size_t>(r) * HEXMOE_EP_HANDLE_BYTES, sizeof(h));
+    void* p = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return report_cuda_error(e, "hexmoe_ep_connect: cudaIpcOpenMemHandle");
+    ep->peer[r] = static_cast<uint8_t*>(p);
+    ep->opened[r] = true;
+  }
+  ep->connected = true;
+  return HEXMOE_OK;
+}
+
+size_t hexmoe_ep_workspace_bytes(const hexmoe_ep* ep, const hexmoe_layer* local, int32_t block_m) {
+  if (!ep || !local) return 0;
+  return slots_workspace_bytes(local, static_cast<int64_t>(ep->world) * ep->seg_len, block_m);
+}
+
+int hexmoe_ep_dispatch(hexmoe_ep* ep, const void* x, int32_t x_dtype, int64_t tokens, const float* topk_weights,
+                       const void* topk_ids, int32_t ids_dtype, void* stream) {
+  if (int rc = ep_check(ep, "hexmoe_ep_dispatch: null context")) return rc;
+  if (tokens < 0 || tokens > ep->cap)
+    return report_error(HEXMOE_E_ARG, "hexmoe_ep_dispatch: tokens outside 0..max_tokens of the context");
+  if (x_dtype != ep->row_dtype && !(x_dtype == HEXMOE_F32 && ep->row_dtype == HEXMOE_BF16))
+    return report_error(HEXMOE_E_DTYPE, "hexmoe_ep_dispatch: x dtype must be the row dtype (or F32 for BF16 rows)");
+  if (ids_dtype != HEXMOE_I32 && ids_dtype != HEXMOE_I64) return report_error(HEXMOE_E_DTYPE, "ids dtype");
+  if (tokens > 0 && (!x || !topk_weights || !topk_ids || reinterpret_cast<uintptr_t>(x) % 16))
+    return report_error(HEXMOE_E_ARG, "hexmoe_ep_dispatch: null or unaligned pointer");
+  int32_t* dev_err = device_error_word();
+  if (!dev_err) return report_error(HEXMOE_E_CUDA, "device error word unavailable");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const EpArgs a = ep_args(ep, dev_err);
+  const bool i64 = ids_dtype == HEXMOE_I64;
+  if (i64) ep_plan_kernel<true><<<1, kPlanThreads, 0, st>>>(a, topk_ids, tokens);
+  else ep_plan_kernel<false><<<1, kPlanThreads, 0, st>>>(a, topk_ids, tokens);
+  const int grid = grid_for(tokens, kSendThreads / 32);
+  if (x_dtype == HEXMOE_F32) {
+    if (i64) ep_send_kernel<float, true><<<grid, kSendThreads, 0, st>>>(a, static_cast<const float*>(x), topk_ids, topk_weights, tokens);
+    else ep_send_kernel<float, false><<<grid, kSendThreads, 0, st>>>(a, static_cast<const float*>(x), topk_ids, topk_weights, tokens);
+  } else {
+    if (i64) ep_send_kernel<uint16_t, true><<<grid, kSendThreads, 0, st>>>(a, static_cast<const uint16_t*>(x), topk_ids, topk_weights, tokens);
+    else ep_send_kernel<uint16_t, false><<<grid, kSendThreads, 0, st>>>(a, static_cast<const uint16_t*>(x), topk_ids, topk_weights, tokens);
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return report_cuda_error(e, "hexmoe_ep_dispatch launch");
+  ep->last_tokens = tokens;
+  return HEXMOE_OK;
+}
+
+int hexmoe_ep_experts(hexmoe_ep* ep, const hexmoe_layer* local, int32_t block_m, void* workspace,
+                      size_t workspace_bytes, void* stream) {
+  if (int rc = ep_check(ep, "hexmoe_ep_experts: null context")) return rc;
+  int32_t* dev_err = device_error_word();
+  if (!dev_err) return report_error(HEXMOE_E_CUDA, "device error word unavailable");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const EpArgs a = ep_args(ep, dev_err);
+  ep_wait_kernel<<<1, 32, 0, st>>>(a, ep->o_disp);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return report_cuda_error(e, "hexmoe_ep_experts: wait launch");
+  const int64_t S = static_cast<int64_t>(ep->world) * ep->seg_len;
+  void* y = nullptr;
+  if (local) {
+    const hexmoe_layer_desc* d = layer_desc(local);
+    if (d->hidden != ep->H || d->num_experts != ep->E)
+      return report_error(HEXMOE_E_ARG, "hexmoe_ep_experts: the local layer's hidden / num_experts differ from the context");
+    const size_t need = slots_workspace_bytes(local, S, block_m);
+    if (!workspace || workspace_bytes < need)
+      return report_error(HEXMOE_E_ARG, "hexmoe_ep_experts: workspace smaller than hexmoe_ep_workspace_bytes");
+    uint8_t* R = ep->region;
+    int rc = forward_slot_space(local, R + ep->o_x, ep->row_dtype, S, reinterpret_cast<const int32_t*>(R + ep->o_exp),
+                                reinterpret_cast<const float*>(R + ep->o_w), reinterpret_cast<const int32_t*>(R + ep->o_row),
+                                reinterpret_cast<const int32_t*>(R + ep->o_slots), ep->seg_len, nullptr, block_m,
+                                workspace, workspace_bytes, st, &y);
+    if (rc) return rc;
+  }
+  // without local experts nothing can have been routed here: rows = 0 from every source
+  const int64_t rows_max = static_cast<int64_t>(ep->world) * ep->cap;
+  const int grid = grid_for(local ? rows_max / 4 : 1, kSendThreads / 32);
+  if (ep->row_dtype == HEXMOE_BF16)
+    ep_return_kernel<__nv_bfloat16><<<grid, kSendThreads, 0, st>>>(a, static_cast<const __nv_bfloat16*>(y));
+  else
+    ep_return_kernel<__half><<<grid, kSendThreads, 0, st>>>(a, static_cast<const __half*>(y));
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return report_cuda_error(e, "hexmoe_ep_experts: return launch");
+  return HEXMOE_OK;
+}
+
+int hexmoe_ep_combine(hexmoe_ep* ep, int64_t tokens, void* out, int32_t out_dtype, void* stream) {
+  if (int rc = ep_check(ep, "hexmoe_ep_combine: null context")) return rc;
+  if (tokens != ep->last_tokens) return report_error(HEXMOE_E_ARG, "hexmoe_ep_combine: tokens differ from the dispatch");
+  if (out_dtype != HEXMOE_F32 && out_dtype != ep->row_dtype)
+    return report_error(HEXMOE_E_DTYPE, "hexmoe_ep_combine: out dtype must be the row dtype or F32");
+  if (tokens > 0 && (!out || reinterpret_cast<uintptr_t>(out) % 16))
+    return report_error(HEXMOE_E_ARG, "hexmoe_ep_combine: null or unaligned out");
+  int32_t* dev_err = device_error_word();
+  if (!dev_err) return report_error(HEXMOE_E_CUDA, "device error word unavailable");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const EpArgs a = ep_args(ep, dev_err);
+  ep_wait_kernel<<<1, 32, 0, st>>>(a, ep->o_ret_flag);
+  if (tokens > 0) {
+    const int64_t total = tokens * (ep->H / 8);
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, 148 * 8));
+    const bool bf = ep->row_dtype == HEXMOE_BF16;
+    if (out_dtype == HEXMOE_F32) {
+      if (bf) ep_combine_kernel<__nv_bfloat16, HEXMOE_F32><<<grid, 256, 0, st>>>(a, tokens, out);
+      else ep_combine_kernel<__half, HEXMOE_F32><<<grid, 256, 0, st>>>(a, tokens, out);
+    } else if (bf) {
+      ep_combine_kernel<__nv_bfloat16, HEXMOE_BF16><<<grid, 256, 0, st>>>(a, tokens, out);
+    } else {
+      ep_combine_kernel<__half, HEXMOE_F16><<<grid, 256, 0, st>>>(a, tokens, out);
+    }
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return report_cuda_error(e, "hexmoe_ep_combine launch");
+  return HEXMOE_OK;
+}
+
+int hexmoe_ep_forward(hexmoe_ep* ep, const hexmoe_layer* local, const void* x, int32_t x_dtype, int64_t tokens,
+                      const float* topk_weights, const void* topk_ids, int32_t ids_dtype, void* out, int32_t out_dtype,
+                      int32_t block_m, void* workspace, size_t workspace_bytes, void* stream) {
+  if (int rc = hexmoe_ep_dispatch(ep, x, x_dtype, tokens, topk_weights, topk_ids, ids_dtype, stream)) return rc;
+  if (int rc = hexmoe_ep_experts(ep, local, block_m, workspace, workspace_bytes, stream)) return rc;
+  return hexmoe_ep_combine(ep, tokens, out, out_dtype, stream);
+}
+
+int hexmoe_ep_destroy(hexmoe_ep* ep) {
+  if (!ep) return HEXMOE_OK;
+  int prev = -1;
+  cudaGetDevice(&prev);
+  if (prev != ep->device) cudaSetDevice(ep->device);
+  for (int r = 0; r < kEpMaxWorld; ++r)
+    if (ep->opened[r]) cudaIpcCloseMemHandle(ep->peer[r]);
+  cudaFree(ep->region);
+  cudaFree(ep->local);
+  if (prev >= 0 && prev != ep->device) cudaSetDevice(prev);
+  delete ep;
+  return HEXMOE_OK;
+}
+
+}  // extern "C"

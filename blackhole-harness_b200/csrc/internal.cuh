@@ -78,9 +78,11 @@ struct GemmParams {
 cudaError_t launch_gemm(const GemmParams& p, bool glu, bool bf16, int grid, cudaStream_t stream, bool pdl);
 
 // Small kernels (kernels.cu).
+// seg_counts (optional): the ragged slot space of the expert-parallel receive
+// side, segments of seg_len slots of which only the first seg_counts[g] exist.
 cudaError_t launch_align(const void* ids, bool ids64, int64_t S, int32_t E, int32_t bm, int32_t* sid, int32_t* eid,
                          int32_t* npp, int32_t* scratch, size_t scratch_bytes, int32_t* dev_err, cudaStream_t st,
-                         bool pdl);
+                         bool pdl, const int32_t* seg_counts = nullptr, int64_t seg_len = 0);
 size_t align_scratch_bytes(int64_t S, int32_t E);
 cudaError_t launch_dequant(const hexmoe_parts& parts, int bits, int block, int n, int rows, int cols, int rows_pad,
                            int cols_pad, const int32_t* experts, void* out, int out_dtype, int64_t stride_e,
@@ -92,13 +94,28 @@ cudaError_t launch_combine(const void* y, int y_dtype, int64_t T, int32_t topk, 
 cudaError_t launch_tile_index(const uint32_t* idx, int bits, int n, int rows_pad, int cols_pad, uint32_t* out,
                               cudaStream_t st);
 cudaError_t launch_cast_to16(const float* x, void* out, bool bf16, int64_t n, cudaStream_t st);
-// x_sorted[r] = x[sorted_ids[r] / topk] for every plan row r < npp holding a slot
-// (x in x_dtype, x_sorted 16-bit: bf16 for f32 input); padding rows untouched.
+// x_sorted[r] = x[row(sorted_ids[r])] for every plan row r < npp holding a slot,
+// row(s) = s / topk, or slot_row[s] when a map is given (x in x_dtype, x_sorted
+// 16-bit: bf16 for f32 input); padding rows untouched.
 cudaError_t launch_gather_rows(const void* x, int x_dtype, int64_t T, int32_t H, const int32_t* sid,
                                const int32_t* npp, int64_t max_rows, int32_t topk, int64_t S, void* xs,
-                               cudaStream_t st, bool pdl);
+                               cudaStream_t st, bool pdl, const int32_t* slot_row = nullptr);
 cudaError_t launch_route_topk(const void* logits, int dtype, int64_t T, int32_t E, int32_t k, int renorm, float* w,
                               int32_t* ids, cudaStream_t st);
+// The layer's description (api.cu).
+const hexmoe_layer_desc* layer_desc(const hexmoe_layer* layer);
+// The layer forward up to its per-slot rows y[num_slots, hidden] (16-bit) over
+// a general slot space: slot s has expert slot_expert[s], weight slot_weight[s]
+// and activation row x[slot_row[s]]; with seg_counts, only the first
+// seg_counts[g] slots of each seg_len-slot segment exist (the others are never
+// read or written).  Workspace: slots_workspace_bytes(layer, num_slots, block_m);
+// y == nullptr puts the rows into the workspace's own y region.  *y_used
+// (optional) receives where they went.
+int forward_slot_space(const hexmoe_layer* layer, const void* x, int32_t x_dtype, int64_t num_slots,
+                       const int32_t* slot_expert, const float* slot_weight, const int32_t* slot_row,
+                       const int32_t* seg_counts, int64_t seg_len, void* y, int32_t block_m, void* workspace,
+                       size_t workspace_bytes, cudaStream_t st, void** y_used = nullptr);
+size_t slots_workspace_bytes(const hexmoe_layer* layer, int64_t num_slots, int32_t block_m);
 int32_t* device_error_word();  // address of this device's error word (nullptr on failure)
 cudaError_t read_device_error(int32_t* value, bool clear);   // synchronous, current device
 cudaError_t launch_build_expert_map(const hexmoe_layer_desc& d, int32_t* map, cudaStream_t st);

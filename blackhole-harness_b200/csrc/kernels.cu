@@ -99,23 +99,45 @@ __device__ __forceinline__ unsigned equal_lanes(uint32_t v, int nbits) {
   return m;
 }
 
+// Ragged slot space (the expert-parallel receive side): slots form segments of
+// seg_len, of which only the first counts[seg] are present; the rest are not
+// slots at all (skipped, not errors).  counts == nullptr: every slot present.
+struct AlignRagged {
+  const int32_t* counts;
+  int64_t seg_len;
+  __device__ __forceinline__ bool present(int64_t s) const {
+    return !counts || (s % seg_len) < __ldg(counts + s / seg_len);
+  }
+  // [s_begin, s_end) clipped to the present prefix of its segment when it lies
+  // in one segment (the several-CTA align's warp ranges always do)
+  __device__ __forceinline__ int64_t clip_end(int64_t s_begin, int64_t s_end) const {
+    if (!counts || s_begin >= s_end) return s_end;
+    const int64_t seg = s_begin / seg_len;
+    if ((s_end - 1) / seg_len != seg) return s_end;
+    const int64_t e = seg * seg_len + __ldg(counts + seg);
+    return e < s_end ? e : s_end;
+  }
+};
+
 // Expert ids of chunks c0, c0 + 32, ... (kAlignBatch of them) for this lane,
 // every load issued before the first is used; -1 past s_end or for an id
 // outside 0..E-1 (which also sets the error word).
 template <bool I64>
 __device__ __forceinline__ void load_ids(const void* ids, int64_t c0, int64_t s_end, int lane, int32_t E,
-                                         int32_t* dev_err, int32_t (&ev)[kAlignBatch]) {
+                                         const AlignRagged& rg, int32_t* dev_err, int32_t (&ev)[kAlignBatch]) {
   int64_t raw[kAlignBatch];
+  bool live[kAlignBatch];
 #pragma unroll
   for (int u = 0; u < kAlignBatch; ++u) {
     const int64_t s = c0 + u * 32 + lane;
-    raw[u] = s < s_end ? (I64 ? __ldg(static_cast<const int64_t*>(ids) + s)
-                              : static_cast<int64_t>(__ldg(static_cast<const int32_t*>(ids) + s)))
-                       : -1;
+    live[u] = s < s_end && rg.present(s);
+    raw[u] = live[u] ? (I64 ? __ldg(static_cast<const int64_t*>(ids) + s)
+                            : static_cast<int64_t>(__ldg(static_cast<const int32_t*>(ids) + s)))
+                     : -1;
   }
 #pragma unroll
   for (int u = 0; u < kAlignBatch; ++u) {
-    const bool in_seg = c0 + u * 32 + lane < s_end;
+    const bool in_seg = live[u];
     const bool bad = in_seg && (raw[u] < 0 || raw[u] >= E);
     if (bad) atomicOr(dev_err, kDevErrExpertId);
     ev[u] = (in_seg && !bad) ? static_cast<int32_t>(raw[u]) : -1;
@@ -125,10 +147,11 @@ __device__ __forceinline__ void load_ids(const void* ids, int64_t c0, int64_t s_
 // Count: my_hist[e] += slots of expert e in [s_begin, s_end).
 template <bool I64>
 __device__ void warp_count(const void* ids, int64_t s_begin, int64_t s_end, int lane, int32_t E, int id_bits,
-                           int32_t* my_hist, int32_t* dev_err) {
+                           const AlignRagged& rg, int32_t* my_hist, int32_t* dev_err) {
+  s_end = rg.clip_end(s_begin, s_end);
   for (int64_t c0 = s_begin; c0 < s_end; c0 += 32 * kAlignBatch) {
     int32_t ev[kAlignBatch];
-    load_ids<I64>(ids, c0, s_end, lane, E, dev_err, ev);
+    load_ids<I64>(ids, c0, s_end, lane, E, rg, dev_err, ev);
 #pragma unroll
     for (int u = 0; u < kAlignBatch; ++u) {
       const int32_t e = ev[u];
@@ -143,10 +166,11 @@ __device__ void warp_count(const void* ids, int64_t s_begin, int64_t s_end, int 
 // my_pos[e] advances past the chunk's slots of e.
 template <bool I64>
 __device__ void warp_scatter(const void* ids, int64_t s_begin, int64_t s_end, int lane, int32_t E, int id_bits,
-                             int32_t* my_pos, int32_t* sid, int32_t* dev_err) {
+                             const AlignRagged& rg, int32_t* my_pos, int32_t* sid, int32_t* dev_err) {
+  s_end = rg.clip_end(s_begin, s_end);
   for (int64_t c0 = s_begin; c0 < s_end; c0 += 32 * kAlignBatch) {
     int32_t ev[kAlignBatch];
-    load_ids<I64>(ids, c0, s_end, lane, E, dev_err, ev);
+    load_ids<I64>(ids, c0, s_end, lane, E, rg, dev_err, ev);
 #pragma unroll
     for (int u = 0; u < kAlignBatch; ++u) {
       const int32_t e = ev[u];
@@ -215,7 +239,7 @@ __device__ void plan_runs(const int32_t* counts, int32_t* blk_start, int64_t S, 
 template <bool I64>
 __global__ void __launch_bounds__(kAlignThreads, 1)
     align_kernel(const void* __restrict__ ids, int64_t S, int32_t E, int32_t bm, int32_t* __restrict__ sid,
-                 int32_t* __restrict__ eid, int32_t* __restrict__ npp, int32_t* dev_err) {
+                 int32_t* __restrict__ eid, int32_t* __restrict__ npp, AlignRagged rg, int32_t* dev_err) {
   extern __shared__ int32_t sh[];
   int32_t* hist = sh;                                  // [kAlignWarps][E]
   int32_t* blk_start = sh + kAlignWarps * E;           // [E]
@@ -230,7 +254,7 @@ __global__ void __launch_bounds__(kAlignThreads, 1)
   const int64_t seg = (S + kAlignWarps - 1) / kAlignWarps;
   const int64_t s_begin = warp * seg;
   const int64_t s_end = s_begin + seg < S ? s_begin + seg : S;
-  warp_count<I64>(ids, s_begin, s_end, lane, E, id_bits, hist + warp * E, dev_err);
+  warp_count<I64>(ids, s_begin, s_end, lane, E, id_bits, rg, hist + warp * E, dev_err);
   __syncthreads();
   // per expert: exclusive prefix of the warps' counts, and the total
   constexpr int kPer = kAlignMaxExperts / kAlignThreads;
@@ -250,7 +274,7 @@ __global__ void __launch_bounds__(kAlignThreads, 1)
   plan_runs(counts, blk_start, S, E, bm, sid, eid, npp, scan_tmp, total_blocks);
   for (int i = threadIdx.x; i < kAlignWarps * E; i += kAlignThreads) hist[i] += blk_start[i % E] * bm;
   __syncthreads();
-  warp_scatter<I64>(ids, s_begin, s_end, lane, E, id_bits, hist + warp * E, sid, dev_err);
+  warp_scatter<I64>(ids, s_begin, s_end, lane, E, id_bits, rg, hist + warp * E, sid, dev_err);
   pdl_launch_dependents();
 }
 
@@ -258,7 +282,7 @@ __global__ void __launch_bounds__(kAlignThreads, 1)
 template <bool I64>
 __global__ void __launch_bounds__(kAlignThreads, 1)
     align_count_kernel(const void* __restrict__ ids, int64_t S, int32_t E, int32_t* __restrict__ cnt,
-                       int32_t* dev_err) {
+                       AlignRagged rg, int32_t* dev_err) {
   extern __shared__ int32_t hist[];                    // [kAlignWarps][E]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int id_bits = 32 - __clz(E);
@@ -268,7 +292,7 @@ __global__ void __launch_bounds__(kAlignThreads, 1)
   const int64_t r0 = static_cast<int64_t>(blockIdx.x) * kAlignSeg, r1 = r0 + kAlignSeg < S ? r0 + kAlignSeg : S;
   const int64_t s_begin = r0 + warp * (kAlignSeg / kAlignWarps);
   const int64_t s_end = s_begin + kAlignSeg / kAlignWarps < r1 ? s_begin + kAlignSeg / kAlignWarps : r1;
-  warp_count<I64>(ids, s_begin, s_end, lane, E, id_bits, hist + warp * E, dev_err);
+  warp_count<I64>(ids, s_begin, s_end, lane, E, id_bits, rg, hist + warp * E, dev_err);
   __syncthreads();
   for (int e = threadIdx.x; e < E; e += kAlignThreads) {
     int32_t acc = 0;
@@ -319,7 +343,7 @@ __global__ void __launch_bounds__(kAlignThreads, 1)
 template <bool I64>
 __global__ void __launch_bounds__(kAlignThreads, 1)
     align_scatter_kernel(const void* __restrict__ ids, int64_t S, int32_t E, const int32_t* __restrict__ off,
-                         int32_t* __restrict__ sid, int32_t* dev_err) {
+                         int32_t* __restrict__ sid, AlignRagged rg, int32_t* dev_err) {
   extern __shared__ int32_t hist[];                    // [kAlignWarps][E]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int id_bits = 32 - __clz(E);
@@ -329,7 +353,7 @@ __global__ void __launch_bounds__(kAlignThreads, 1)
   const int64_t r0 = static_cast<int64_t>(blockIdx.x) * kAlignSeg, r1 = r0 + kAlignSeg < S ? r0 + kAlignSeg : S;
   const int64_t s_begin = r0 + warp * (kAlignSeg / kAlignWarps);
   const int64_t s_end = s_begin + kAlignSeg / kAlignWarps < r1 ? s_begin + kAlignSeg / kAlignWarps : r1;
-  warp_count<I64>(ids, s_begin, s_end, lane, E, id_bits, hist + warp * E, dev_err);
+  warp_count<I64>(ids, s_begin, s_end, lane, E, id_bits, rg, hist + warp * E, dev_err);
   __syncthreads();
   for (int e = threadIdx.x; e < E; e += kAlignThreads) {
     int32_t pos = off[static_cast<int64_t>(blockIdx.x) * E + e];
@@ -340,7 +364,7 @@ __global__ void __launch_bounds__(kAlignThreads, 1)
     }
   }
   __syncthreads();
-  warp_scatter<I64>(ids, s_begin, s_end, lane, E, id_bits, hist + warp * E, sid, dev_err);
+  warp_scatter<I64>(ids, s_begin, s_end, lane, E, id_bits, rg, hist + warp * E, sid, dev_err);
   pdl_launch_dependents();
 }
 
@@ -352,7 +376,8 @@ size_t align_scratch_bytes(int64_t S, int32_t E) {
 
 cudaError_t launch_align(const void* ids, bool ids64, int64_t S, int32_t E, int32_t bm, int32_t* sid, int32_t* eid,
                          int32_t* npp, int32_t* scratch, size_t scratch_bytes, int32_t* dev_err, cudaStream_t st,
-                         bool pdl) {
+                         bool pdl, const int32_t* seg_counts, int64_t seg_len) {
+  const AlignRagged rg{seg_counts, seg_counts ? seg_len : 1};
   if (E > kAlignMaxExperts) return cudaErrorInvalidValue;
   static std::atomic<bool> configured[64] = {};   // per device
   static std::mutex mu;
@@ -389,14 +414,14 @@ cudaError_t launch_align(const void* ids, bool ids64, int64_t S, int32_t E, int3
   if (need == 0 || !scratch || scratch_bytes < need) {
     cfg.gridDim = dim3(1);
     cfg.dynamicSmemBytes = hist_bytes + 2 * E * sizeof(int32_t);
-    return ids64 ? cudaLaunchKernelEx(&cfg, align_kernel<true>, ids, S, E, bm, sid, eid, npp, dev_err)
-                 : cudaLaunchKernelEx(&cfg, align_kernel<false>, ids, S, E, bm, sid, eid, npp, dev_err);
+    return ids64 ? cudaLaunchKernelEx(&cfg, align_kernel<true>, ids, S, E, bm, sid, eid, npp, rg, dev_err)
+                 : cudaLaunchKernelEx(&cfg, align_kernel<false>, ids, S, E, bm, sid, eid, npp, rg, dev_err);
   }
   const int32_t G = static_cast<int32_t>((S + kAlignSeg - 1) / kAlignSeg);
   cfg.gridDim = dim3(G);
   cfg.dynamicSmemBytes = hist_bytes;
-  e = ids64 ? cudaLaunchKernelEx(&cfg, align_count_kernel<true>, ids, S, E, scratch, dev_err)
-            : cudaLaunchKernelEx(&cfg, align_count_kernel<false>, ids, S, E, scratch, dev_err);
+  e = ids64 ? cudaLaunchKernelEx(&cfg, align_count_kernel<true>, ids, S, E, scratch, rg, dev_err)
+            : cudaLaunchKernelEx(&cfg, align_count_kernel<false>, ids, S, E, scratch, rg, dev_err);
   if (e != cudaSuccess) return e;
   cfg.numAttrs = 1;   // the next two follow kernels of this library
   cfg.gridDim = dim3(1);
@@ -406,9 +431,9 @@ cudaError_t launch_align(const void* ids, bool ids64, int64_t S, int32_t E, int3
   cfg.gridDim = dim3(G);
   cfg.dynamicSmemBytes = hist_bytes;
   return ids64 ? cudaLaunchKernelEx(&cfg, align_scatter_kernel<true>, ids, S, E, static_cast<const int32_t*>(scratch),
-                                    sid, dev_err)
+                                    sid, rg, dev_err)
                : cudaLaunchKernelEx(&cfg, align_scatter_kernel<false>, ids, S, E,
-                                    static_cast<const int32_t*>(scratch), sid, dev_err);
+                                    static_cast<const int32_t*>(scratch), sid, rg, dev_err);
 }
 
 // ---------------------------------------------------------------------------
@@ -607,7 +632,7 @@ cudaError_t launch_combine(const void* y, int y_dtype, int64_t T, int32_t topk, 
 template <typename XT>
 __global__ void gather_rows_kernel(const XT* __restrict__ x, int32_t H, const int32_t* __restrict__ sid,
                                    const int32_t* __restrict__ npp, int64_t max_rows, int32_t topk, int64_t S,
-                                   uint16_t* __restrict__ xs) {
+                                   const int32_t* __restrict__ slot_row, uint16_t* __restrict__ xs) {
   pdl_wait();
   const int64_t rows = min(static_cast<int64_t>(__ldg(npp)), max_rows);
   const int lane = threadIdx.x & 31;
@@ -615,7 +640,8 @@ __global__ void gather_rows_kernel(const XT* __restrict__ x, int32_t H, const in
   for (int64_t r = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5; r < rows; r += nwarps) {
     const int s = __ldg(sid + r);
     if (s >= S) continue;
-    const XT* src = x + static_cast<int64_t>(s / topk) * H;
+    const int64_t xr = slot_row ? static_cast<int64_t>(__ldg(slot_row + s)) : static_cast<int64_t>(s / topk);
+    const XT* src = x + xr * H;
     uint4* dst = reinterpret_cast<uint4*>(xs + r * H);
     for (int c = lane; c < H / 8; c += 32) {
       if constexpr (sizeof(XT) == 2) {
@@ -633,7 +659,7 @@ __global__ void gather_rows_kernel(const XT* __restrict__ x, int32_t H, const in
 
 cudaError_t launch_gather_rows(const void* x, int x_dtype, int64_t T, int32_t H, const int32_t* sid,
                                const int32_t* npp, int64_t max_rows, int32_t topk, int64_t S, void* xs,
-                               cudaStream_t st, bool pdl) {
+                               cudaStream_t st, bool pdl, const int32_t* slot_row) {
   (void)T;
   if (max_rows == 0) return cudaSuccess;
   const int threads = 256;
@@ -650,9 +676,9 @@ cudaError_t launch_gather_rows(const void* x, int x_dtype, int64_t T, int32_t H,
   uint16_t* out = static_cast<uint16_t*>(xs);
   if (x_dtype == HEXMOE_F32)
     return cudaLaunchKernelEx(&cfg, gather_rows_kernel<float>, static_cast<const float*>(x), H, sid, npp, max_rows,
-                              topk, S, out);
+                              topk, S, slot_row, out);
   return cudaLaunchKernelEx(&cfg, gather_rows_kernel<uint16_t>, static_cast<const uint16_t*>(x), H, sid, npp,
-                            max_rows, topk, S, out);
+                            max_rows, topk, S, slot_row, out);
 }
 
 // ---------------------------------------------------------------------------

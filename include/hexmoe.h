@@ -244,6 +244,73 @@ HEXMOE_API int hexmoe_dequant(const hexmoe_parts* parts, int32_t bits, int32_t b
                    const int32_t* experts, void* out, int32_t out_dtype, int64_t stride_e,
                    int64_t stride_row, int64_t row_off, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Expert parallelism over NVLink peer memory.  No counterpart in the reference,
+ * which runs each MoE layer on one GPU and refuses expert parallelism
+ * (vllm_hex.py:101-102); these replace, for a multi-GPU node, what hex_moe
+ * (hex_moe.py:374-382) does on one GPU.
+ *
+ * Experts are sharded contiguously: rank r of `world` owns global experts
+ * [r*P, (r+1)*P), P = ceil(num_experts / world), and runs them as a
+ * hexmoe_layer built from its own tiers only (global expert ids kept).  Each
+ * rank's context owns one device region that every other rank maps through
+ * CUDA IPC; kernels store token rows, slot records and partial sums straight
+ * into the owning rank's region with plain stores, and signal with epoch flags
+ * (release / acquire at system scope).  Nothing synchronises with the host, so
+ * a forward can be captured in a CUDA graph.
+ *
+ * Per forward: every token row crosses once per rank that owns one of its
+ * experts (not once per slot); the owner runs its experts on the received
+ * slots and returns, per row, the fp32 sum of that row's weighted slot
+ * outputs in top-k order rounded once to the row dtype; the home rank adds the
+ * returned partials in rank order in fp32 and rounds once.  (One GPU sums the
+ * k slot outputs of a token in top-k order instead, so the two differ in the
+ * rounding of the partial sums, within the layer tolerance.)
+ *
+ * Protocol rules: every rank calls init, exchanges handles (hexmoe_ep_handle,
+ * gathered in rank order by the caller), connects, and then runs the same
+ * sequence of forwards (dispatch -> experts -> combine) on one stream; a rank
+ * with no tokens still takes part.  Destroy only after every rank has finished
+ * its last forward (a host barrier).  A peer that stops taking part makes the
+ * others' bounded waits (2 s) run out: they set the timeout bit of the device
+ * error word and return instead of hanging.  Expert ids outside 0..E-1 are
+ * dropped and set the expert-id bit. */
+#define HEXMOE_EP_MAX_WORLD 8
+#define HEXMOE_EP_HANDLE_BYTES 64
+typedef struct hexmoe_ep hexmoe_ep;
+
+/* Context of rank `rank` of `world` on the current device, for up to
+ * max_tokens tokens per rank per forward, top-`topk` over num_experts global
+ * experts of width `hidden`; rows travel as row_dtype (BF16 or F16).  Allocates
+ * the shared region (2 x world x max_tokens x hidden x 2 bytes of rows plus
+ * ~12 x world x max_tokens x topk bytes of slot records) and its private state;
+ * synchronises the device. */
+HEXMOE_API int hexmoe_ep_init(int32_t rank, int32_t world, int32_t num_experts, int32_t hidden, int32_t topk,
+                              int64_t max_tokens, int32_t row_dtype, hexmoe_ep** out);
+/* The CUDA IPC handle (HEXMOE_EP_HANDLE_BYTES) of this rank's region. */
+HEXMOE_API int hexmoe_ep_handle(const hexmoe_ep* ep, void* handle_out);
+/* Maps every other rank's region from the gathered handles [world][64] (rank order). */
+HEXMOE_API int hexmoe_ep_connect(hexmoe_ep* ep, const void* handles);
+/* Scratch bytes hexmoe_ep_experts / hexmoe_ep_forward need with this rank's layer. */
+HEXMOE_API size_t hexmoe_ep_workspace_bytes(const hexmoe_ep* ep, const hexmoe_layer* local, int32_t block_m);
+/* Phase 1: route this rank's tokens to the owners of their experts (x [T,
+ * hidden] in row_dtype, or F32 with BF16 rows; weights f32 [T, topk]; ids
+ * [T, topk] global). */
+HEXMOE_API int hexmoe_ep_dispatch(hexmoe_ep* ep, const void* x, int32_t x_dtype, int64_t tokens,
+                                  const float* topk_weights, const void* topk_ids, int32_t ids_dtype, void* stream);
+/* Phase 2: wait for every rank's dispatch, run `local` (NULL on a rank that owns
+ * no experts) on the received slots, return the partial sums to their ranks. */
+HEXMOE_API int hexmoe_ep_experts(hexmoe_ep* ep, const hexmoe_layer* local, int32_t block_m, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+/* Phase 3: wait for every rank's return; out [T, hidden] (row_dtype or F32). */
+HEXMOE_API int hexmoe_ep_combine(hexmoe_ep* ep, int64_t tokens, void* out, int32_t out_dtype, void* stream);
+/* The three phases in one call. */
+HEXMOE_API int hexmoe_ep_forward(hexmoe_ep* ep, const hexmoe_layer* local, const void* x, int32_t x_dtype,
+                                 int64_t tokens, const float* topk_weights, const void* topk_ids, int32_t ids_dtype,
+                                 void* out, int32_t out_dtype, int32_t block_m, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+HEXMOE_API int hexmoe_ep_destroy(hexmoe_ep* ep);
+
 /* Router: probabilities = softmax(logits[t, :E]) in fp32, the topk largest
  * (ties: lower expert id first), renormalised to sum 1 when renormalize != 0
  * (Qwen3 norm_topk_prob).  logits f32/bf16/f16 [T, E] row stride E.  The

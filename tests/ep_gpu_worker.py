@@ -1,7 +1,10 @@
 """One rank of the multi-GPU expert-parallel check (launched by test_ep_gpu.py with
-torchrun, one process per GPU, NCCL): the EP layer on this rank's tokens must equal
-the single-GPU layer on the same tokens bit for bit.  Prints "EP-OK <rank> ..." on
-success."""
+torchrun, one process per GPU).  The hexmoe_ep_* path (peer-memory dispatch,
+local experts, pre-summed return, rank-ordered combine) on this rank's tokens
+must equal, bit for bit, the single-GPU layer's per-slot rows of the same
+tokens put through the same combine (ep.reference_combine); with one rank it
+must equal the plain single-GPU layer.  A CUDA-graph replay of the EP forward
+must give the eager result.  Prints "EP-OK <rank> of <world>" on success."""
 
 from __future__ import annotations
 
@@ -23,38 +26,74 @@ def main() -> int:
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     dist.init_process_group("nccl", timeout=timedelta(seconds=60), device_id=dev)
+    ep = None
     try:
         from blackhole_b200 import hex_data as hd
-        from blackhole_b200.ep import EPMoE, ExpertShard, shard_tiers
-        from blackhole_b200.hex_moe import HexTier, hex_moe
+        from blackhole_b200.ep import EPMoE, ExpertShard, reference_combine, shard_tiers
+        from blackhole_b200.hex_moe import HexTier, device_status, layer_for
 
-        E, H, I, K = 16, 512, 256, 4
+        device_status(local, clear=True)
+        E, H, I, K, BM = 16, 512, 256, 4, 16
         L = hd.synth_layer(E, H, I, "mixed", 128, seed=5, device=dev)
         mk = lambda ts: [HexTier(t["bits"], t["experts"], t["gate_proj"], t["up_proj"], t["down_proj"]).prepare(E)  # noqa: E731
                          for t in ts]
-        full = mk(L.tiers)
+        full = layer_for(mk(L.tiers))
         shard = ExpertShard(E, rank, world)
-        ep = EPMoE(shard, mk(shard_tiers(L.tiers, shard)), block_m=16)
-        for T, zipf in ((48 + 16 * rank, None), (96, 1.2), (0 if rank == world - 1 else 8, None)):
-            w, ids = hd.synth_routing(T, E, K, seed=11 + rank, zipf=zipf, device=dev)
-            x = hd.synth_x(T, H, seed=21 + rank, device=dev)
+        ep = EPMoE(shard, mk(shard_tiers(L.tiers, shard)), block_m=BM, max_tokens=128, topk=K, hidden=H)
+        cases = ((48 + 16 * rank, None), (96, 1.2), (0 if rank == world - 1 else 8, None), (128, None))
+        for T, zipf in cases:
+            w, ids = hd.synth_routing(T, E, K, seed=11 + rank + T, zipf=zipf, device=dev)
+            x = hd.synth_x(T, H, seed=21 + rank + T, device=dev)
             got = ep(x, w, ids)
-            # the single-GPU layer, one slot per row (the EP path's arithmetic), then the same combine
-            want_slots = hex_moe(x.repeat_interleave(K, 0), w.reshape(-1, 1), ids.reshape(-1, 1), full,
-                                 {"BLOCK_M": 16})
-            want = ep.combine_fn(want_slots, T, K) if T else want_slots
             torch.cuda.synchronize()
+            if T == 0:
+                if got.shape != (0, H):
+                    print(f"EP-SHAPE rank {rank}", flush=True)
+                    return 1
+                continue
+            y = full.forward_slots(x, w, ids, BM)
+            want = reference_combine(y, ids, shard, x.dtype)
             if not torch.equal(got, want):
                 print(f"EP-MISMATCH rank {rank} T={T} max diff {(got.float() - want.float()).abs().max().item()}",
                       flush=True)
                 return 1
-            ref = hex_moe(x, w, ids, full)          # the plain single-GPU layer: same up to combine order
-            if T and not torch.allclose(got.float(), ref.float(), rtol=2e-2, atol=1e-2):
+            ref = full.forward(x, w, ids, BM)       # the plain single-GPU layer
+            if world == 1 and not torch.equal(got, ref):
+                print(f"EP-ONE-RANK rank {rank} T={T}", flush=True)
+                return 1
+            if not torch.allclose(got.float(), ref.float(), rtol=2e-2, atol=1e-2):
                 print(f"EP-TOL rank {rank} T={T}", flush=True)
                 return 1
+        # the EP forward captured in a CUDA graph (no host synchronisation inside)
+        T = 64
+        w, ids = hd.synth_routing(T, E, K, seed=77 + rank, device=dev)
+        x = hd.synth_x(T, H, seed=78 + rank, device=dev)
+        eager = ep(x, w, ids)
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            ep(x, w, ids)
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            out = ep(x, w, ids)
+        for _ in range(2):
+            g.replay()
+            torch.cuda.synchronize()
+            if not torch.equal(out, eager):
+                print(f"EP-GRAPH rank {rank}", flush=True)
+                return 1
+        del g
+        err = device_status(local, clear=True)
+        if err:
+            print(f"EP-DEVERR rank {rank} word {err}", flush=True)
+            return 1
         print(f"EP-OK {rank} of {world}", flush=True)
         return 0
     finally:
+        if ep is not None:
+            ep.close()
         dist.destroy_process_group()
 
 

@@ -1,11 +1,14 @@
-"""Expert parallelism (blackhole_b200.ep) on CPU ranks over gloo, world size 2 and 3,
-with the C oracle standing in for each rank's local experts.
+"""Expert parallelism (blackhole_b200.ep) on CPU ranks over gloo, world sizes 2, 3,
+5 and 8, with the C oracle standing in for each rank's local experts.
 
 The reference has no multi-GPU path (its plugin refuses expert parallelism), so
-the bar is the single-process layer: every slot is computed by its owner rank at
-top-1, rounded to the activation dtype and summed in fp32 at its source rank,
-which must reproduce the single-process per-slot computation bit for bit, and
-the oracle's moe_reference within the layer tolerance.
+the bar is the single-process computation: every slot computed alone at top-1
+and rounded to the activation dtype (as the single-GPU layer's per-slot rows),
+then per owner rank the fp32 sum of the token's slots in top-k order rounded
+once, then those partials summed in rank order (ep.reference_combine).  EP must
+reproduce that bit for bit, and the oracle's moe_reference within the layer
+tolerance.  The same host protocol (one row per token and destination rank,
+pre-summed returns) is what the hexmoe_ep_* kernels run on GPUs.
 """
 
 from __future__ import annotations
@@ -41,19 +44,15 @@ def _tokens(rank: int, T: int, zipf=None):
     return x, w, ids
 
 
-def _per_slot_reference(x, w, ids, tiers_np):
-    """Every slot alone at top-1 (weighted, rounded to bf16), then fp32 sum: the
-    arithmetic the EP path performs, in one process."""
+def _per_slot_rows(x, w, ids, tiers_np) -> torch.Tensor:
+    """Every slot alone at top-1 (weighted, rounded to bf16): the single-GPU
+    layer's per-slot rows [T * k, H], in one process."""
     import hexoracle
     T, k = ids.shape
     layer = hexoracle.Layer(tiers_np, E, H, I, BLOCK)
     xs = np.repeat(x.float().numpy(), k, axis=0)
     y = layer.forward(xs, w.reshape(-1, 1).numpy(), ids.reshape(-1, 1).numpy())
-    y = hexoracle.round_bf16(y).reshape(T, k, H)
-    acc = y[:, 0].copy()
-    for j in range(1, k):           # slots added in order, as the layer's combine does
-        acc += y[:, j]
-    return acc
+    return torch.from_numpy(hexoracle.round_bf16(y)).to(torch.bfloat16)
 
 
 def _worker(rank: int, world: int, port: int, T_of, zipf, out_q):
@@ -119,15 +118,12 @@ def test_ep_matches_single_process(oracle, world, T_of, zipf):
         assert got.shape == (T_of[r], H)
         if T_of[r] == 0:
             continue
-        per_slot = hexoracle_round(_per_slot_reference(x, w, ids, full_np))
+        from blackhole_b200.ep import ExpertShard, reference_combine
+        per_slot = reference_combine(_per_slot_rows(x, w, ids, full_np), ids, ExpertShard(E, r, world),
+                                     torch.bfloat16).float().numpy()
         assert np.array_equal(got, per_slot), rel_err(got, per_slot)
         want = oracle.moe_reference(x.float().numpy(), w.numpy(), ids.numpy(), full_np, E, BLOCK)
         assert within(got, want), rel_err(got, want)
-
-
-def hexoracle_round(a):
-    import hexoracle
-    return hexoracle.round_bf16(a)
 
 
 def _bad_id_worker(rank: int, world: int, port: int, out_q):
@@ -150,8 +146,10 @@ def _bad_id_worker(rank: int, world: int, port: int, out_q):
 
 
 def test_out_of_range_id_raises_on_every_rank():
-    """A bad expert id on one rank ends the call with ValueError on every rank,
-    before any token row moves (the flag rides on the count exchange)."""
+    """On CPU ranks a bad expert id on one rank ends the call with ValueError on
+    every rank, before any token row moves (the flag rides on the count
+    exchange).  The GPU path has no host exchange: it drops the slot and sets
+    the device error word."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
@@ -192,3 +190,28 @@ def test_expert_shard_ownership():
     assert sh.owner(torch.tensor([0, 11, 12, 95])).tolist() == [0, 0, 1, 7]
     sh = ExpertShard(10, 3, 4)                 # uneven: 3, 3, 3, 1
     assert sh.local_range == (9, 10)
+
+
+def test_plan_dispatch_rows_and_slots():
+    """One row per (token, owner rank) in token order; slots in (token, j) order."""
+    from blackhole_b200.ep import ExpertShard, plan_dispatch
+    ids = torch.tensor([[0, 5, 1], [7, 6, 2], [3, 4, 5]])        # E=8 over 4 ranks: 2 experts each
+    p = plan_dispatch(ids, ExpertShard(8, 0, 4))
+    assert [r.tolist() for r in p.rows] == [[0], [1, 2], [0, 2], [1]]
+    assert p.pos.tolist() == [[0, -1, 0, -1], [-1, 0, -1, 0], [-1, 1, 1, -1]]
+    assert [list(zip(t.tolist(), j.tolist())) for t, j in p.slots] == [
+        [(0, 0), (0, 2)], [(1, 2), (2, 0)], [(0, 1), (2, 1), (2, 2)], [(1, 0), (1, 1)]]
+
+
+def test_reference_combine_single_rank_is_the_layer_combine():
+    """With one rank the EP combine is the single-GPU combine (slots in order, fp32, once rounded)."""
+    from blackhole_b200.ep import ExpertShard, reference_combine
+    g = torch.Generator().manual_seed(3)
+    T, k = 9, 4
+    y = torch.randn(T * k, 16, generator=g).to(torch.bfloat16)
+    ids = torch.randint(0, 12, (T, k), generator=g)
+    want = y.view(T, k, 16).float()
+    acc = want[:, 0]
+    for j in range(1, k):
+        acc = acc + want[:, j]
+    assert torch.equal(reference_combine(y, ids, ExpertShard(12, 0, 1), torch.bfloat16), acc.to(torch.bfloat16))

@@ -1,6 +1,8 @@
-"""Expert parallelism over NCCL: the EP layer equals the single-GPU layer bit for
-bit on every rank (tests/ep_gpu_worker.py, one process per GPU), on two GPUs and,
-so that a one-GPU run covers the same code, as a single rank."""
+"""Expert parallelism over NVLink peer memory (hexmoe_ep_*): on every rank the EP
+layer equals the single-GPU layer's per-slot rows put through the EP combine, bit
+for bit (tests/ep_gpu_worker.py, one process per GPU), on two GPUs and, so that a
+one-GPU run covers the same kernels, as a single rank (which must equal the plain
+layer bit for bit).  NCCL only carries the one-time IPC handle exchange."""
 
 from __future__ import annotations
 
@@ -36,7 +38,7 @@ def test_ep_two_gpus_matches_single_gpu():
 
 @pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU")
 def test_ep_one_rank_matches_single_gpu():
-    """The CUDA expert-parallel path (owner grouping by the align kernel, the
-    per-slot forward, the row-mapped combine) in a one-rank NCCL group: every
-    all-to-all is a copy to itself, and the result equals the layer bit for bit."""
+    """The expert-parallel kernels (plan, dispatch to itself, ragged align and
+    mapped gather, pre-summed return, combine) as a single rank: the result
+    equals the single-GPU layer bit for bit."""
     _run_workers(1, 29562)
