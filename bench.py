@@ -1,33 +1,39 @@
 """Benchmark of the HEX fused-MoE layer on B200 (one JSON line on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--tokens T] [--impl b200|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--no-extras]
 
-Workload (the metric's decode config, on one GPU): a Qwen3-30B-A3B REAP-25% MoE
-layer, 96 experts, hidden 2048, moe_intermediate 768, top-8, SwiGLU, every
-expert 3-bit / 8-level HEX with fp8 e4m3 scales per 128 inputs, T = 64 tokens
-(the largest point of the 1/8/32/64 decode sweep; the other points are
-reported under "sweep").  Synthetic seeded data (blackhole_b200.hex_data): no
-dataset exists on this path.
-
-One step = one layer forward (align plan, gate/up GEMM with SwiGLU, down GEMM
-with the top-k weight, combine) over one batch already in HBM, timed with CUDA
+Headline workload: the prefill config that runs on 1, 2, 4 and 8 GPUs (cfg3): a
+Qwen3-30B-A3B REAP-25% MoE layer, 96 experts, hidden 2048, moe_intermediate 768,
+top-8, SwiGLU, half the experts (seeded) 4-bit / 16-level and half 3-bit /
+8-level HEX with fp8 e4m3 scales per 128 inputs, 4096 tokens per GPU.  At N=1
+one step is the single-GPU layer (hexmoe_forward: align plan, gather, gate/up
+GEMM with SwiGLU, down GEMM with the top-k weight, combine); at N>1 it is the
+expert-parallel layer (hexmoe_ep_forward: experts sharded 96/N per GPU, token
+rows dispatched to their experts' GPUs over NVLink peer memory, pre-summed
+partials returned), value = all ranks' tokens over the slowest rank's time.
+Synthetic seeded data (blackhole_b200.hex_data): no dataset exists on this
+path.  Steps are replayed from a CUDA graph with inputs in HBM, timed with CUDA
 events on the launching stream; a 256 MiB buffer is written between timed
-steps so every step starts with a cold L2 (126 MB).  `e2e` is the same step
-through the public API (blackhole_b200.hex_moe.hex_moe) with the inputs copied
-from pinned host memory and the output copied back inside the timed region.
-`roofline` is for the dominant kernel (the gate/up grouped GEMM), timed alone
-the same way.  `cpu_baseline` times the CPU oracle (a C restatement of the
-reference's torch moe_reference) on this host.
+steps (cold L2, 126 MB).  `e2e` is the same step through the public API
+(hex_moe / EPMoE) with the inputs copied from pinned host memory and the
+output copied back inside the timed region.  `roofline` is for the dominant
+kernel, the gate/up grouped GEMM of the 1-GPU layer, timed alone (tensor-bound).
 
-Multi-GPU (torchrun, one process per GPU): the decode path does not shard
-(replicas only): each rank runs its own batch, `value` is the sum of all ranks'
-tokens over the slowest rank's time (max over ranks), scaling "weak".
+Other objects of the line: `decode` (cfg2: all-3-bit, T = 64 with the decode
+roofline against HBM, and the 1/8/32/64 sweep), `prefill_T16384` (cfg3 at
+16384 tokens on one GPU), `cfg4_slice` (one GPU's share of cfg4 at 8 GPUs: 16
+experts of H=4096, I=1536, 1024 tokens routed over them); at N>1 `ep` (per-phase
+times, per-rank expert time, and a bit-exactness check of rank 0's output), and
+at N=8 `cfg4_ep` and `cfg5_ep` (128 experts 16 per GPU; Zipf-skewed routing at
+32768 tokens).  `cpu_baseline`: the oracle (a C restatement of the reference's
+moe_reference) on the host cores over a bounded sample of the headline.
+`gpu_reference`: the reference's own Triton hex_moe on the same GPU, when a copy
+of it is installed under baseline/_ref.
 
 --impl reference times the reference's CPU implementation of the path (the
-oracle port of hex_ref.moe_reference, all host threads) on the same metric; each
-step is a bounded sample: the experts of one eighth of the layer, with their
-routed slots, dequantized and multiplied as moe_reference does per call;
-tokens are counted as slots processed / top-k.
+oracle port of hex_ref.moe_reference, all host threads) on the headline config;
+each step is a bounded sample: a fixed slice of the batch's tokens through every
+expert, dequantized per call as moe_reference does.
 """
 
 from __future__ import annotations
@@ -36,7 +42,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import time
 from pathlib import Path
@@ -46,6 +51,7 @@ sys.path[:0] = [str(ROOT / "blackhole-harness_b200"), str(ROOT / "oracle")]
 
 METRIC = "HEX MoE layer tokens/s (decode & prefill) and % of HBM / bf16 roofline, 1/2/4/8 B200"
 E, H, I, K_TOP, BLOCK = 96, 2048, 768, 8, 128
+T_PREFILL = 4096
 FLUSH_BYTES = 256 << 20
 
 
@@ -59,8 +65,8 @@ def peaks() -> dict:
 
 
 class Clocks:
-    """SM clock and throttle-reason sampling (NVML, back to back: a few hundred µs per
-    sample) during the timed region."""
+    """SM clock and throttle-reason sampling (NVML) on a thread, each sample time-
+    stamped, so the samples inside a timed window can be picked out afterwards."""
     REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
                0x80: "hw_power_brake_slowdown"}
 
@@ -90,24 +96,30 @@ class Clocks:
                 rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
                 if i % 10 == 0:     # the power query is the slow one: every tenth sample
                     pw = nv.nvmlDeviceGetPowerUsage(self.h) / 1000.0
-                self.samples.append((sm, rs, pw))
+                self.samples.append((time.perf_counter(), sm, rs, pw))
                 i += 1
             except Exception:  # noqa: BLE001
                 pass
-            self.stop_ev.wait(0.0001)
+            self.stop_ev.wait(0.0002)
 
-    def stop(self) -> dict | None:
+    def stop(self, window: tuple[float, float] | None = None) -> dict | None:
+        """Summary of the samples (those inside `window` = (t0, t1) perf_counter
+        seconds, when given and any fall inside it)."""
         if self.thread is None:
             return None
         self.stop_ev.set()
         self.thread.join(timeout=2)
-        if not self.samples:
+        smp = self.samples
+        if window:
+            inside = [s for s in smp if window[0] <= s[0] <= window[1]]
+            smp = inside or smp
+        if not smp:
             return None
-        sm = [s[0] for s in self.samples]
+        sm = [s[1] for s in smp]
         loaded = [x for x in sm if x > 0.5 * self.max_mhz] or sm
-        reasons = sorted({name for _, rs, _ in self.samples for bit, name in self.REASONS.items() if rs & bit})
+        reasons = sorted({name for _, _, rs, _ in smp for bit, name in self.REASONS.items() if rs & bit})
         return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": self.max_mhz, "reasons": reasons,
-                "samples": len(sm), "power_w_max": max(s[2] for s in self.samples)}
+                "samples": len(sm), "power_w_max": max(s[3] for s in smp)}
 
 
 def graphed(fn):
@@ -126,16 +138,36 @@ def graphed(fn):
     return g
 
 
-def build_layer(device, seed=0, bits="3", E_=E, H_=H, I_=I, block=BLOCK):
+def time_steps(fn, steps: int, flush, stream) -> list[float]:
+    """ms of each of `steps` calls of fn, CUDA events on `stream`, L2 flushed before each."""
     import torch
+    times = []
+    for _ in range(steps):
+        flush()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        fn()
+        b.record(stream)
+        times.append((a, b))
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in times]
 
-    from blackhole_b200 import hex_data as hd
+
+def max_over_ranks(ms: float, world: int, dev) -> float:
+    if world == 1:
+        return ms
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t)
+
+
+def build_tiers(layer_tiers, num_experts: int):
     from blackhole_b200.hex_moe import HexTier
-    L = hd.synth_layer(E_, H_, I_, bits, block, seed=seed, device=device)
-    tiers = [HexTier(t["bits"], t["experts"], t["gate_proj"], t["up_proj"], t["down_proj"]).prepare(E_)
-             for t in L.tiers]
-    torch.cuda.synchronize(device)
-    return L, tiers
+    return [HexTier(t["bits"], t["experts"], t["gate_proj"], t["up_proj"], t["down_proj"]).prepare(num_experts)
+            for t in layer_tiers]
 
 
 def weight_bytes(tiers_bits: dict, block: int, H_: int, I_: int, projections: int = 3) -> float:
@@ -156,117 +188,343 @@ def routed_bits(L, ids) -> dict:
     return out
 
 
-def time_steps(fn, steps: int, flush, stream) -> list[float]:
-    import torch
-    times = []
-    for _ in range(steps):
-        flush()
-        a = torch.cuda.Event(enable_timing=True)
-        b = torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        fn()
-        b.record(stream)
-        times.append((a, b))
-    torch.cuda.synchronize()
-    return [a.elapsed_time(b) for a, b in times]
+def moe_flops(tokens: int, k: int, H_: int, I_: int, projections: int = 3) -> float:
+    """Algorithmic FLOPs of the routed experts: 2 * slots * projections * H * I (padding not counted)."""
+    return 2.0 * tokens * k * projections * H_ * I_
 
 
-def cpu_baseline(sample_experts: int = 12, T: int = 64, seed: int = 0) -> dict:
-    """The oracle (C port of hex_ref.moe_reference) on this host's cores, on a bounded
-    sample of the workload: the routed slots of `sample_experts` of the 96 experts,
-    dequantized and multiplied per call as the reference does."""
+# ---------------------------------------------------------------------------- CPU (oracle) arms
+def _oracle_layer(L, keep_experts=None):
+    """hexoracle.Layer over a synthetic layer's tiers (numpy views)."""
     import numpy as np
     import torch
 
     import hexoracle
+    tiers = []
+    for t in L.tiers:
+        d = {"bits": t["bits"], "experts": t["experts"].cpu().numpy().astype(np.int64)}
+        for p in ("gate_proj", "up_proj", "down_proj"):
+            d[p] = {q: (v.view(torch.int32) if v.dtype == torch.uint32 else v).cpu().numpy() for q, v in t[p].items()}
+        tiers.append(d)
+    return hexoracle.Layer(tiers, L.E, L.H, L.I, L.block)
+
+
+def headline_inputs(rank: int = 0, T: int = T_PREFILL, device="cpu"):
+    from blackhole_b200 import hex_data as hd
+    w, ids = hd.synth_routing(T, E, K_TOP, seed=5 + 1000 * rank, device=device)
+    x = hd.synth_x(T, H, seed=6 + 1000 * rank, device=device)
+    return x, w, ids
+
+
+def cpu_baseline(sample_tokens: int = 32, reps: int = 2) -> dict:
+    """The oracle (C port of hex_ref.moe_reference) on this host's cores, on a bounded
+    sample of the headline workload: `sample_tokens` of the 4096 tokens through
+    the layer, every expert dequantized per call as the reference does."""
+    import hexoracle
     from blackhole_b200 import hex_data as hd
     threads = hexoracle.set_threads(os.cpu_count())
-    L = hd.synth_layer(E, H, I, "3", BLOCK, seed=seed)
-    w, ids = hd.synth_routing(T, E, K_TOP, seed=seed + 1)
-    x = hd.synth_x(T, H, seed=seed + 2).float().numpy()
-    t = L.tiers[0]
-    keep = list(range(sample_experts))
-    sub = {"bits": 3, "experts": np.array(keep, np.int64)}
-    for p in ("gate_proj", "up_proj", "down_proj"):
-        sub[p] = {q: (v[keep].view(torch.int32) if v.dtype == torch.uint32 else v[keep]).numpy()
-                  for q, v in t[p].items()}
-    slots = int(np.isin(ids.numpy(), keep).sum())
-    layer = hexoracle.Layer([sub], E, H, I, BLOCK)
-    layer.forward(x, w.numpy(), ids.numpy())               # warm-up (page-in)
+    L = hd.synth_layer(E, H, I, "mixed", BLOCK, seed=3)
+    x, w, ids = headline_inputs()
+    xs, ws, ids_s = x[:sample_tokens].float().numpy(), w[:sample_tokens].numpy(), ids[:sample_tokens].numpy()
+    layer = _oracle_layer(L)
+    layer.forward(xs, ws, ids_s)                        # warm-up (page-in)
     t0 = time.perf_counter()
-    reps = 2
     for _ in range(reps):
-        layer.forward(x, w.numpy(), ids.numpy())
+        layer.forward(xs, ws, ids_s)
     dt = (time.perf_counter() - t0) / reps
-    tok = slots / K_TOP
-    layer.forward(x, w.numpy(), ids.numpy(), cache_weights=True)     # fills the dequantized cache
+    layer.forward(xs, ws, ids_s, cache_weights=True)    # fills the dequantized cache
     t1 = time.perf_counter()
-    layer.forward(x, w.numpy(), ids.numpy(), cache_weights=True)
-    layer.forward(x, w.numpy(), ids.numpy(), cache_weights=True)
-    dt_mm = time.perf_counter() - t1
-    return {"value": tok / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"T={T} decode batch, the {slots} slots routed to {sample_experts} of {E} experts per call "
-                      f"({tok:.1f} token-equivalents), weights dequantized every call as hex_ref.moe_reference does",
-            "seconds_per_call": dt, "matmul_only_tokens_per_s": tok / (dt_mm / 2 if dt_mm > 0 else 1)}
+    for _ in range(reps):
+        layer.forward(xs, ws, ids_s, cache_weights=True)
+    dt_mm = (time.perf_counter() - t1) / reps
+    return {"value": sample_tokens / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{sample_tokens} of the {T_PREFILL} cfg3 prefill tokens per call (top-{K_TOP}, all {E} mixed "
+                      "3/4-bit experts dequantized every call as hex_ref.moe_reference does)",
+            "seconds_per_call": dt, "matmul_only_tokens_per_s": sample_tokens / dt_mm}
 
 
 def reference_arm(args) -> None:
-    """--impl reference: the reference's CPU path (oracle port) on the host cores."""
-    import numpy as np
-    import torch
-
+    """--impl reference: the reference's CPU path (oracle port of moe_reference) on
+    the host cores, on the headline config; rank 0 alone."""
     import hexoracle
     from blackhole_b200 import hex_data as hd
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
+    if int(os.environ.get("RANK", "0")) != 0:
         return
     threads = hexoracle.set_threads(os.cpu_count())
-    T = args.tokens
-    L = hd.synth_layer(E, H, I, "3", BLOCK, seed=0)
-    w, ids = hd.synth_routing(T, E, K_TOP, seed=1)
-    x = hd.synth_x(T, H, seed=2).float().numpy()
-    t = L.tiers[0]
-    groups = 8
-    per = E // groups
-    layers, tok = [], []
-    for g in range(groups):
-        keep = list(range(g * per, (g + 1) * per))
-        sub = {"bits": 3, "experts": np.array(keep, np.int64)}
-        for p in ("gate_proj", "up_proj", "down_proj"):
-            sub[p] = {q: (v[keep].view(torch.int32) if v.dtype == torch.uint32 else v[keep]).numpy()
-                      for q, v in t[p].items()}
-        layers.append(hexoracle.Layer([sub], E, H, I, BLOCK))
-        tok.append(float(np.isin(ids.numpy(), keep).sum()) / K_TOP)
+    L = hd.synth_layer(E, H, I, "mixed", BLOCK, seed=3)
+    x, w, ids = headline_inputs()
+    layer = _oracle_layer(L)
+    per = 32
+    slices = T_PREFILL // per
+
+    def step(s):
+        sl = slice((s % slices) * per, (s % slices + 1) * per)
+        layer.forward(x[sl].float().numpy(), w[sl].numpy(), ids[sl].numpy())
+
     for s in range(args.warmup):
-        layers[s % groups].forward(x, w.numpy(), ids.numpy())
-    done, secs = 0.0, 0.0
+        step(s)
+    secs = 0.0
     for s in range(args.steps):
         t0 = time.perf_counter()
-        layers[s % groups].forward(x, w.numpy(), ids.numpy())
+        step(s)
         secs += time.perf_counter() - t0
-        done += tok[s % groups]
-    value = done / secs
+    value = per * args.steps / secs
     line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": secs / args.steps * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-            "config": {"workload": f"cfg2 decode: E={E} H={H} I={I} top-{K_TOP}, 3-bit HEX, fp8 block-{BLOCK} "
-                                   f"scales, T={T}", "tokens": T, "parallelism": "host cores"},
+            "config": {"workload": f"cfg3 prefill: E={E} H={H} I={I} top-{K_TOP}, mixed 3/4-bit HEX, fp8 block-{BLOCK} "
+                                   f"scales, {T_PREFILL} tokens", "tokens": T_PREFILL, "parallelism": "host cores"},
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
-                             "sample": f"each step: the slots of {per} of {E} experts (one eighth of the layer, "
-                                       "rotating), dequantized and multiplied as hex_ref.moe_reference"},
+                             "sample": f"each step: {per} of the {T_PREFILL} tokens (a rotating slice) through all {E} "
+                                       "experts, dequantized and multiplied as hex_ref.moe_reference"},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------- one-GPU measurements
+def gate_up_alone(layer, x, w, ids, bm: int, steps: int, flush, stream):
+    """ms per launch of the gate/up grouped GEMM alone (graph-replayed, L2 flushed)."""
+    T, k = ids.shape
+    plan = layer.plan(ids, bm)
+    xs = layer.gather(x, k, plan, bm)
+    act = layer.gate_up(xs, T, k, plan, bm)
+    g = graphed(lambda: layer.gate_up(xs, T, k, plan, bm, act))
+    for _ in range(3):
+        g.replay()
+    ms = time_steps(g.replay, steps, flush, stream)
+    return sum(ms) / len(ms)
+
+
+def layer_step_ms(layer, x, w, ids, bm: int, steps: int, flush, stream, warmup: int = 3) -> float:
+    g = graphed(lambda: layer.forward(x, w, ids, bm))
+    for _ in range(warmup):
+        g.replay()
+    ms = time_steps(g.replay, steps, flush, stream)
+    return sum(ms) / len(ms)
+
+
+def prefill_one_gpu(dev, layer, T: int, steps: int, flush, stream, pk, seed: int = 50) -> dict:
+    from blackhole_b200 import hex_data as hd
+    w, ids = hd.synth_routing(T, E, K_TOP, seed=seed, device=dev)
+    x = hd.synth_x(T, H, seed=seed + 1, device=dev)
+    t = layer_step_ms(layer, x, w, ids, 128, steps, flush, stream)
+    fl = moe_flops(T, K_TOP, H, I)
+    return {"workload": f"cfg3 prefill: E={E} H={H} I={I} top-{K_TOP}, mixed 3/4-bit HEX, fp8 block-{BLOCK} scales, "
+                        f"T={T}, 1 GPU", "tokens_per_s": T / (t * 1e-3), "ms": t, "TFLOPs": fl / t / 1e9,
+            "bf16_frac": fl / t / 1e9 / pk["bf16_tflops"]}
+
+
+def decode_block(dev, steps: int, flush, stream, pk) -> dict:
+    """cfg2 decode: all-3-bit 96-expert layer, T = 64 (roofline against HBM: the
+    gate/up kernel alone and the whole layer), and the 1/8/32/64 sweep."""
+    from blackhole_b200 import hex_data as hd
+    from blackhole_b200.hex_moe import layer_for
+    L = hd.synth_layer(E, H, I, "3", BLOCK, seed=0, device=dev)
+    layer = layer_for(build_tiers(L.tiers, E))
+    out = {"workload": f"cfg2 decode: E={E} H={H} I={I} top-{K_TOP}, 3-bit/8-level HEX, fp8 block-{BLOCK} scales, "
+                       "1 GPU, block_m 16", "sweep": {}}
+    for T in (1, 8, 32, 64):
+        w, ids = hd.synth_routing(T, E, K_TOP, seed=1 if T == 64 else 10 + T, device=dev)
+        x = hd.synth_x(T, H, seed=2 if T == 64 else 20 + T, device=dev)
+        t = layer_step_ms(layer, x, w, ids, 16, steps, flush, stream)
+        rb = routed_bits(L, ids.cpu())
+        byts = weight_bytes(rb, BLOCK, H, I) + 2 * T * H * 2 + T * K_TOP * 12
+        out["sweep"][f"T={T}"] = {"tokens_per_s": T / (t * 1e-3), "us": t * 1e3, "experts_routed": sum(rb.values()),
+                                  "GBps": byts / t / 1e6, "hbm_frac": byts / t / 1e6 / pk["hbm_gbs"]}
+        if T == 64:
+            gu = gate_up_alone(layer, x, w, ids, 16, steps, flush, stream)
+            gu_bytes = weight_bytes(rb, BLOCK, H, I, projections=2) + T * K_TOP * (H + I) * 2
+            out.update({"tokens": T, "tokens_per_s": T / (t * 1e-3), "ms": t, "experts_routed": sum(rb.values()),
+                        "roofline": {"bound": "hbm", "kernel": "hex_gemm_kernel<GLU> (gate/up)", "ms": gu,
+                                     "algorithmic_bytes": gu_bytes, "achieved": gu_bytes / gu / 1e6,
+                                     "peak": pk["hbm_gbs"], "unit": "GB/s",
+                                     "frac": gu_bytes / gu / 1e6 / pk["hbm_gbs"],
+                                     "peak_src": pk["src"] + " (hbm_gbs)",
+                                     "traffic": read_traffic("gate_up_cfg2_T64_dram_bytes"),
+                                     "layer_bytes": byts, "layer_achieved_gbs": byts / t / 1e6,
+                                     "layer_frac": byts / t / 1e6 / pk["hbm_gbs"]}})
+    return out
+
+
+def cfg4_slice(dev, steps: int, flush, stream, pk) -> dict:
+    """One GPU's share of cfg4 at 8 GPUs: 16 of the 128 experts (H=4096, I=1536,
+    mixed 3/4-bit, block-128 scales) with 1024 tokens routed top-8 over them."""
+    from blackhole_b200 import hex_data as hd
+    from blackhole_b200.hex_moe import layer_for
+    E4, H4, I4, T4 = 16, 4096, 1536, 1024
+    L = hd.synth_layer(E4, H4, I4, "mixed", BLOCK, seed=44, device=dev)
+    layer = layer_for(build_tiers(L.tiers, E4))
+    w, ids = hd.synth_routing(T4, E4, K_TOP, seed=45, device=dev)
+    x = hd.synth_x(T4, H4, seed=46, device=dev)
+    t = layer_step_ms(layer, x, w, ids, 128, steps, flush, stream)
+    fl = moe_flops(T4, K_TOP, H4, I4)
+    return {"workload": "cfg4 per-GPU slice: 16 experts H=4096 I=1536 top-8 over them, mixed 3/4-bit, 1024 tokens",
+            "tokens_per_s": T4 / (t * 1e-3), "ms": t, "TFLOPs": fl / t / 1e9, "bf16_frac": fl / t / 1e9 / pk["bf16_tflops"]}
+
+
+def read_traffic(key: str):
+    """DRAM bytes per launch of a kernel from the committed ncu summary, if any."""
+    p = ROOT / "profiles" / "traffic.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()).get(key)
+        except (ValueError, AttributeError):
+            return None
+    return None
+
+
+# ---------------------------------------------------------------------------- expert parallelism
+def make_ep(dev, rank: int, world: int, L, num_experts: int, hidden: int, max_tokens: int):
+    from blackhole_b200.ep import EPMoE, ExpertShard, shard_tiers
+    shard = ExpertShard(num_experts, rank, world)
+    local = build_tiers(shard_tiers(L.tiers, shard), num_experts)
+    return EPMoE(shard, local, block_m=128, max_tokens=max_tokens, topk=K_TOP, hidden=hidden), shard
+
+
+def ep_phases(ep, x, w, ids, dev, world: int, reps: int = 5) -> dict:
+    """Per-phase ms (dispatch / experts / combine) of eager EP forwards, this rank's
+    mean, and every rank's expert-phase ms (all ranks take part)."""
+    import torch
+    import torch.distributed as dist
+    acc = torch.zeros(3, dtype=torch.float64)
+    for _ in range(reps):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        ep(x, w, ids, events=ev)
+        torch.cuda.synchronize()
+        acc += torch.tensor([ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2]), ev[2].elapsed_time(ev[3])],
+                            dtype=torch.float64)
+    mine = (acc / reps).to(dev)
+    every = [torch.zeros_like(mine) for _ in range(world)]
+    dist.all_gather(every, mine)
+    per_rank = [[round(float(v), 4) for v in t.cpu()] for t in every]
+    return {"dispatch_ms": float(mine[0]), "experts_ms": float(mine[1]), "combine_ms": float(mine[2]),
+            "per_rank_dispatch_experts_combine_ms": per_rank}
+
+
+def ep_run(dev, rank: int, world: int, L, num_experts: int, hidden: int, inter: int, T: int, steps: int, flush,
+           stream, pk, seed: int, zipf=None, label: str = "") -> tuple[dict, object]:
+    """One EP workload: max-over-ranks ms per graph-replayed step and phase times."""
+    import torch
+    import torch.distributed as dist
+
+    from blackhole_b200 import hex_data as hd
+    ep, shard = make_ep(dev, rank, world, L, num_experts, hidden, T)
+    w, ids = hd.synth_routing(T, num_experts, K_TOP, seed=seed + 1000 * rank, zipf=zipf, device=dev)
+    x = hd.synth_x(T, hidden, seed=seed + 1 + 1000 * rank, device=dev)
+    for _ in range(2):
+        ep(x, w, ids)
+    g = graphed(lambda: ep(x, w, ids))
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    dist.barrier()
+    ms = time_steps(g.replay, steps, flush, stream)
+    step = max_over_ranks(sum(ms) / len(ms), world, dev)
+    ph = ep_phases(ep, x, w, ids, dev, world)
+    fl = moe_flops(T * world, K_TOP, hidden, inter)
+    res = {"workload": label, "tokens_per_s": world * T / (step * 1e-3), "ms": step, "TFLOPs": fl / step / 1e9,
+           "bf16_frac_per_gpu": fl / world / step / 1e9 / pk["bf16_tflops"], "scaling": "weak", **ph}
+    del g
+    torch.cuda.synchronize()
+    return res, (ep, shard, x, w, ids)
+
+
+def ep_bit_check(L, ep_state, got) -> dict:
+    """Rank 0: `got`, the EP output of its tokens (from a forward every rank
+    made), against the single-GPU layer's per-slot rows of the same tokens put
+    through the EP combine (bit for bit), and against the plain single-GPU
+    layer (max abs difference)."""
+    import torch
+
+    from blackhole_b200.ep import reference_combine
+    from blackhole_b200.hex_moe import layer_for
+    ep, shard, x, w, ids = ep_state
+    full = layer_for(build_tiers(L.tiers, L.E))
+    y = full.forward_slots(x, w, ids, 128)
+    want = reference_combine(y, ids, shard, x.dtype)
+    plain = full.forward(x, w, ids, 128)
+    torch.cuda.synchronize()
+    d = (got.float() - plain.float()).abs()
+    tol = bool(torch.all(d <= 1e-2 + 2e-2 * plain.float().abs()))
+    return {"bit_equal": bool(torch.equal(got, want)), "tokens_checked": int(x.shape[0]),
+            "max_abs_err_vs_single_gpu_layer": float(d.max()), "within_layer_tolerance": tol}
+
+
+# ---------------------------------------------------------------------------- the reference's GPU kernel
+def gpu_reference(dev, steps: int, flush, stream) -> dict:
+    """The reference's own Triton path (runtime/blackhole_runtime/hex_moe.py, an
+    unmodified copy installed under baseline/_ref) on the same GPU and the same
+    synthetic layers and routings: hex_moe(path="fused") replayed from a CUDA
+    graph (as its hex_check.timeit does) and path="dequant" (its prefill path:
+    every expert to bf16, then vLLM's fused_experts) eagerly, L2 flushed between
+    steps.  Its layout fixes 32-input scale blocks, so the block-128 codes are
+    repeated 4x along the inputs (identical weights).  Context only: nothing of
+    this repository runs on this path."""
+    ref = ROOT / "baseline" / "_ref"
+    if not (ref / "blackhole_runtime" / "hex_moe.py").exists():
+        return {"unavailable": "the reference runtime is not installed under baseline/_ref"}
+    import torch
+    sys.path.insert(0, str(ref))
+    try:
+        from blackhole_runtime import hex_moe as rh
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"import failed: {type(e).__name__}: {e}"}
+    from blackhole_b200 import hex_data as hd
+    out = {"source": "baseline/_ref/blackhole_runtime/hex_moe.py (reference, unmodified)"}
+
+    def ref_tiers(L):
+        ts = []
+        for t in L.tiers:
+            parts = []
+            for p in ("gate_proj", "up_proj", "down_proj"):
+                d = {q: v.clone() for q, v in t[p].items()}
+                d["block_scale"] = hd.expand_block_scale(d["block_scale"], L.block)
+                parts.append(d)
+            ts.append(rh.HexTier(t["bits"], t["experts"].clone(), *parts).prepare(L.E))
+        return ts
+
+    def timed(fn, graph: bool) -> float:
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        run = graphed(fn).replay if graph else fn
+        return sum(time_steps(run, steps, flush, stream)) / steps
+
+    cases = (("cfg3_prefill_T4096", "mixed", 3, T_PREFILL, (("fused", True), ("dequant", False))),
+             ("cfg2_decode_T64", "3", 0, 64, (("fused", True),)))
+    for name, bits, seed, T, paths in cases:
+        try:
+            L = hd.synth_layer(E, H, I, bits, BLOCK, seed=seed, device=dev)
+            tiers = ref_tiers(L)
+            if T == T_PREFILL:
+                x, w, ids = headline_inputs(0, T, dev)
+            else:
+                w, ids = hd.synth_routing(T, E, K_TOP, seed=1, device=dev)
+                x = hd.synth_x(T, H, seed=2, device=dev)
+            res = {}
+            for path, graph in paths:
+                try:
+                    ms = timed(lambda: rh.hex_moe(x, w, ids, tiers, path=path), graph)
+                    res[path] = {"ms": ms, "tokens_per_s": T / (ms * 1e-3)}
+                except Exception as e:  # noqa: BLE001
+                    res[path] = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
+            out[name] = res
+            del tiers, L
+            torch.cuda.empty_cache()
+        except Exception as e:  # noqa: BLE001
+            out[name] = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
+    return out
+
+
+# ---------------------------------------------------------------------------- main
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--tokens", type=int, default=64)
     ap.add_argument("--impl", default="b200", choices=("b200", "reference"))
-    ap.add_argument("--no-extras", action="store_true", help="skip the sweep, prefill and CPU baseline")
-    ap.add_argument("--profile", action="store_true", help="a few launches only (for ncu)")
+    ap.add_argument("--no-extras", action="store_true", help="headline, e2e and roofline only")
+    ap.add_argument("--profile", action="store_true", help="a few eager headline steps only (for ncu)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -276,8 +534,8 @@ def main() -> None:
     import torch
     import torch.distributed as dist
 
-    from blackhole_b200 import hex_data as hd
     from blackhole_b200.hex_moe import device_status, hex_moe, layer_for
+    from blackhole_b200 import hex_data as hd
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -287,236 +545,147 @@ def main() -> None:
     if world > 1:
         from datetime import timedelta
         os.environ.setdefault("NCCL_DEBUG", "WARN")     # stdout carries the JSON line only
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-    T = args.tokens
-    L, tiers = build_layer(dev, seed=0)
-    layer = layer_for(tiers)
-    w, ids = hd.synth_routing(T, E, K_TOP, seed=1 + 1000 * rank)
-    x = hd.synth_x(T, H, seed=2 + 1000 * rank, device=dev)
-    w, ids = w.to(dev), ids.to(dev)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
+    pk = peaks()
     stream = torch.cuda.current_stream(dev)
     flush_buf = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
 
     def flush():
         flush_buf.fill_(rank & 0xFF)
 
-    bm = 16 if T <= 64 else 128     # align block height: decode batches / prefill
+    # ---- the headline step: cfg3 prefill, 4096 tokens per GPU
+    T = T_PREFILL
+    L3 = hd.synth_layer(E, H, I, "mixed", BLOCK, seed=3, device=dev)
+    x, w, ids = headline_inputs(rank, T, dev)
+    layer, tiers3, ep, shard = None, None, None, None
+    if world == 1:
+        tiers3 = build_tiers(L3.tiers, E)
+        layer = layer_for(tiers3)
 
-    def step_eager():
-        layer.forward(x, w, ids, bm)
+        def step_fn():
+            return layer.forward(x, w, ids, 128)
+        launches = 7       # align (count, plan, scatter), gather, gate/up, down, combine
+        par = "1 GPU"
+    else:
+        ep, shard = make_ep(dev, rank, world, L3, E, H, T)
 
+        def step_fn():
+            return ep(x, w, ids)
+        launches = 12      # plan, send, wait, align x3, gather, gate/up, down, return, wait, combine
+        par = f"expert parallel x{world}: {E // world} experts per GPU, token rows over NVLink peer memory"
     if args.profile:
         for _ in range(args.warmup):
-            step_eager()
-        plan = layer.plan(ids, bm)
-        xs = layer.gather(x, K_TOP, plan, bm)
-        act = layer.gate_up(xs, T, K_TOP, plan, bm)
-        layer.down(act, w, plan, bm)
+            step_fn()
         torch.cuda.synchronize()
         return
-
-    for _ in range(args.warmup):
-        step_eager()
-    g_step = graphed(step_eager)
-    step = g_step.replay
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
     clocks = Clocks(local)
+    for _ in range(args.warmup):
+        step_fn()
+    g_step = graphed(step_fn)
+    for _ in range(args.warmup):
+        g_step.replay()
     torch.cuda.synchronize()
-    t_wall = time.perf_counter()
-    ms = time_steps(step, args.steps, flush, stream)
-    t_wall = time.perf_counter() - t_wall
-    clk = clocks.stop()
-    step_ms = sum(ms) / len(ms)
     if world > 1:
-        tt = torch.tensor([sum(ms)], device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        step_ms = float(tt) / len(ms)
         dist.barrier()
+    t0 = time.perf_counter()
+    ms = time_steps(g_step.replay, args.steps, flush, stream)
+    t1 = time.perf_counter()
+    clk = clocks.stop(window=(t0, t1))
+    step_ms = max_over_ranks(sum(ms) / len(ms), world, dev)
     value = world * T / (step_ms * 1e-3)
 
     # ---- e2e through the public API: pinned host inputs in, output back, each step
-    xh = x.cpu().pin_memory()
-    wh = w.cpu().pin_memory()
-    ih = ids.cpu().pin_memory()
+    xh, wh, ih = x.cpu().pin_memory(), w.cpu().pin_memory(), ids.cpu().pin_memory()
     oh = torch.empty(T, H, dtype=x.dtype).pin_memory()
 
     def e2e_step():
         xd = xh.to(dev, non_blocking=True)
         wd = wh.to(dev, non_blocking=True)
         idd = ih.to(dev, non_blocking=True)
-        out = hex_moe(xd, wd, idd, tiers, {"BLOCK_M": bm})
+        out = hex_moe(xd, wd, idd, tiers3, {"BLOCK_M": 128}) if world == 1 else ep(xd, wd, idd)
         oh.copy_(out, non_blocking=True)
 
     for _ in range(args.warmup):
         e2e_step()
-    e2e_ms = time_steps(e2e_step, args.steps, flush, stream)
-    e2e_step_ms = sum(e2e_ms) / len(e2e_ms)
+    torch.cuda.synchronize()
     if world > 1:
-        tt = torch.tensor([sum(e2e_ms)], device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        e2e_step_ms = float(tt) / len(e2e_ms)
-    h2d = xh.numel() * xh.element_size() + wh.numel() * 4 + ih.numel() * 8
+        dist.barrier()
+    e2e_ms = time_steps(e2e_step, args.steps, flush, stream)
+    e2e_step_ms = max_over_ranks(sum(e2e_ms) / len(e2e_ms), world, dev)
+    h2d = xh.numel() * xh.element_size() + wh.numel() * 4 + ih.numel() * ih.element_size()
     d2h = oh.numel() * oh.element_size()
 
-    # ---- dominant kernel alone: the gate/up grouped GEMM
-    plan = layer.plan(ids, bm)
-    xs = layer.gather(x, K_TOP, plan, bm)
-    act = layer.gate_up(xs, T, K_TOP, plan, bm)
-    g_gu = graphed(lambda: layer.gate_up(xs, T, K_TOP, plan, bm, act))
-    for _ in range(args.warmup):
-        g_gu.replay()
-    gu_ms = time_steps(g_gu.replay, args.steps, flush, stream)
-    gu = sum(gu_ms) / len(gu_ms)
-    rb = routed_bits(L, ids.cpu())
-    U = sum(rb.values())
-    gu_bytes = weight_bytes(rb, BLOCK, H, I, projections=2) + T * K_TOP * (H + I) * 2   # weights, token rows, act
-    layer_bytes = weight_bytes(rb, BLOCK, H, I, projections=3) + 2 * T * H * 2 + T * K_TOP * 12
-    pk = peaks()
-    err = device_status(local)
-
     extras = {}
-    if world > 1 and not args.no_extras:
-        extras["prefill_ep"] = run_ep_prefill(dev, rank, world, flush, stream, pk)   # every rank takes part
-    if not args.no_extras and rank == 0:
-        extras.update(run_extras(dev, L, tiers, layer, flush, stream, args, pk, cpu=world == 1))
+    # ---- expert parallelism: phases, per-rank expert time, rank 0's bit check (all ranks take part)
+    if world > 1:
+        got = ep(x, w, ids)
+        torch.cuda.synchronize()
+        ph = ep_phases(ep, x, w, ids, dev, world)
+        extras["ep"] = {"workload": f"cfg3 prefill, {E // world} experts and {T} tokens per GPU", **ph}
+        if rank == 0:
+            extras["ep"]["check"] = ep_bit_check(L3, (ep, shard, x, w, ids), got)
+        if world == 8 and not args.no_extras:
+            L4 = hd.synth_layer(128, 4096, 1536, "mixed", BLOCK, seed=44, device=dev)
+            r4, st4 = ep_run(dev, rank, world, L4, 128, 4096, 1536, 8192 // world, args.steps, flush, stream, pk, 61,
+                             label="cfg4: 128 experts H=4096 I=1536 top-8 mixed 3/4-bit, 16 per GPU, 8192 tokens")
+            st4[0].close()
+            del L4, st4
+            L5 = hd.synth_layer(E, H, I, "3", BLOCK, seed=9, device=dev)
+            r5, st5 = ep_run(dev, rank, world, L5, E, H, I, 32768 // world, args.steps, flush, stream, pk, 71,
+                             zipf=1.2, label="cfg5: 96 experts 3-bit, Zipf(1.2) routing skew, 32768 tokens, 12 per GPU")
+            st5[0].close()
+            del L5, st5
+            extras["cfg4_ep"], extras["cfg5_ep"] = r4, r5
+            torch.cuda.empty_cache()
 
-    if rank != 0:
-        if world > 1:
-            dist.barrier()
-            dist.destroy_process_group()
-        return
-    launches = 5 * args.steps   # align, gather, gate/up, down, combine per step
-    traffic = read_traffic()
-    line = {
-        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"cfg2 decode: E={E} H={H} I={I} top-{K_TOP}, SwiGLU, 3-bit/8-level HEX, "
-                               f"fp8 e4m3 block-{BLOCK} scales, T={T} tokens per GPU", "tokens": T,
-                   "experts_routed": U, "block_m": bm, "parallelism": f"replicas x{world}" if world > 1 else "1 GPU",
-                   "l2": "flushed between timed steps (256 MiB write)", "timed_wall_s": t_wall},
-        "e2e": {"value": world * T / (e2e_step_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_step_ms},
-        "gpu_launches": launches,
-        "roofline": {"bound": "hbm", "kernel": "hex_gemm_kernel<GLU> (gate/up)", "achieved": gu_bytes / gu / 1e6,
-                     "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": gu_bytes / gu / 1e6 / pk["hbm_gbs"],
-                     "traffic": traffic, "peak_src": pk["src"] + " (hbm_gbs, burst)", "ms": gu,
-                     "algorithmic_bytes": gu_bytes,
-                     "layer_achieved_gbs": layer_bytes / step_ms / 1e6,
-                     "layer_frac": layer_bytes / step_ms / 1e6 / pk["hbm_gbs"], "layer_bytes": layer_bytes},
-        "clocks": clk, "device_error_word": err,
-    }
-    line.update(extras)
-    print(json.dumps(line), flush=True)
+    # ---- the dominant kernel alone: gate/up grouped GEMM of the one-GPU layer (rank 0)
+    roof = None
+    if rank == 0:
+        if layer is None:
+            tiers3 = build_tiers(L3.tiers, E)
+            layer = layer_for(tiers3)
+        gu = gate_up_alone(layer, x, w, ids, 128, args.steps, flush, stream)
+        gfl = moe_flops(T, K_TOP, H, I, projections=2)
+        roof = {"bound": "tensor", "kernel": "hex_gemm_kernel<GLU> (gate/up), cfg3 T=4096, 1 GPU",
+                "achieved": gfl / gu / 1e9, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": gfl / gu / 1e9 / pk["bf16_tflops"], "traffic": read_traffic("gate_up_cfg3_T4096_dram_bytes"),
+                "peak_src": pk["src"] + " (bf16_tflops, burst: the kernel is timed alone)", "ms": gu,
+                "algorithmic_flops": gfl}
+        if world == 1:
+            fl = moe_flops(T, K_TOP, H, I)
+            roof.update({"layer_TFLOPs": fl / step_ms / 1e9, "layer_frac": fl / step_ms / 1e9 / pk["bf16_tflops"]})
+        if world == 1 and not args.no_extras:
+            extras["decode"] = decode_block(dev, max(args.steps, 10), flush, stream, pk)
+            extras["prefill_T16384"] = prefill_one_gpu(dev, layer, 16384, max(5, args.steps // 2), flush, stream, pk)
+            extras["cfg4_slice"] = cfg4_slice(dev, max(5, args.steps // 2), flush, stream, pk)
+            torch.cuda.empty_cache()
+            try:
+                extras["cpu_baseline"] = cpu_baseline()
+            except Exception as e:  # noqa: BLE001  (the baseline is reported, not required)
+                extras["cpu_baseline"] = {"value": None, "error": f"{type(e).__name__}: {e}"}
+            extras["gpu_reference"] = gpu_reference(dev, max(5, args.steps // 2), flush, stream)
+    err = device_status(local)
+    del g_step
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"cfg3 prefill: E={E} H={H} I={I} top-{K_TOP}, SwiGLU, mixed 3/4-bit HEX (half the "
+                                   f"experts each), fp8 e4m3 block-{BLOCK} scales, {T} tokens per GPU",
+                       "tokens": T, "block_m": 128, "parallelism": par,
+                       "l2": "flushed between timed steps (256 MiB write)", "timed_wall_s": t1 - t0},
+            "e2e": {"value": world * T / (e2e_step_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": e2e_step_ms},
+            "gpu_launches": launches * args.steps, "roofline": roof, "clocks": clk, "device_error_word": err,
+        }
+        line.update(extras)
+        print(json.dumps(line), flush=True)
+    if ep is not None:
+        ep.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
-
-
-def run_ep_prefill(dev, rank: int, world: int, flush, stream, pk, T: int = 4096, steps: int = 5) -> dict:
-    """cfg3 prefill with expert parallelism: the 96 experts (mixed 3/4-bit) sharded
-    over the ranks, T tokens per rank routed to their owners by all-to-all
-    (blackhole_b200.ep), max-over-ranks time per step."""
-    import torch
-    import torch.distributed as dist
-
-    from blackhole_b200 import hex_data as hd
-    from blackhole_b200.ep import EPMoE, ExpertShard, shard_tiers
-    from blackhole_b200.hex_moe import HexTier
-    Lm = hd.synth_layer(E, H, I, "mixed", BLOCK, seed=0, device=dev)
-    shard = ExpertShard(E, rank, world)
-    local = [HexTier(t["bits"], t["experts"], t["gate_proj"], t["up_proj"], t["down_proj"]).prepare(E)
-             for t in shard_tiers(Lm.tiers, shard)]
-    del Lm
-    ep = EPMoE(shard, local)
-    w, ids = hd.synth_routing(T, E, K_TOP, seed=7 + 1000 * rank, device=dev)
-    x = hd.synth_x(T, H, seed=8 + 1000 * rank, device=dev)
-    for _ in range(2):
-        ep(x, w, ids)
-    torch.cuda.synchronize()
-    dist.barrier()
-    ms = time_steps(lambda: ep(x, w, ids), steps, flush, stream)
-    tt = torch.tensor([sum(ms)], device=dev)
-    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-    step_ms = float(tt) / steps
-    flops = 2.0 * world * T * K_TOP * 3 * H * I
-    return {"workload": f"cfg3 prefill with expert parallelism: E={E} H={H} I={I} top-{K_TOP}, mixed 3/4-bit HEX, "
-                        f"{E // world} experts and {T} tokens per GPU, NCCL all-to-all dispatch/combine",
-            "tokens_per_s": world * T / (step_ms * 1e-3), "ms": step_ms, "TFLOPs": flops / (step_ms * 1e-3) / 1e12,
-            "bf16_frac_per_gpu": flops / world / (step_ms * 1e-3) / 1e12 / pk["bf16_tflops"], "scaling": "weak"}
-
-
-def read_traffic():
-    """DRAM bytes per launch of the gate/up kernel from the committed ncu summary, if any."""
-    p = ROOT / "profiles" / "traffic.json"
-    if p.exists():
-        try:
-            return json.loads(p.read_text()).get("gate_up_cfg2_T64_dram_bytes")
-        except (ValueError, AttributeError):
-            return None
-    return None
-
-
-def run_extras(dev, L, tiers, layer, flush, stream, args, pk, cpu: bool = True) -> dict:
-    import torch
-
-    from blackhole_b200 import hex_data as hd
-    from blackhole_b200.hex_moe import layer_for
-    out = {"sweep": {}}
-    steps = max(5, args.steps // 2)
-    for T in (1, 8, 32, 64):
-        w, ids = hd.synth_routing(T, E, K_TOP, seed=10 + T)
-        x = hd.synth_x(T, H, seed=20 + T, device=dev)
-        w, ids = w.to(dev), ids.to(dev)
-        g = graphed(lambda: layer.forward(x, w, ids, 16))
-        for _ in range(3):
-            g.replay()
-        ms = time_steps(g.replay, steps, flush, stream)
-        t = sum(ms) / len(ms)
-        rb = routed_bits(L, ids.cpu())
-        byts = weight_bytes(rb, BLOCK, H, I) + 2 * T * H * 2 + T * K_TOP * 12
-        out["sweep"][f"T={T}"] = {"tokens_per_s": T / (t * 1e-3), "us": t * 1e3, "experts_routed": sum(rb.values()),
-                                  "GBps": byts / t / 1e6, "hbm_frac": byts / t / 1e6 / pk["hbm_gbs"]}
-    # prefill: cfg3 (mixed 3/4-bit, 96 experts), T = 4096, one GPU
-    del tiers
-    L3, t3 = build_layer(dev, seed=3, bits="mixed")
-    lay3 = layer_for(t3)
-    T = 4096
-    w, ids = hd.synth_routing(T, E, K_TOP, seed=5)
-    x = hd.synth_x(T, H, seed=6, device=dev)
-    w, ids = w.to(dev), ids.to(dev)
-    g3 = graphed(lambda: lay3.forward(x, w, ids, 128))
-    for _ in range(3):
-        g3.replay()
-    ms = time_steps(g3.replay, steps, flush, stream)
-    t = sum(ms) / len(ms)
-    flops = 2.0 * T * K_TOP * 3 * H * I
-    plan = lay3.plan(ids, 128)
-    xs = lay3.gather(x, K_TOP, plan, 128)
-    act = lay3.gate_up(xs, T, K_TOP, plan, 128)
-    g3u = graphed(lambda: lay3.gate_up(xs, T, K_TOP, plan, 128, act))
-    g3u.replay()
-    gms = time_steps(g3u.replay, steps, flush, stream)
-    g = sum(gms) / len(gms)
-    gflops = 2.0 * T * K_TOP * 2 * H * I
-    out["prefill"] = {"workload": "cfg3 prefill: E=96 H=2048 I=768 top-8, mixed 3/4-bit HEX (half each), "
-                                  "fp8 block-128 scales, T=4096, 1 GPU",
-                      "tokens_per_s": T / (t * 1e-3), "ms": t, "TFLOPs": flops / t / 1e9,
-                      "bf16_frac": flops / t / 1e9 / pk["bf16_tflops"],
-                      "gate_up_ms": g, "gate_up_TFLOPs": gflops / g / 1e9,
-                      "gate_up_bf16_frac": gflops / g / 1e9 / pk["bf16_tflops"]}
-    del lay3, t3, L3, act, xs, g3, g3u
-    torch.cuda.empty_cache()
-    if cpu:   # rank 0 at N=1 only
-        try:
-            out["cpu_baseline"] = cpu_baseline()
-        except Exception as e:  # noqa: BLE001  (the baseline is reported, not required)
-            out["cpu_baseline"] = {"value": None, "error": f"{type(e).__name__}: {e}"}
-    return out
 
 
 if __name__ == "__main__":

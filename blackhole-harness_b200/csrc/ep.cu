@@ -5,7 +5,7 @@
 // Experts are sharded contiguously: rank r owns global experts [r*P, (r+1)*P),
 // P = ceil(E / world).  Every rank owns one region of device memory that it
 // exports by CUDA IPC and every other rank maps, so kernels on any rank store
-// straight into any rank's region over NVLink (plain stores, no multicast):
+// straight into any rank's region over NVLink (plain stores from SMs):
 //
 //   flags      disp[world], ret[world] (uint64): the epoch a source's dispatch /
 //              a destination's return has completed, written with release

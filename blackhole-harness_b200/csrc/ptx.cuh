@@ -100,7 +100,7 @@ __device__ __forceinline__ bool mbar_wait_idle(uint64_t* bar, uint32_t parity, v
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
-// 2-D tiled load of one box into shared memory, completing on `bar` (no multicast).
+// 2-D tiled load of one box into this CTA's shared memory, completing on `bar`.
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int32_t x,
                                             int32_t y) {
   asm volatile(
