@@ -321,21 +321,26 @@ def decode_block(dev, steps: int, flush, stream, pk) -> dict:
     from blackhole_b200.hex_moe import layer_for
     L = hd.synth_layer(E, H, I, "3", BLOCK, seed=0, device=dev)
     layer = layer_for(build_tiers(L.tiers, E))
+    from blackhole_b200.hex_moe import auto_block_m
     out = {"workload": f"cfg2 decode: E={E} H={H} I={I} top-{K_TOP}, 3-bit/8-level HEX, fp8 block-{BLOCK} scales, "
-                       "1 GPU, block_m 16", "sweep": {}}
+                       "1 GPU, automatic tile height (8: the small-batch kernels, up to 8 slots per expert)",
+           "sweep": {}}
     for T in (1, 8, 32, 64):
         w, ids = hd.synth_routing(T, E, K_TOP, seed=1 if T == 64 else 10 + T, device=dev)
         x = hd.synth_x(T, H, seed=2 if T == 64 else 20 + T, device=dev)
-        t = layer_step_ms(layer, x, w, ids, 16, steps, flush, stream)
+        bm = auto_block_m(T * K_TOP, E)
+        t = layer_step_ms(layer, x, w, ids, bm, steps, flush, stream)
         rb = routed_bits(L, ids.cpu())
         byts = weight_bytes(rb, BLOCK, H, I) + 2 * T * H * 2 + T * K_TOP * 12
         out["sweep"][f"T={T}"] = {"tokens_per_s": T / (t * 1e-3), "us": t * 1e3, "experts_routed": sum(rb.values()),
-                                  "GBps": byts / t / 1e6, "hbm_frac": byts / t / 1e6 / pk["hbm_gbs"]}
+                                  "block_m": bm, "GBps": byts / t / 1e6, "hbm_frac": byts / t / 1e6 / pk["hbm_gbs"]}
         if T == 64:
-            gu = gate_up_alone(layer, x, w, ids, 16, steps, flush, stream)
+            gu = gate_up_alone(layer, x, w, ids, bm, steps, flush, stream)
             gu_bytes = weight_bytes(rb, BLOCK, H, I, projections=2) + T * K_TOP * (H + I) * 2
             out.update({"tokens": T, "tokens_per_s": T / (t * 1e-3), "ms": t, "experts_routed": sum(rb.values()),
-                        "roofline": {"bound": "hbm", "kernel": "hex_gemm_kernel<GLU> (gate/up)", "ms": gu,
+                        "block_m": bm,
+                        "roofline": {"bound": "hbm", "kernel": "gate/up grouped GEMM (hex_decode_kernel<GLU> at block_m 8)",
+                                     "ms": gu,
                                      "algorithmic_bytes": gu_bytes, "achieved": gu_bytes / gu / 1e6,
                                      "peak": pk["hbm_gbs"], "unit": "GB/s",
                                      "frac": gu_bytes / gu / 1e6 / pk["hbm_gbs"],

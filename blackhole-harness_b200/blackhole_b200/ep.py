@@ -179,9 +179,20 @@ class EPMoE:
                                                self.max_tokens, rdt, ctypes.byref(h)), "hexmoe_ep_init")
             self._ctx = h
             if shard.world > 1:
+                # every rank must build the same buffer layout: agree on it before mapping anything
+                on_dev = dist.get_backend(group) == "nccl"
+                cfg = torch.tensor([self.max_tokens, self.topk, self.hidden, rdt, shard.num_experts],
+                                   dtype=torch.int64)
+                cfg_t = cfg.to(self.device) if on_dev else cfg
+                cfgs = [torch.empty_like(cfg_t) for _ in range(shard.world)]
+                dist.all_gather(cfgs, cfg_t, group=group)
+                if any(not torch.equal(c.cpu(), cfg) for c in cfgs):
+                    _lib.lib.hexmoe_ep_destroy(h)
+                    self._ctx = None
+                    raise ValueError("EPMoE: ranks disagree on max_tokens / topk / hidden / row dtype / experts: "
+                                     f"{[c.cpu().tolist() for c in cfgs]}")
                 mine = torch.empty(_lib.EP_HANDLE_BYTES, dtype=torch.uint8)
                 _lib.check(_lib.lib.hexmoe_ep_handle(h, mine.data_ptr()), "hexmoe_ep_handle")
-                on_dev = dist.get_backend(group) == "nccl"
                 t = mine.to(self.device) if on_dev else mine
                 got = [torch.empty_like(t) for _ in range(shard.world)]
                 dist.all_gather(got, t, group=group)
@@ -269,11 +280,15 @@ class EPMoE:
         w = w.to(torch.float32)
         bad = bool(((ids < 0) | (ids >= E)).any())
         plan = plan_dispatch(ids.clamp(0, max(E - 1, 0)), self.shard)
-        # 1. rows, slots and this rank's error flag per destination, read on the host
-        info = torch.tensor([[len(plan.rows[d]), len(plan.slots[d][0]), int(bad)] for d in range(world)],
+        # 1. rows, slots, this rank's error flag, hidden and top-k per destination, read on
+        #    the host: a bad id or ranks that disagree on the shapes fail on every rank
+        #    before any row moves
+        info = torch.tensor([[len(plan.rows[d]), len(plan.slots[d][0]), int(bad), H, k] for d in range(world)],
                             dtype=torch.int64)
         recv_info = torch.empty_like(info)
         dist.all_to_all_single(recv_info, info, group=self.group)
+        if bool((recv_info[:, 3] != H).any() | (recv_info[:, 4] != k).any()):
+            raise ValueError(f"ranks disagree on hidden / topk: {recv_info[:, 3:].tolist()}")
         if bool(recv_info[:, 2].any()) or bad:
             raise ValueError("topk_ids out of range" if bad else "topk_ids out of range on another rank")
         sent_rows = [len(r) for r in plan.rows]

@@ -14,9 +14,11 @@ Same names, argument meaning and exceptions as the reference module
                             weight tile once into tensor memory, so a bf16 copy
                             of every expert in HBM (the reference's prefill path)
                             would only add traffic.  Accepted for compatibility.
-  config / align_mode       config["BLOCK_M"] (16/32/64/128) sets the tile
-                            height (tokens per expert tile); the other keys and
-                            align_mode are accepted and have no effect.
+  config / align_mode       config["BLOCK_M"] sets the tile height (tokens per
+                            expert tile): 8 runs the small-batch (decode)
+                            kernels, 16/32/64/128 the tcgen05 grouped GEMM;
+                            the other keys and align_mode are accepted and have
+                            no effect.
   dequant_all / align       hexmoe_dequant (bit-exact) / hexmoe_align (stable,
                             equal to the reference output bit for bit).
 
@@ -314,9 +316,10 @@ def combine_rows(y: torch.Tensor, T: int, k: int, rows: torch.Tensor, out_dtype=
 
 def auto_block_m(slots: int, num_experts: int) -> int:
     """The block_m hexmoe_forward picks when given 0 (api.cu auto_block_m): the
+    small-batch kernels (8) while an expert averages at most 8 slots, else the
     smallest of 16/32/64/128 covering the mean slots per expert."""
     avg = -(-slots // max(num_experts, 1))
-    for bm in (16, 32, 64):
+    for bm in (8, 16, 32, 64):
         if avg <= bm:
             return bm
     return 128
@@ -405,7 +408,7 @@ def _block_m(config: dict | None) -> int:
         env = os.environ.get("BLACKHOLE_HEX_TILES")
         return int(env.split(",")[0]) if env else 0
     bm = int(config.get("BLOCK_M", 0))
-    return bm if bm in (16, 32, 64, 128) else 0
+    return bm if bm in (8, 16, 32, 64, 128) else 0
 
 
 def hex_moe_fused(x, topk_weights, topk_ids, tiers: list[HexTier], config: dict | None = None,

@@ -20,6 +20,10 @@ struct hexmoe_layer {
   // up, down), carved from one allocation owned by the layer
   void* tiled_mem;
   const uint8_t* idx_t[kMaxTiers][3];
+  // code tables of every (tier, projection) for bf16 [0] and f16 [1] operands
+  // (launch_code_tables layout), read by the small-batch kernels
+  void* tab_mem;
+  const uint4* tab[kMaxTiers][3][2];
 };
 
 namespace {
@@ -75,8 +79,11 @@ int make_tmap(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int elem
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+// The tile height hexmoe_forward picks: the small-batch kernels (8) while an
+// expert averages at most 8 slots (decode), then the tcgen05 GEMM's heights.
 int auto_block_m(int64_t S, int32_t E) {
   const int64_t avg = (S + E - 1) / std::max(E, 1);
+  if (avg <= 8) return kDecBlock;
   if (avg <= 16) return 16;
   if (avg <= 32) return 32;
   if (avg <= 64) return 64;
@@ -104,6 +111,8 @@ WsLayout ws_layout(const hexmoe_layer_desc& d, int64_t T, int32_t k, int32_t bm,
   w.total = off;
   return w;
 }
+
+bool valid_block_m(int bm) { return bm == kDecBlock || bm == 16 || bm == 32 || bm == 64 || bm == 128; }
 
 int check_dtype16(int32_t dt, const char* what) {
   if (dt != HEXMOE_F32 && dt != HEXMOE_BF16 && dt != HEXMOE_F16) return fail(HEXMOE_E_DTYPE, "%s: bad dtype %d", what, dt);
@@ -206,6 +215,29 @@ int run_gate_up(const hexmoe_layer* layer, const void* xs, bool bf16, int64_t to
   p.out = act; p.ld_out = d.inter_pad;
   p.topk_w = nullptr;
   p.dev_err = dev_err;
+  if (bm == kDecBlock) {
+    DecParams q{};
+    for (int t = 0; t < d.num_tiers; ++t)
+      for (int j = 0; j < 2; ++j) {
+        q.idx_t[t][j] = layer->idx_t[t][j];
+        q.bs[t][j] = p.bs[t][j];
+        q.tab[t][j] = layer->tab[t][j][bf16 ? 0 : 1];
+      }
+    for (int t = 0; t < d.num_tiers; ++t) q.bits[t] = p.bits[t];
+    q.num_tiers = d.num_tiers; q.expert_map = d.expert_map; q.num_experts = d.num_experts;
+    q.sorted_ids = sid; q.expert_ids = eid; q.npp = npp; q.num_slots = static_cast<int32_t>(S);
+    q.rows_pad = d.inter_pad; q.rows_store = d.inter_pad; q.k_pad = d.hidden_pad;
+    q.block = d.block; q.m_tiles = d.inter_pad / kTileM; q.ksteps = d.hidden_pad / kKStep;
+    q.out = act; q.ld_out = d.inter_pad; q.topk_w = nullptr; q.dev_err = dev_err;
+    if (!plan_decode(q, 2)) return fail(HEXMOE_E_UNSUPPORTED, "hidden %d does not fit the small-batch kernel", d.hidden_pad);
+    if (int rc = make_tmap(&q.tm_b, xs, dt16, 2, d.hidden, static_cast<uint64_t>(max_blocks) * bm, 2ull * d.hidden, 64,
+                           kDecBlock, CU_TENSOR_MAP_SWIZZLE_128B, "x_sorted tensor map"))
+      return rc;
+    const int grid = static_cast<int>(std::min<int64_t>(layer->num_sms, max_blocks * q.m_tiles));
+    cudaError_t e = launch_decode_gemm(q, true, bf16, grid, st, pdl);
+    if (e != cudaSuccess) return cuda_fail(e, "gate/up (small batch) launch");
+    return HEXMOE_OK;
+  }
   if (int rc = plan_gemm(p, true, bm, d.hidden_pad, d.block)) return rc;
   for (int t = 0; t < d.num_tiers; ++t) {
     p.idx_t[t][0] = layer->idx_t[t][0];
@@ -246,6 +278,28 @@ int run_down(const hexmoe_layer* layer, const void* act, bool bf16, int64_t toke
   q.out = y; q.ld_out = d.hidden;
   q.topk_w = topk_weights;
   q.dev_err = dev_err;
+  if (bm == kDecBlock) {
+    DecParams r{};
+    for (int t = 0; t < d.num_tiers; ++t) {
+      r.idx_t[t][0] = layer->idx_t[t][2];
+      r.bs[t][0] = q.bs[t][0];
+      r.tab[t][0] = layer->tab[t][2][bf16 ? 0 : 1];
+      r.bits[t] = q.bits[t];
+    }
+    r.num_tiers = d.num_tiers; r.expert_map = d.expert_map; r.num_experts = d.num_experts;
+    r.sorted_ids = sid; r.expert_ids = eid; r.npp = npp; r.num_slots = static_cast<int32_t>(S);
+    r.rows_pad = d.hidden_pad; r.rows_store = d.hidden; r.k_pad = d.inter_pad;
+    r.block = d.block; r.m_tiles = d.hidden_pad / kTileM; r.ksteps = d.inter_pad / kKStep;
+    r.out = y; r.ld_out = d.hidden; r.topk_w = topk_weights; r.dev_err = dev_err;
+    if (!plan_decode(r, 1)) return fail(HEXMOE_E_UNSUPPORTED, "inter %d does not fit the small-batch kernel", d.inter_pad);
+    if (int rc = make_tmap(&r.tm_b, act, dt16, 2, d.inter_pad, static_cast<uint64_t>(max_blocks) * bm,
+                           2ull * d.inter_pad, 64, kDecBlock, CU_TENSOR_MAP_SWIZZLE_128B, "act tensor map"))
+      return rc;
+    const int grid = static_cast<int>(std::min<int64_t>(layer->num_sms, max_blocks * r.m_tiles));
+    cudaError_t e = launch_decode_gemm(r, false, bf16, grid, st, pdl);
+    if (e != cudaSuccess) return cuda_fail(e, "down (small batch) launch");
+    return HEXMOE_OK;
+  }
   if (int rc = plan_gemm(q, false, bm, d.inter_pad, d.block)) return rc;
   for (int t = 0; t < d.num_tiers; ++t) q.idx_t[t][0] = layer->idx_t[t][2];
   if (int rc = make_tmap(&q.tm_b, act, dt16, 2, d.inter_pad, static_cast<uint64_t>(max_blocks) * bm,
@@ -261,7 +315,7 @@ int check_phase(const hexmoe_layer* layer, int32_t dt, int64_t tokens, int32_t t
   if (!layer) return fail(HEXMOE_E_ARG, "null layer");
   if (dt != HEXMOE_BF16 && dt != HEXMOE_F16) return fail(HEXMOE_E_DTYPE, "phase dtype must be BF16 or F16");
   if (tokens < 0 || topk <= 0 || topk > layer->desc.num_experts) return fail(HEXMOE_E_ARG, "tokens / topk");
-  if (bm != 16 && bm != 32 && bm != 64 && bm != 128) return fail(HEXMOE_E_ARG, "block_m %d not in {16, 32, 64, 128}", bm);
+  if (!valid_block_m(bm)) return fail(HEXMOE_E_ARG, "block_m %d not in {8, 16, 32, 64, 128}", bm);
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev != layer->device) return fail(HEXMOE_E_ARG, "layer was created on device %d, current device is %d", layer->device, dev);
@@ -368,12 +422,32 @@ int hexmoe_layer_create(const hexmoe_layer_desc* desc, hexmoe_layer** out) {
       e = launch_tile_index(parts[j]->idx, tr.bits, tr.n, rows, cols, reinterpret_cast<uint32_t*>(dst), st);
     }
   }
+  // code tables: per tier and projection, n x (256 or 512) x 16 B, for bf16 and f16
+  size_t tab_bytes = 0;
+  size_t tab_off[kMaxTiers][3];
+  for (int t = 0; t < d.num_tiers; ++t)
+    for (int j = 0; j < 3; ++j) {
+      tab_off[t][j] = tab_bytes;
+      tab_bytes += 2 * align_up(static_cast<size_t>(d.tiers[t].n) * (d.tiers[t].bits == 3 ? 256 : 512) * 16, 256);
+    }
+  if (e == cudaSuccess) e = cudaMalloc(&L->tab_mem, tab_bytes);
+  for (int t = 0; t < d.num_tiers && e == cudaSuccess; ++t) {
+    const hexmoe_tier& tr = d.tiers[t];
+    const hexmoe_parts* parts[3] = {&tr.gate, &tr.up, &tr.down};
+    const size_t one = align_up(static_cast<size_t>(tr.n) * (tr.bits == 3 ? 256 : 512) * 16, 256);
+    for (int j = 0; j < 3 && e == cudaSuccess; ++j)
+      for (int k = 0; k < 2 && e == cudaSuccess; ++k) {
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(L->tab_mem) + tab_off[t][j] + k * one);
+        L->tab[t][j][k] = dst;
+        e = launch_code_tables(parts[j]->levels, parts[j]->expert_scale, tr.bits, tr.n, k == 0, dst, st);
+      }
+  }
   const cudaError_t es = cudaStreamSynchronize(st);
   if (e == cudaSuccess) e = es;
   cudaStreamDestroy(st);
   if (e != cudaSuccess) {
     hexmoe_layer_destroy(L);
-    return cuda_fail(e, "hexmoe_layer_create: tiling the index streams");
+    return cuda_fail(e, "hexmoe_layer_create: tiling the index streams / code tables");
   }
   *out = L;
   return HEXMOE_OK;
@@ -381,9 +455,10 @@ int hexmoe_layer_create(const hexmoe_layer_desc* desc, hexmoe_layer** out) {
 
 int hexmoe_layer_destroy(hexmoe_layer* layer) {
   if (!layer) return HEXMOE_OK;
-  if (layer->tiled_mem) {
+  if (layer->tiled_mem || layer->tab_mem) {
     DeviceGuard g(layer->device);
-    cudaFree(layer->tiled_mem);
+    if (layer->tiled_mem) cudaFree(layer->tiled_mem);
+    if (layer->tab_mem) cudaFree(layer->tab_mem);
   }
   delete layer;
   return HEXMOE_OK;
@@ -425,7 +500,7 @@ int forward_impl(const hexmoe_layer* layer, const void* x, int32_t x_dtype, int6
   const int64_t S = tokens * topk;
   if (S >= (1ll << 31) - 1) return fail(HEXMOE_E_ARG, "too many slots");
   const int bm = block_m > 0 ? block_m : auto_block_m(S, d.num_experts);
-  if (bm != 16 && bm != 32 && bm != 64 && bm != 128) return fail(HEXMOE_E_ARG, "block_m %d not in {16, 32, 64, 128}", bm);
+  if (!valid_block_m(bm)) return fail(HEXMOE_E_ARG, "block_m %d not in {8, 16, 32, 64, 128}", bm);
   const WsLayout w = ws_layout(d, tokens, topk, bm, x_dtype);
   if (workspace_bytes < w.total)
     return fail(HEXMOE_E_ARG, "workspace %zu bytes < %zu needed", workspace_bytes, w.total);

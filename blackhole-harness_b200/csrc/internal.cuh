@@ -77,6 +77,40 @@ struct GemmParams {
 // with the top-k weight); returns a cudaError_t.
 cudaError_t launch_gemm(const GemmParams& p, bool glu, bool bf16, int grid, cudaStream_t stream, bool pdl);
 
+// The small-batch grouped GEMM (decode_gemm.cu): align blocks of kDecBlock
+// slots; persistent CTAs over the tiles (block, 128 weight rows), a producer
+// warp streaming 128-input steps through a shared-memory ring, kSbWarps
+// consumer warps of 16 rows each.
+constexpr int kDecBlock = 8;
+constexpr int kSbWarps = 8;      // consumer warps of a small-batch CTA
+constexpr int kDecStages = 8;
+struct DecParams {
+  CUtensorMap tm_b;                     // plan-ordered B rows (x_sorted or act): boxes of 64 inputs x 8 rows, 128-B swizzle
+  const uint8_t* idx_t[kMaxTiers][2];   // tiled index streams (hexmoe_tile_index layout)
+  const uint8_t* bs[kMaxTiers][2];      // block scales [n, rows_pad, k_pad/block]
+  const uint4* tab[kMaxTiers][2];       // code tables [n][256 (3-bit) or 512 (4-bit)] of the operand type
+  int32_t bits[kMaxTiers];
+  int32_t num_tiers;
+  const int32_t* expert_map;
+  int32_t num_experts;
+  const int32_t* sorted_ids;            // align plan with block_m = kDecBlock
+  const int32_t* expert_ids;
+  const int32_t* npp;
+  int32_t num_slots;
+  int32_t rows_pad, rows_store, k_pad, block, m_tiles, ksteps;
+  int32_t ds;                           // ring depth (stages)
+  uint32_t stage_bytes, off_tab, tab_bytes, off_sc, sc_bytes, off_red, smem_bytes;   // shared-memory carve-up
+  void* out;                            // gate/up: act [plan rows, ld_out]; down: y [S, ld_out]
+  int64_t ld_out;
+  const float* topk_w;
+  int32_t* dev_err;
+};
+bool plan_decode(DecParams& p, int nproj);   // the shared-memory carve-up; false when it does not fit
+cudaError_t launch_decode_gemm(const DecParams& p, bool glu, bool bf16, int grid, cudaStream_t st, bool pdl);
+// Code tables of one projection of a tier (kernels.cu): out [n][256 or 512] uint4.
+cudaError_t launch_code_tables(const float* levels, const float* es, int bits, int n, bool bf16, uint4* out,
+                               cudaStream_t st);
+
 // Small kernels (kernels.cu).
 // seg_counts (optional): the ragged slot space of the expert-parallel receive
 // side, segments of seg_len slots of which only the first seg_counts[g] exist.

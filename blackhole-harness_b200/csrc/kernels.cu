@@ -1,6 +1,7 @@
 // kernels.cu — the small kernels around the grouped GEMM: the align plan, the
 // bit-exact dequantization, the top-k combine, the fp32 -> 16-bit cast and
 // the router.
+#include <algorithm>
 #include <atomic>
 #include <mutex>
 
@@ -765,6 +766,48 @@ cudaError_t launch_route_topk(const void* logits, int dtype, int64_t T, int32_t 
   else if (dtype == HEXMOE_BF16)
     route_topk_kernel<HEXMOE_BF16><<<grid, threads, 0, st>>>(logits, T, E, k, renorm, w, ids);
   else route_topk_kernel<HEXMOE_F16><<<grid, threads, 0, st>>>(logits, T, E, k, renorm, w, ids);
+  return cudaGetLastError();
+}
+
+}  // namespace hexmoe
+
+namespace hexmoe {
+
+// ---------------------------------------------------------------------------
+// Code tables of one projection of a tier (layer create): for expert e and fp8
+// scale code c, the expert's level table times fp8(c) * expert_scale[e],
+// rounded to the operand type, as byte planes (decode.cuh Table8 / Table16):
+// out[e * 256 + c] (3-bit) or out[e * 512 + c] and out[e * 512 + 256 + c]
+// (4-bit: entries 0-7 / 8-15 low planes, then high planes).  The same values
+// the grouped GEMM builds per tile: T[l] = rne16(levels[l] * (fp8(c) * es)).
+template <bool BF16>
+__global__ void code_table_kernel(const float* __restrict__ levels, const float* __restrict__ es, int bits, int n,
+                                  uint4* __restrict__ out) {
+  const int L = 1 << bits;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n * 256; i += gridDim.x * blockDim.x) {
+    const int e = i >> 8, c = i & 255;
+    const float s = __fmul_rn(fp8_hex_value(static_cast<uint32_t>(c)), __ldg(es + e));
+    const float* lev = levels + static_cast<int64_t>(e) * L;
+    float lv[16];
+    for (int l = 0; l < L; ++l) lv[l] = __ldg(lev + l);
+    if (bits == 3) {
+      const Table8 t = make_table8<BF16>(lv, s);
+      out[static_cast<int64_t>(e) * 256 + c] = make_uint4(t.l0, t.l1, t.h0, t.h1);
+    } else {
+      const Table16 t = make_table16<BF16>(lv, s);
+      out[static_cast<int64_t>(e) * 512 + c] = make_uint4(t.la0, t.la1, t.lb0, t.lb1);
+      out[static_cast<int64_t>(e) * 512 + 256 + c] = make_uint4(t.ha0, t.ha1, t.hb0, t.hb1);
+    }
+  }
+}
+
+cudaError_t launch_code_tables(const float* levels, const float* es, int bits, int n, bool bf16, uint4* out,
+                               cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  const int threads = 256;
+  const int grid = std::min(n, 148 * 4);
+  if (bf16) code_table_kernel<true><<<grid, threads, 0, st>>>(levels, es, bits, n, out);
+  else code_table_kernel<false><<<grid, threads, 0, st>>>(levels, es, bits, n, out);
   return cudaGetLastError();
 }
 

@@ -137,8 +137,11 @@ HEXMOE_API int hexmoe_tile_index(const uint32_t* idx, int32_t bits, int32_t n, i
                                  int32_t cols_pad, uint32_t* out, void* stream);
 
 /* Scratch bytes hexmoe_forward needs for `tokens` tokens at top-`topk` with
- * tile height `block_m` (16, 32, 64 or 128; 0 = automatic, as
- * default_config hex_moe.py:264-283 picks it) and activation dtype x_dtype. */
+ * tile height `block_m` and activation dtype x_dtype.  block_m 16, 32, 64 or
+ * 128: the tcgen05 grouped GEMM with tiles of that many slots of one expert;
+ * 8: the small-batch (decode) kernels, mma.sync over weights decoded in
+ * registers, one CTA per 8 slots of one expert and 16 weight rows; 0 =
+ * automatic, as default_config hex_moe.py:264-283 picks it. */
 HEXMOE_API size_t hexmoe_forward_workspace_bytes(const hexmoe_layer* layer, int64_t tokens, int32_t topk,
                                       int32_t block_m, int32_t x_dtype);
 

@@ -215,3 +215,78 @@ def test_reference_combine_single_rank_is_the_layer_combine():
     for j in range(1, k):
         acc = acc + want[:, j]
     assert torch.equal(reference_combine(y, ids, ExpertShard(12, 0, 1), torch.bfloat16), acc.to(torch.bfloat16))
+
+
+def _leaving_worker(rank: int, world: int, port: int, out_q):
+    """Rank 1 takes part in one forward and then leaves (exits between steps);
+    rank 0's next forward must fail with an error, not hang."""
+    import time
+    from datetime import timedelta
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=10))
+    from blackhole_b200.ep import EPMoE, ExpertShard
+    ep = EPMoE(ExpertShard(E, rank, world), expert_fn=lambda xr, wr, ir: xr)
+    x, w, ids = _tokens(rank, 6)
+    ep(x, w, ids)
+    if rank == 1:
+        out_q.put((rank, "left"))
+        out_q.close()
+        out_q.join_thread()             # the message is out; then no goodbye: the process is simply gone
+        os._exit(0)
+    t0 = time.monotonic()
+    try:
+        ep(x, w, ids)
+        out_q.put((rank, "no error"))
+    except Exception as e:  # noqa: BLE001  (gloo raises RuntimeError subclasses)
+        out_q.put((rank, f"raised after {time.monotonic() - t0:.1f}s: {type(e).__name__}"))
+    out_q.close()
+    out_q.join_thread()
+    os._exit(0)
+
+
+def test_rank_that_leaves_fails_the_others_within_the_timeout():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_leaving_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in range(2))
+    for p in procs:
+        p.join(timeout=30)
+    assert res[1] == "left"
+    assert res[0].startswith("raised after"), res[0]
+    assert float(res[0].split()[2].rstrip("s:")) < 60
+
+
+def _mismatch_worker(rank: int, world: int, port: int, out_q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from blackhole_b200.ep import EPMoE, ExpertShard
+        ep = EPMoE(ExpertShard(E, rank, world), expert_fn=lambda xr, wr, ir: xr)
+        x, w, ids = _tokens(rank, 5)
+        if rank == 1:
+            x = x[:, : H // 2].contiguous()          # this rank's rows are narrower than everyone else's
+        try:
+            ep(x, w, ids)
+            out_q.put((rank, "no error"))
+        except ValueError as e:
+            out_q.put((rank, str(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ranks_that_disagree_on_shapes_raise_on_every_rank():
+    """A rank whose rows have another width fails the call on every rank, in the
+    count exchange, before any row moves."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_mismatch_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+    assert all(v.startswith("ranks disagree on hidden / topk") for v in res.values()), res

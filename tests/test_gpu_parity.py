@@ -202,7 +202,7 @@ def test_layer_matches_reference_golden_bf16(T):
     for path in ("auto", "fused", "dequant"):
         got = hex_moe(x, w, ids, tiers, path=path).float().cpu().numpy()
         assert within(got, z["out_bf16"]), (path, rel_err(got, z["out_bf16"]))
-    for bm in (16, 32, 64, 128):
+    for bm in (8, 16, 32, 64, 128):
         got = hex_moe(x, w, ids, tiers, {"BLOCK_M": bm}).float().cpu().numpy()
         assert within(got, z["out_bf16"]), (bm, rel_err(got, z["out_bf16"]))
     # fp32 activations: computed in bf16 inside, returned in fp32
@@ -223,17 +223,19 @@ def test_layer_cfg1_tiny_config(oracle):
     assert within(got, z["out_bf16"]), rel_err(got, z["out_bf16"])
 
 
+@pytest.mark.parametrize("bm", [0, 8, 16])
 @pytest.mark.parametrize("T", [1, 8, 32, 64])
-def test_layer_decode_cfg2_shape(oracle, T):
+def test_layer_decode_cfg2_shape(oracle, T, bm):
     c = hd.CONFIGS["cfg2"]
     L = hd.synth_layer(c["E"], c["H"], c["I"], "3", c["block"], seed=7)
     w, ids = hd.synth_routing(T, c["E"], c["k"], seed=T)
     x = hd.synth_x(T, c["H"], seed=100 + T)
-    got, want = _run_layer(oracle, L, w, ids, x)
+    got, want = _run_layer(oracle, L, w, ids, x, block_m=bm or None)
     assert within(got, want), rel_err(got, want)
 
 
-@pytest.mark.parametrize("bits,block,bm", [("mixed", 128, 0), ("mixed", 32, 64), ("4", 32, 128), ("3", 128, 32)])
+@pytest.mark.parametrize("bits,block,bm", [("mixed", 128, 0), ("mixed", 32, 64), ("4", 32, 128), ("3", 128, 32),
+                                           ("mixed", 32, 8), ("4", 128, 8)])
 def test_layer_prefill_mixed_tiers(oracle, bits, block, bm):
     E, H, I, k, T = 24, 512, 384, 4, 700
     L = hd.synth_layer(E, H, I, bits, block, seed=31)
@@ -276,12 +278,13 @@ def test_layer_cfg4_one_gpu_slice(oracle):
     assert within(got, want), rel_err(got, want)
 
 
-def test_layer_fp16_activations(oracle):
+@pytest.mark.parametrize("bm", [0, 8])
+def test_layer_fp16_activations(oracle, bm):
     E, H, I, k, T = 16, 256, 256, 4, 50
     L = hd.synth_layer(E, H, I, "mixed", 32, seed=41)
     w, ids = hd.synth_routing(T, E, k, seed=42)
     x = hd.synth_x(T, H, seed=43, dtype=torch.float16)
-    got, want = _run_layer(oracle, L, w, ids, x, act="float16")
+    got, want = _run_layer(oracle, L, w, ids, x, block_m=bm or None, act="float16")
     assert within(got, want), rel_err(got, want)
 
 
@@ -298,6 +301,8 @@ def test_layer_skewed_routing_and_empty_experts(oracle):
     w2 = torch.full((300, k), 1.0 / k)
     x2 = hd.synth_x(300, H, seed=54)
     got, want = _run_layer(oracle, L, w2, ids2, x2, block_m=16)
+    assert within(got, want), rel_err(got, want)
+    got, want = _run_layer(oracle, L, w2, ids2, x2, block_m=8)      # many 8-slot blocks per expert
     assert within(got, want), rel_err(got, want)
 
 

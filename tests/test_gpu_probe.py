@@ -15,8 +15,9 @@ activations, so that every output is a single weight times an exact factor:
            (silu's exp differs between the GPU and numpy in the last fp32 bit)
 
 Every (expert, row, input) of every projection is covered, for 3- and 4-bit
-tiers, scale blocks 32 and 128, bf16 and f16 operands, and tile heights 16
-(down with split MMA issue) and 128 (one issuer).  The reference value is the
+tiers, scale blocks 32 and 128, bf16 and f16 operands, and tile heights 8 (the
+small-batch mma.sync kernels and their precomputed code tables), 16 (tcgen05,
+down with split MMA issue) and 128 (tcgen05, one issuer).  The reference value is the
 oracle's fp32 dequantization (blackhole/anatomy/hex.py:180-204) rounded to
 nearest even.
 """
@@ -92,7 +93,7 @@ def _one_hot_batch(ncol: int):
 
 @pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("block", [32, 128])
-@pytest.mark.parametrize("bm", [16, 128])
+@pytest.mark.parametrize("bm", [8, 16, 128])
 def test_down_operands_bitexact(oracle, dt, block, bm):
     L = _tiers(block, seed=70 + block + bm)
     layer = _layer(L)
@@ -113,7 +114,7 @@ def test_down_operands_bitexact(oracle, dt, block, bm):
 
 @pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("block", [32, 128])
-@pytest.mark.parametrize("bm", [16, 128])
+@pytest.mark.parametrize("bm", [8, 16, 128])
 def test_up_operands_bitexact(oracle, dt, block, bm):
     L = _tiers(block, seed=80 + block + bm, gate_const=64.0)
     layer = _layer(L)
@@ -136,8 +137,8 @@ def test_up_operands_bitexact(oracle, dt, block, bm):
 
 @pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("block", [32, 128])
-def test_gate_operands_within_one_ulp(oracle, dt, block):
-    bm = 64
+@pytest.mark.parametrize("bm", [8, 64])
+def test_gate_operands_within_one_ulp(oracle, dt, block, bm):
     L = _tiers(block, seed=90 + block, up_const=1.0)
     layer = _layer(L)
     T, ids, w = _one_hot_batch(H)
