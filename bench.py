@@ -23,9 +23,10 @@ Other objects of the line: `decode` (cfg2: all-3-bit, T = 64 with the decode
 roofline against HBM, and the 1/8/32/64 sweep), `prefill_T16384` (cfg3 at
 16384 tokens on one GPU), `cfg4_slice` (one GPU's share of cfg4 at 8 GPUs: 16
 experts of H=4096, I=1536, 1024 tokens routed over them); at N>1 `ep` (per-phase
-times, per-rank expert time, and a bit-exactness check of rank 0's output), and
-at N=8 `cfg4_ep` and `cfg5_ep` (128 experts 16 per GPU; Zipf-skewed routing at
-32768 tokens).  `cpu_baseline`: the oracle (a C restatement of the reference's
+times, per-rank expert time, and a bit-exactness check of rank 0's output),
+`cfg4_ep` and `cfg5_ep` (cfg4: 128 experts of H=4096, 8192 tokens over the
+GPUs, 16 experts per GPU at N=8; cfg5: Zipf-skewed routing, 32768 tokens over
+the GPUs; each with per-rank expert time).  `cpu_baseline`: the oracle (a C restatement of the reference's
 moe_reference) on the host cores over a bounded sample of the headline.
 `gpu_reference`: the reference's own Triton hex_moe on the same GPU, when a copy
 of it is installed under baseline/_ref.
@@ -629,15 +630,17 @@ def main() -> None:
         extras["ep"] = {"workload": f"cfg3 prefill, {E // world} experts and {T} tokens per GPU", **ph}
         if rank == 0:
             extras["ep"]["check"] = ep_bit_check(L3, (ep, shard, x, w, ids), got)
-        if world == 8 and not args.no_extras:
+        if not args.no_extras:
             L4 = hd.synth_layer(128, 4096, 1536, "mixed", BLOCK, seed=44, device=dev)
             r4, st4 = ep_run(dev, rank, world, L4, 128, 4096, 1536, 8192 // world, args.steps, flush, stream, pk, 61,
-                             label="cfg4: 128 experts H=4096 I=1536 top-8 mixed 3/4-bit, 16 per GPU, 8192 tokens")
+                             label=f"cfg4: 128 experts H=4096 I=1536 top-8 mixed 3/4-bit, {128 // world} per GPU, "
+                                   f"8192 tokens ({8192 // world} per GPU)")
             st4[0].close()
             del L4, st4
             L5 = hd.synth_layer(E, H, I, "3", BLOCK, seed=9, device=dev)
             r5, st5 = ep_run(dev, rank, world, L5, E, H, I, 32768 // world, args.steps, flush, stream, pk, 71,
-                             zipf=1.2, label="cfg5: 96 experts 3-bit, Zipf(1.2) routing skew, 32768 tokens, 12 per GPU")
+                             zipf=1.2, label=f"cfg5: 96 experts 3-bit, Zipf(1.2) routing skew, 32768 tokens "
+                                             f"({32768 // world} per GPU), {E // world} experts per GPU")
             st5[0].close()
             del L5, st5
             extras["cfg4_ep"], extras["cfg5_ep"] = r4, r5

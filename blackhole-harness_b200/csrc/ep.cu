@@ -22,8 +22,9 @@
 //              returns for this rank's tokens, in the order they were sent
 //
 // One forward, all on the caller's stream, no host synchronisation:
-//   plan      (1 CTA) epoch += 1; per token and destination rank, the row
-//             position and the first slot offset (stable scans over tokens)
+//   plan      (a CTA per 256 tokens) per token and destination rank, the row
+//             position and the first slot offset (stable scans over tokens);
+//             the last CTA adds up the CTAs' totals and advances the epoch
 //   send      (all SMs) each token row read once and stored to every rank that
 //             owns one of its experts, with its slot records; the last CTA
 //             writes the counts and raises disp[me] = epoch on every rank
@@ -66,10 +67,12 @@ struct EpArgs {
   uint64_t o_disp, o_ret_flag, o_rows, o_slots, o_x, o_row, o_exp, o_w, o_rowslot, o_ret;
   // this rank's private state
   int64_t* epoch;
-  uint32_t* done;               // [2]: CTAs finished in send / return
+  uint32_t* done;               // [3]: CTAs finished in send / return / plan
   int32_t* tot;                 // [world][2]: rows and slots sent to every rank
-  int32_t* pos;                 // [cap][world]: row position of token t at rank d, -1 = none
-  int32_t* soff;                // [cap][world]: first slot offset of token t at rank d
+  int32_t* pos;                 // [cap][world]: token t's row position at rank d within its plan CTA, -1 = none
+  int32_t* soff;                // [cap][world]: first slot offset of token t at rank d within its plan CTA
+  int64_t* plan_tot;            // [plan CTAs][kEpMaxWorld]: each plan CTA's totals (rows << 32 | slots)
+  int64_t* plan_off;            // [plan CTAs][kEpMaxWorld]: their exclusive offsets over CTAs
   int32_t* dev_err;
 };
 
@@ -88,53 +91,51 @@ __device__ __forceinline__ T* at(uint8_t* base, uint64_t off) {
 }
 
 // ---------------------------------------------------------------- plan
-// Counts of token t per destination, packed rows << 32 | slots.
+// One thread per token, kPlanThreads tokens per CTA, many CTAs.  Per token and
+// destination rank d: c = (1 << 32 | slots) when the token has slots at d, else
+// 0.  Each CTA scans c over its tokens (exclusive, per d) into the token's
+// local row position and first slot offset, and stores its totals; the last
+// CTA to finish turns the totals into per-CTA offsets (exclusive over CTAs, so
+// token order is kept), the per-rank totals, and advances the epoch.  The send
+// kernel adds the CTA offset to the local position.
+constexpr int kPlanThreads = 256;
+
 template <bool I64>
-__device__ __forceinline__ void token_counts(const EpArgs& a, const void* ids, int64_t t, int64_t (&c)[kEpMaxWorld],
-                                             bool report) {
+__device__ __forceinline__ void token_counts(const EpArgs& a, const void* ids, int64_t t, int64_t (&c)[kEpMaxWorld]) {
+  int32_t n[kEpMaxWorld];
 #pragma unroll
-  for (int d = 0; d < kEpMaxWorld; ++d) c[d] = 0;
+  for (int d = 0; d < kEpMaxWorld; ++d) n[d] = 0;
   for (int j = 0; j < a.topk; ++j) {
-    const int64_t e = I64 ? static_cast<const int64_t*>(ids)[t * a.topk + j]
-                          : static_cast<const int32_t*>(ids)[t * a.topk + j];
+    const int64_t e = I64 ? __ldg(static_cast<const int64_t*>(ids) + t * a.topk + j)
+                          : static_cast<int64_t>(__ldg(static_cast<const int32_t*>(ids) + t * a.topk + j));
     if (e < 0 || e >= a.E) {
-      if (report) atomicOr(a.dev_err, kDevErrExpertId);
+      atomicOr(a.dev_err, kDevErrExpertId);
       continue;
     }
     const int d = static_cast<int>(e / a.P);
 #pragma unroll
-    for (int q = 0; q < kEpMaxWorld; ++q)
-      if (q == d) c[q] += 1;
+    for (int q = 0; q < kEpMaxWorld; ++q) n[q] += q == d ? 1 : 0;
   }
 #pragma unroll
-  for (int d = 0; d < kEpMaxWorld; ++d)
-    if (c[d]) c[d] += 1ll << 32;
+  for (int d = 0; d < kEpMaxWorld; ++d) c[d] = n[d] ? (1ll << 32) + n[d] : 0;
 }
 
-constexpr int kPlanThreads = 1024;
-
 template <bool I64>
-__global__ void __launch_bounds__(kPlanThreads, 1) ep_plan_kernel(EpArgs a, const void* __restrict__ ids, int64_t T) {
-  __shared__ int64_t wtot[32][kEpMaxWorld];
-  __shared__ int64_t wbase[32][kEpMaxWorld];
+__global__ void __launch_bounds__(kPlanThreads) ep_plan_kernel(EpArgs a, const void* __restrict__ ids, int64_t T) {
+  __shared__ int64_t wtot[kPlanThreads / 32][kEpMaxWorld];
+  __shared__ bool last;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  if (tid == 0) *a.epoch = *a.epoch + 1;
-  const int64_t per = (T + kPlanThreads - 1) / kPlanThreads;
-  const int64_t t0 = min(static_cast<int64_t>(tid) * per, T), t1 = min(t0 + per, T);
-  int64_t run[kEpMaxWorld];
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * kPlanThreads + tid;
+  int64_t c[kEpMaxWorld];
+  if (t < T) token_counts<I64>(a, ids, t, c);
+  else {
 #pragma unroll
-  for (int d = 0; d < kEpMaxWorld; ++d) run[d] = 0;
-  for (int64_t t = t0; t < t1; ++t) {
-    int64_t c[kEpMaxWorld];
-    token_counts<I64>(a, ids, t, c, true);
-#pragma unroll
-    for (int d = 0; d < kEpMaxWorld; ++d) run[d] += c[d];
+    for (int d = 0; d < kEpMaxWorld; ++d) c[d] = 0;
   }
-  // exclusive scan over threads (token ranges are in thread order)
   int64_t incl[kEpMaxWorld];
 #pragma unroll
   for (int d = 0; d < kEpMaxWorld; ++d) {
-    int64_t v = run[d];
+    int64_t v = c[d];
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const int64_t u = __shfl_up_sync(0xffffffffu, v, o);
@@ -144,37 +145,45 @@ __global__ void __launch_bounds__(kPlanThreads, 1) ep_plan_kernel(EpArgs a, cons
     if (lane == 31) wtot[warp][d] = v;
   }
   __syncthreads();
-  if (warp == 0) {
+  int64_t* cta_tot = a.plan_tot + static_cast<int64_t>(blockIdx.x) * kEpMaxWorld;
 #pragma unroll
-    for (int d = 0; d < kEpMaxWorld; ++d) {
-      const int64_t own = wtot[lane][d];
-      int64_t v = own;
+  for (int d = 0; d < kEpMaxWorld; ++d) {
+    int64_t before = 0, all = 0;
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int64_t u = __shfl_up_sync(0xffffffffu, v, o);
-        if (lane >= o) v += u;
-      }
-      wbase[lane][d] = v - own;
-      if (lane == 31 && d < a.world) {
-        a.tot[2 * d] = static_cast<int32_t>(v >> 32);
-        a.tot[2 * d + 1] = static_cast<int32_t>(v & 0xffffffffll);
-      }
+    for (int w = 0; w < kPlanThreads / 32; ++w) {
+      const int64_t v = wtot[w][d];
+      before += w < warp ? v : 0;
+      all += v;
+    }
+    const int64_t ex = before + incl[d] - c[d];
+    if (t < T && d < a.world) {
+      a.pos[t * a.world + d] = c[d] ? static_cast<int32_t>(ex >> 32) : -1;
+      a.soff[t * a.world + d] = static_cast<int32_t>(ex & 0xffffffffll);
+    }
+    if (tid == 0) cta_tot[d] = all;
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) last = atomicAdd(a.done + 2, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  if (tid < kEpMaxWorld) {
+    // exclusive offsets over the CTAs for destination d = tid
+    int64_t run = 0;
+    for (unsigned g = 0; g < gridDim.x; ++g) {
+      const int64_t v = *reinterpret_cast<volatile int64_t*>(a.plan_tot + static_cast<int64_t>(g) * kEpMaxWorld + tid);
+      a.plan_off[static_cast<int64_t>(g) * kEpMaxWorld + tid] = run;
+      run += v;
+    }
+    if (tid < a.world) {
+      a.tot[2 * tid] = static_cast<int32_t>(run >> 32);
+      a.tot[2 * tid + 1] = static_cast<int32_t>(run & 0xffffffffll);
     }
   }
-  __syncthreads();
-  int64_t base[kEpMaxWorld];
-#pragma unroll
-  for (int d = 0; d < kEpMaxWorld; ++d) base[d] = wbase[warp][d] + incl[d] - run[d];
-  for (int64_t t = t0; t < t1; ++t) {
-    int64_t c[kEpMaxWorld];
-    token_counts<I64>(a, ids, t, c, false);
-#pragma unroll
-    for (int d = 0; d < kEpMaxWorld; ++d) {
-      if (d >= a.world) break;
-      a.pos[t * a.world + d] = c[d] ? static_cast<int32_t>(base[d] >> 32) : -1;
-      a.soff[t * a.world + d] = static_cast<int32_t>(base[d] & 0xffffffffll);
-      base[d] += c[d];
-    }
+  if (tid == 0) {
+    *a.epoch = *a.epoch + 1;
+    a.done[2] = 0;
   }
 }
 
@@ -193,10 +202,13 @@ __global__ void __launch_bounds__(kSendThreads) ep_send_kernel(EpArgs a, const X
   const int hv = a.H / 8;                         // 16-byte vectors of 8 16-bit values per row
   for (int64_t t = (blockIdx.x * static_cast<int64_t>(kSendThreads) + threadIdx.x) >> 5; t < T; t += nwarps) {
     int32_t pos[kEpMaxWorld], so[kEpMaxWorld];
+    const int64_t* off = a.plan_off + (t / kPlanThreads) * kEpMaxWorld;
 #pragma unroll
     for (int d = 0; d < kEpMaxWorld; ++d) {
+      const int64_t o = d < a.world ? __ldg(off + d) : 0;
       pos[d] = d < a.world ? __ldg(a.pos + t * a.world + d) : -1;
-      so[d] = d < a.world ? __ldg(a.soff + t * a.world + d) : 0;
+      so[d] = d < a.world ? __ldg(a.soff + t * a.world + d) + static_cast<int32_t>(o & 0xffffffffll) : 0;
+      if (pos[d] >= 0) pos[d] += static_cast<int32_t>(o >> 32);
     }
     for (int c0 = 0; c0 < hv; c0 += 8 * 32) {
       uint4 v[8];
@@ -373,9 +385,11 @@ __global__ void ep_combine_kernel(EpArgs a, int64_t T, void* __restrict__ out) {
     const int64_t t = i / hv;
     const int c = static_cast<int>(i % hv);
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    const int64_t* off = a.plan_off + (t / kPlanThreads) * kEpMaxWorld;
     for (int d = 0; d < a.world; ++d) {
-      const int32_t p = __ldg(a.pos + t * a.world + d);
+      int32_t p = __ldg(a.pos + t * a.world + d);
       if (p < 0) continue;
+      p += static_cast<int32_t>(__ldg(off + d) >> 32);
       const uint4 v = *(reinterpret_cast<const uint4*>(ret + (static_cast<int64_t>(d) * a.cap + p) * a.H) + c);
       const YT* e = reinterpret_cast<const YT*>(&v);
 #pragma unroll
@@ -413,6 +427,7 @@ struct hexmoe_ep {
   int64_t* epoch;
   uint32_t* done;
   int32_t *tot, *pos, *soff;
+  int64_t *plan_tot, *plan_off;
   int64_t last_tokens;
 };
 
@@ -430,6 +445,7 @@ EpArgs ep_args(const hexmoe_ep* ep, int32_t* dev_err) {
   a.o_x = ep->o_x; a.o_row = ep->o_row; a.o_exp = ep->o_exp; a.o_w = ep->o_w; a.o_rowslot = ep->o_rowslot;
   a.o_ret = ep->o_ret;
   a.epoch = ep->epoch; a.done = ep->done; a.tot = ep->tot; a.pos = ep->pos; a.soff = ep->soff;
+  a.plan_tot = ep->plan_tot; a.plan_off = ep->plan_off;
   a.dev_err = dev_err;
   return a;
 }
@@ -443,12 +459,15 @@ int ep_check(const hexmoe_ep* ep, const char* what) {
   return HEXMOE_OK;
 }
 
+// Grid of the send / return kernels: at most two CTAs per SM, warps looping
+// over their tokens / rows (each CTA ends with one system-scope fence, so fewer,
+// longer-lived CTAs fence less).
 int grid_for(int64_t work_warps, int per_cta_warps) {
   int sms = 148;
   int dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t want = (work_warps + per_cta_warps - 1) / per_cta_warps;
-  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, static_cast<int64_t>(sms) * 8)));
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, static_cast<int64_t>(sms) * 2)));
 }
 
 }  // namespace
@@ -488,7 +507,9 @@ int hexmoe_ep_init(int32_t rank, int32_t world, int32_t num_experts, int32_t hid
   ep->region_bytes = off;
   cudaError_t e = cudaMalloc(&ep->region, ep->region_bytes);
   if (e != cudaSuccess) { delete ep; return report_cuda_error(e, "hexmoe_ep_init: region allocation"); }
-  const size_t local_bytes = up256(8 + 8) + up256(W * 2 * 4) + 2 * up256(ep->cap * W * 4);
+  const size_t plan_ctas = static_cast<size_t>((ep->cap + kPlanThreads - 1) / kPlanThreads);
+  const size_t local_bytes =
+      up256(8 + 16) + up256(W * 2 * 4) + 2 * up256(ep->cap * W * 4) + 2 * up256(plan_ctas * kEpMaxWorld * 8);
   e = cudaMalloc(&ep->local, local_bytes);
   if (e == cudaSuccess) e = cudaMemset(ep->region, 0, header);
   if (e == cudaSuccess) e = cudaMemset(ep->local, 0, local_bytes);
@@ -499,11 +520,15 @@ int hexmoe_ep_init(int32_t rank, int32_t world, int32_t num_experts, int32_t hid
     delete ep;
     return report_cuda_error(e, "hexmoe_ep_init: local state");
   }
+  size_t lo = 0;
   ep->epoch = reinterpret_cast<int64_t*>(ep->local);
   ep->done = reinterpret_cast<uint32_t*>(ep->local + 8);
-  ep->tot = reinterpret_cast<int32_t*>(ep->local + up256(16));
-  ep->pos = reinterpret_cast<int32_t*>(ep->local + up256(16) + up256(W * 8));
-  ep->soff = reinterpret_cast<int32_t*>(ep->local + up256(16) + up256(W * 8) + up256(ep->cap * W * 4));
+  lo = up256(8 + 16);
+  ep->tot = reinterpret_cast<int32_t*>(ep->local + lo); lo += up256(W * 2 * 4);
+  ep->pos = reinterpret_cast<int32_t*>(ep->local + lo); lo += up256(ep->cap * W * 4);
+  ep->soff = reinterpret_cast<int32_t*>(ep->local + lo); lo += up256(ep->cap * W * 4);
+  ep->plan_tot = reinterpret_cast<int64_t*>(ep->local + lo); lo += up256(plan_ctas * kEpMaxWorld * 8);
+  ep->plan_off = reinterpret_cast<int64_t*>(ep->local + lo);
   for (int d = 0; d < kEpMaxWorld; ++d) { ep->peer[d] = nullptr; ep->opened[d] = false; }
   ep->peer[rank] = ep->region;
   ep->connected = world == 1;
@@ -559,8 +584,9 @@ int hexmoe_ep_dispatch(hexmoe_ep* ep, const void* x, int32_t x_dtype, int64_t to
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const EpArgs a = ep_args(ep, dev_err);
   const bool i64 = ids_dtype == HEXMOE_I64;
-  if (i64) ep_plan_kernel<true><<<1, kPlanThreads, 0, st>>>(a, topk_ids, tokens);
-  else ep_plan_kernel<false><<<1, kPlanThreads, 0, st>>>(a, topk_ids, tokens);
+  const unsigned plan_grid = static_cast<unsigned>(std::max<int64_t>(1, (tokens + kPlanThreads - 1) / kPlanThreads));
+  if (i64) ep_plan_kernel<true><<<plan_grid, kPlanThreads, 0, st>>>(a, topk_ids, tokens);
+  else ep_plan_kernel<false><<<plan_grid, kPlanThreads, 0, st>>>(a, topk_ids, tokens);
   const int grid = grid_for(tokens, kSendThreads / 32);
   if (x_dtype == HEXMOE_F32) {
     if (i64) ep_send_kernel<float, true><<<grid, kSendThreads, 0, st>>>(a, static_cast<const float*>(x), topk_ids, topk_weights, tokens);
@@ -603,7 +629,7 @@ int hexmoe_ep_experts(hexmoe_ep* ep, const hexmoe_layer* local, int32_t block_m,
   }
   // without local experts nothing can have been routed here: rows = 0 from every source
   const int64_t rows_max = static_cast<int64_t>(ep->world) * ep->cap;
-  const int grid = grid_for(local ? rows_max / 4 : 1, kSendThreads / 32);
+  const int grid = grid_for(local ? rows_max : 1, kSendThreads / 32);
   if (ep->row_dtype == HEXMOE_BF16)
     ep_return_kernel<__nv_bfloat16><<<grid, kSendThreads, 0, st>>>(a, static_cast<const __nv_bfloat16*>(y));
   else
