@@ -530,7 +530,8 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=("b200", "reference"))
     ap.add_argument("--no-extras", action="store_true", help="headline, e2e and roofline only")
-    ap.add_argument("--profile", action="store_true", help="a few eager headline steps only (for ncu)")
+    ap.add_argument("--profile", nargs="?", const="prefill", choices=("prefill", "decode"),
+                    help="a few eager steps only (for ncu): the headline prefill layer, or the cfg2 T=64 decode layer")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -558,6 +559,17 @@ def main() -> None:
 
     def flush():
         flush_buf.fill_(rank & 0xFF)
+
+    if args.profile == "decode":
+        from blackhole_b200.hex_moe import auto_block_m
+        Ld = hd.synth_layer(E, H, I, "3", BLOCK, seed=0, device=dev)
+        lay_d = layer_for(build_tiers(Ld.tiers, E))
+        wd, idd = hd.synth_routing(64, E, K_TOP, seed=1, device=dev)
+        xd = hd.synth_x(64, H, seed=2, device=dev)
+        for _ in range(args.warmup):
+            lay_d.forward(xd, wd, idd, auto_block_m(64 * K_TOP, E))
+        torch.cuda.synchronize()
+        return
 
     # ---- the headline step: cfg3 prefill, 4096 tokens per GPU
     T = T_PREFILL

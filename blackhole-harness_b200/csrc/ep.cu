@@ -334,14 +334,25 @@ __global__ void __launch_bounds__(kSendThreads) ep_return_kernel(EpArgs a, const
       for (int i = 0; i < 4; ++i)
 #pragma unroll
         for (int q = 0; q < 8; ++q) acc[i][q] = 0.f;
-      for (int s = s0; s < s1; ++s) {
-        const uint4* row = reinterpret_cast<const uint4*>(ybase + static_cast<int64_t>(s) * a.H);
+      // slots four at a time: their loads are all in flight before the first add
+      // (the adds themselves stay in slot order)
+      for (int s = s0; s < s1; s += 4) {
+        uint4 v[4][4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int c = c0 + i * 32 + lane;
-          if (c < hv) {
-            const uint4 v = __ldg(row + c);
-            const YT* e = reinterpret_cast<const YT*>(&v);
+        for (int u = 0; u < 4; ++u) {
+          const uint4* row = reinterpret_cast<const uint4*>(ybase + static_cast<int64_t>(s + u) * a.H);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int c = c0 + i * 32 + lane;
+            v[u][i] = (s + u < s1 && c < hv) ? __ldg(row + c) : make_uint4(0, 0, 0, 0);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (s + u >= s1) break;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const YT* e = reinterpret_cast<const YT*>(&v[u][i]);
 #pragma unroll
             for (int q = 0; q < 8; ++q) acc[i][q] += static_cast<float>(e[q]);
           }
@@ -459,15 +470,15 @@ int ep_check(const hexmoe_ep* ep, const char* what) {
   return HEXMOE_OK;
 }
 
-// Grid of the send / return kernels: at most two CTAs per SM, warps looping
-// over their tokens / rows (each CTA ends with one system-scope fence, so fewer,
+// Grid of the send / return kernels: a few CTAs per SM, warps looping over
+// their tokens / rows (each CTA ends with one system-scope fence, so fewer,
 // longer-lived CTAs fence less).
-int grid_for(int64_t work_warps, int per_cta_warps) {
+int grid_for(int64_t work_warps, int per_cta_warps, int ctas_per_sm = 2) {
   int sms = 148;
   int dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t want = (work_warps + per_cta_warps - 1) / per_cta_warps;
-  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, static_cast<int64_t>(sms) * 2)));
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, static_cast<int64_t>(sms) * ctas_per_sm)));
 }
 
 }  // namespace
@@ -629,7 +640,7 @@ int hexmoe_ep_experts(hexmoe_ep* ep, const hexmoe_layer* local, int32_t block_m,
   }
   // without local experts nothing can have been routed here: rows = 0 from every source
   const int64_t rows_max = static_cast<int64_t>(ep->world) * ep->cap;
-  const int grid = grid_for(local ? rows_max : 1, kSendThreads / 32);
+  const int grid = grid_for(local ? rows_max : 1, kSendThreads / 32, 4);
   if (ep->row_dtype == HEXMOE_BF16)
     ep_return_kernel<__nv_bfloat16><<<grid, kSendThreads, 0, st>>>(a, static_cast<const __nv_bfloat16*>(y));
   else
