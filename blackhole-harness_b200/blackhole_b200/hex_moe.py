@@ -314,12 +314,13 @@ def combine_rows(y: torch.Tensor, T: int, k: int, rows: torch.Tensor, out_dtype=
     return out
 
 
-def auto_block_m(slots: int, num_experts: int) -> int:
+def auto_block_m(slots: int, num_experts: int, hidden: int = 0) -> int:
     """The block_m hexmoe_forward picks when given 0 (api.cu auto_block_m): the
-    small-batch kernels (8) while an expert averages at most 8 slots, else the
-    smallest of 16/32/64/128 covering the mean slots per expert."""
+    small-batch kernels (8) while an expert averages at most 8 slots (and the
+    hidden size is a multiple of 64), else the smallest of 16/32/64/128 covering
+    the mean slots per expert."""
     avg = -(-slots // max(num_experts, 1))
-    for bm in (8, 16, 32, 64):
+    for bm in ((8, 16, 32, 64) if hidden % 64 == 0 else (16, 32, 64)):
         if avg <= bm:
             return bm
     return 128

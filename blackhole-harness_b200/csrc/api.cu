@@ -77,13 +77,37 @@ int make_tmap(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int elem
   return HEXMOE_OK;
 }
 
+// The small-batch kernels' view of a row-major 16-bit [rows, cols] matrix:
+// 3-D (64 columns, rows, cols / 64 column chunks), box {64, box_rows, 2}, 128-B
+// swizzle, so one load brings 128 consecutive inputs of box_rows rows as two
+// 64-input halves of box_rows x 128 B each (the layout two 2-D boxes of 64
+// columns would give).
+int make_tmap_chunks(CUtensorMap* m, const void* base, CUtensorMapDataType dt, uint64_t cols, uint64_t rows,
+                     uint64_t pitch_bytes, uint32_t box_rows, const char* what) {
+  auto fn = encode_fn();
+  if (!fn) return fail(HEXMOE_E_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  if (reinterpret_cast<uintptr_t>(base) % 16) return fail(HEXMOE_E_ARG, "%s: base address not 16-byte aligned", what);
+  if (pitch_bytes % 16 || cols % 64) return fail(HEXMOE_E_UNSUPPORTED, "%s: row pitch %llu / columns %llu (block_m 8 needs a multiple of 64)", what,
+                                                   static_cast<unsigned long long>(pitch_bytes),
+                                                   static_cast<unsigned long long>(cols));
+  cuuint64_t dims[3] = {64, rows, cols / 64};
+  cuuint64_t strides[2] = {pitch_bytes, 128};
+  cuuint32_t box[3] = {64, box_rows, 2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(m, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(HEXMOE_E_CUDA, "%s: cuTensorMapEncodeTiled failed (%d)", what, static_cast<int>(r));
+  return HEXMOE_OK;
+}
+
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 // The tile height hexmoe_forward picks: the small-batch kernels (8) while an
 // expert averages at most 8 slots (decode), then the tcgen05 GEMM's heights.
-int auto_block_m(int64_t S, int32_t E) {
+int auto_block_m(int64_t S, int32_t E, int32_t hidden) {
   const int64_t avg = (S + E - 1) / std::max(E, 1);
-  if (avg <= 8) return kDecBlock;
+  if (avg <= 8 && hidden % 64 == 0) return kDecBlock;   // the small-batch kernels read 64-input column chunks
+  if (avg <= 8) return 16;
   if (avg <= 16) return 16;
   if (avg <= 32) return 32;
   if (avg <= 64) return 64;
@@ -229,11 +253,14 @@ int run_gate_up(const hexmoe_layer* layer, const void* xs, bool bf16, int64_t to
     q.rows_pad = d.inter_pad; q.rows_store = d.inter_pad; q.k_pad = d.hidden_pad;
     q.block = d.block; q.m_tiles = d.inter_pad / kTileM; q.ksteps = d.hidden_pad / kKStep;
     q.out = act; q.ld_out = d.inter_pad; q.topk_w = nullptr; q.dev_err = dev_err;
-    if (!plan_decode(q, 2)) return fail(HEXMOE_E_UNSUPPORTED, "hidden %d does not fit the small-batch kernel", d.hidden_pad);
-    if (int rc = make_tmap(&q.tm_b, xs, dt16, 2, d.hidden, static_cast<uint64_t>(max_blocks) * bm, 2ull * d.hidden, 64,
-                           kDecBlock, CU_TENSOR_MAP_SWIZZLE_128B, "x_sorted tensor map"))
+    // two CTAs per SM once the plan can give every SM more than one tile
+    const int per_sm = max_blocks * q.m_tiles > layer->num_sms && plan_decode(q, 2, 2) ? 2 : 1;
+    if (per_sm == 1 && !plan_decode(q, 2, 1))
+      return fail(HEXMOE_E_UNSUPPORTED, "hidden %d does not fit the small-batch kernel", d.hidden_pad);
+    if (int rc = make_tmap_chunks(&q.tm_b, xs, dt16, d.hidden, static_cast<uint64_t>(max_blocks) * bm, 2ull * d.hidden,
+                                  kDecBlock, "x_sorted tensor map"))
       return rc;
-    const int grid = static_cast<int>(std::min<int64_t>(layer->num_sms, max_blocks * q.m_tiles));
+    const int grid = static_cast<int>(std::min<int64_t>(per_sm * layer->num_sms, max_blocks * q.m_tiles));
     cudaError_t e = launch_decode_gemm(q, true, bf16, grid, st, pdl);
     if (e != cudaSuccess) return cuda_fail(e, "gate/up (small batch) launch");
     return HEXMOE_OK;
@@ -291,11 +318,13 @@ int run_down(const hexmoe_layer* layer, const void* act, bool bf16, int64_t toke
     r.rows_pad = d.hidden_pad; r.rows_store = d.hidden; r.k_pad = d.inter_pad;
     r.block = d.block; r.m_tiles = d.hidden_pad / kTileM; r.ksteps = d.inter_pad / kKStep;
     r.out = y; r.ld_out = d.hidden; r.topk_w = topk_weights; r.dev_err = dev_err;
-    if (!plan_decode(r, 1)) return fail(HEXMOE_E_UNSUPPORTED, "inter %d does not fit the small-batch kernel", d.inter_pad);
-    if (int rc = make_tmap(&r.tm_b, act, dt16, 2, d.inter_pad, static_cast<uint64_t>(max_blocks) * bm,
-                           2ull * d.inter_pad, 64, kDecBlock, CU_TENSOR_MAP_SWIZZLE_128B, "act tensor map"))
+    const int per_sm = max_blocks * r.m_tiles > layer->num_sms && plan_decode(r, 1, 2) ? 2 : 1;
+    if (per_sm == 1 && !plan_decode(r, 1, 1))
+      return fail(HEXMOE_E_UNSUPPORTED, "inter %d does not fit the small-batch kernel", d.inter_pad);
+    if (int rc = make_tmap_chunks(&r.tm_b, act, dt16, d.inter_pad, static_cast<uint64_t>(max_blocks) * bm,
+                                  2ull * d.inter_pad, kDecBlock, "act tensor map"))
       return rc;
-    const int grid = static_cast<int>(std::min<int64_t>(layer->num_sms, max_blocks * r.m_tiles));
+    const int grid = static_cast<int>(std::min<int64_t>(per_sm * layer->num_sms, max_blocks * r.m_tiles));
     cudaError_t e = launch_decode_gemm(r, false, bf16, grid, st, pdl);
     if (e != cudaSuccess) return cuda_fail(e, "down (small batch) launch");
     return HEXMOE_OK;
@@ -467,7 +496,7 @@ int hexmoe_layer_destroy(hexmoe_layer* layer) {
 size_t hexmoe_forward_workspace_bytes(const hexmoe_layer* layer, int64_t tokens, int32_t topk, int32_t block_m,
                                       int32_t x_dtype) {
   if (!layer || tokens < 0 || topk <= 0) return 0;
-  const int bm = block_m > 0 ? block_m : auto_block_m(tokens * topk, layer->desc.num_experts);
+  const int bm = block_m > 0 ? block_m : auto_block_m(tokens * topk, layer->desc.num_experts, layer->desc.hidden);
   return ws_layout(layer->desc, tokens, topk, bm, x_dtype).total;
 }
 
@@ -499,7 +528,7 @@ int forward_impl(const hexmoe_layer* layer, const void* x, int32_t x_dtype, int6
     return fail(HEXMOE_E_ARG, "x / out must be 16-byte and workspace 256-byte aligned");
   const int64_t S = tokens * topk;
   if (S >= (1ll << 31) - 1) return fail(HEXMOE_E_ARG, "too many slots");
-  const int bm = block_m > 0 ? block_m : auto_block_m(S, d.num_experts);
+  const int bm = block_m > 0 ? block_m : auto_block_m(S, d.num_experts, d.hidden);
   if (!valid_block_m(bm)) return fail(HEXMOE_E_ARG, "block_m %d not in {8, 16, 32, 64, 128}", bm);
   const WsLayout w = ws_layout(d, tokens, topk, bm, x_dtype);
   if (workspace_bytes < w.total)
@@ -544,7 +573,7 @@ const hexmoe_layer_desc* hexmoe::layer_desc(const hexmoe_layer* layer) { return 
 
 size_t hexmoe::slots_workspace_bytes(const hexmoe_layer* layer, int64_t num_slots, int32_t block_m) {
   if (!layer || num_slots < 0) return 0;
-  const int bm = block_m > 0 ? block_m : auto_block_m(num_slots, layer->desc.num_experts);
+  const int bm = block_m > 0 ? block_m : auto_block_m(num_slots, layer->desc.num_experts, layer->desc.hidden);
   return ws_layout(layer->desc, num_slots, 1, bm, HEXMOE_BF16).total;
 }
 
@@ -555,7 +584,7 @@ int hexmoe::forward_slot_space(const hexmoe_layer* layer, const void* x, int32_t
   if (!layer) return fail(HEXMOE_E_ARG, "forward_slot_space: null layer");
   if (!y) {
     // the per-slot rows go to the workspace's own y region
-    const int bm = block_m > 0 ? block_m : auto_block_m(num_slots, layer->desc.num_experts);
+    const int bm = block_m > 0 ? block_m : auto_block_m(num_slots, layer->desc.num_experts, layer->desc.hidden);
     const WsLayout w = ws_layout(layer->desc, num_slots, 1, bm, x_dtype);
     if (!workspace || workspace_bytes < w.total) return fail(HEXMOE_E_ARG, "forward_slot_space: workspace too small");
     y = static_cast<char*>(workspace) + w.y;

@@ -10,34 +10,44 @@
 //   down:           y[slot, o]  = (act_row . Wd[e, o]) * topk_weight[slot]
 //
 // Persistent CTAs over the tiles (align block b of <= 8 slots of one expert,
-// 128 weight rows m), 8 x kSbGroups consumer warps + 1 producer warp:
+// 128 weight rows m), kDecRQ x kDecKG consumer warps + 1 producer warp; two
+// CTAs per SM (each with half the shared memory) once there are more tiles
+// than SMs, since the consumers are bound by instruction latency more than by
+// issue, and one CTA with the deeper ring while there are few tiles:
 //   producer   per tile the expert's code tables (built at layer creation: the
 //              level table times each fp8 scale code and the expert scale,
 //              rounded to the operand type) and the tile's fp8 scale codes into
-//              one of two buffers (no global load on the consumers' path); per
-//              128-input step the tile's codes (per projection 4 bulk copies of
-//              2 KB: one 32-input block of all 128 rows each, from the layer's
-//              tiled nibble copy) and the block's 8 activation rows (two TMA
-//              boxes of 64 inputs, 128-B swizzle) into a ring of stages
-//   consumers  warp w of a group owns rows 16w .. 16w+15 of the tile; the
-//              groups take the 128-input steps in turn (more warps in flight to
-//              hide shared-memory and decode latency); per step a warp decodes
-//              its codes with prmt lookups into operand pairs and issues the
-//              MMAs; at the end of a tile groups 1.. hand their sums to group 0,
-//              which adds them in group order (a fixed order on every run) and
-//              applies SwiGLU (gate/up) or the top-k weight (down)
+//              one of two buffers; per 128-input step the tile's codes (one
+//              8 KB bulk copy per projection from the layer's tiled nibble
+//              copy) and the block's 8 activation rows (one 3-D TMA box: two
+//              halves of 64 inputs, 128-B swizzle) into a ring of stages; few
+//              copies per stage, since issuing a copy costs the one producer
+//              thread about as much as a 2 KB copy takes to stream
+//   consumers  warp (rq, kg) owns rows 32 rq .. 32 rq + 31 of the tile (two
+//              16-row MMA tiles) and the steps k with k % kDecKG == kg; per step
+//              a lane decodes 4 rows x 32 inputs per projection with prmt
+//              lookups into operand pairs and issues the MMAs; at the end of a
+//              tile the step groups 1.. hand their sums to group 0 through
+//              shared memory, which adds them in group order (a fixed order on
+//              every run) and applies SwiGLU (gate/up) or the top-k weight
+//              (down)
+// 32 rows per warp halve the per-step work that is not decoding (the ring
+// wait, the activation fragment loads, the scale-code and table loads, the
+// release) per decoded weight against 16 rows per warp.
 //
-// Fragments.  Lane (g = lane/4, q = lane%4) owns rows g and g+8 of its warp's
-// 16 and the 32-input block q of each step.  The reduction index inside each
-// 16-wide MMA is permuted the same way in A and B: MMA chunk c of a step takes,
-// from lane (g, q), inputs q*32 + 4c + {0,1} (k = 2q, 2q+1) and q*32 + 4c +
-// {2,3} (k = 2q+8, 2q+9), so a lane's A registers are its own decoded pairs and
-// its B registers its own 32 consecutive inputs of token g.
+// Fragments.  Lane (g = lane/4, q = lane%4) owns rows g, g+8 (MMA tile 0) and
+// g+16, g+24 (MMA tile 1) of its warp's 32 and the 32-input block q of each
+// step.  The reduction index inside each 16-wide MMA is permuted the same way
+// in A and B: MMA chunk c of a step takes, from lane (g, q), inputs q*32 + 4c +
+// {0,1} (k = 2q, 2q+1) and q*32 + 4c + {2,3} (k = 2q+8, 2q+9), so a lane's A
+// registers are its own decoded pairs and its B registers its own 32
+// consecutive inputs of token g.
 //
-// Shared-memory banks.  The 4 blocks of a step are copied 2048 + 32 bytes
-// apart, so the 8 lanes of a quarter warp (rows g, g+1, blocks 0..3) read 8
-// distinct 16-byte bank groups; table entries are shared by the 4 lanes of a
-// row (one scale code per row and 128 inputs), at most 2 rows per quarter warp.
+// Shared-memory banks.  In the tiled copy, block q of a step holds row r at
+// position r ^ 2q, so the 8 lanes of a quarter warp (rows g, g+1, blocks
+// 0..3) read 8 distinct 16-byte bank groups of the contiguous 8 KB step; table
+// entries are shared by the 4 lanes of a row (one scale code per row and 128
+// inputs), at most 2 rows per quarter warp.
 // Every wait is bounded: a lost arrival sets the device error word and the
 // kernel returns after its in-flight copies land.
 #include <algorithm>
@@ -50,25 +60,33 @@
 
 namespace hexmoe {
 
-constexpr uint32_t kDecBlockStride = 2048 + 32;              // one 32-input block of 128 rows, padded
-constexpr uint32_t kDecProjStride = 4 * kDecBlockStride;     // one projection of a step
+constexpr uint32_t kDecProjStride = kStepBytes;             // one projection of a step: 4 blocks x 128 rows x 16 B
 constexpr uint32_t kDecXBytes = 2 * 8 * 128;                 // 8 rows x 128 inputs (two swizzled boxes)
 constexpr uint32_t kDecCtrl = 1024;                          // barriers
-#ifndef HEXMOE_SB_ACC
-#define HEXMOE_SB_ACC 1
+constexpr int kDecRows = 32;                                 // weight rows per consumer warp
+constexpr int kDecRQ = kTileM / kDecRows;                    // consumer warps covering a tile's rows
+#ifndef HEXMOE_DEC_KG
+#define HEXMOE_DEC_KG 2
 #endif
-constexpr int kSbAcc = HEXMOE_SB_ACC;                         // accumulator sets per projection (1, 2, 4 or 8)
-#ifndef HEXMOE_SB_GROUPS
-#define HEXMOE_SB_GROUPS 2
-#endif
-constexpr int kSbGroups = HEXMOE_SB_GROUPS;   // groups of kSbWarps consumer warps taking the steps in turn
-constexpr int kSbConsumers = kSbWarps * kSbGroups;
+constexpr int kDecKG = HEXMOE_DEC_KG;                        // step groups taking the 128-input steps in turn
+constexpr int kDecConsumers = kDecRQ * kDecKG;
+constexpr int kDecThreads = (kDecConsumers + 1) * 32;
+
+// A tile as the producer hands it to the consumers with the tile's tables
+// (one per table buffer): the consumers read no tile list, slot id or top-k
+// weight from global memory themselves.
+struct DecRec {
+  int32_t b, m, bits, end;     // end: no more tiles for this CTA
+  int32_t slot[kDecBlock];     // the block's slot ids (>= num_slots: padding)
+  float w[kDecBlock];          // down: their top-k weights
+};
 
 struct DecCtrl {
   uint64_t c_full[kDecStages], c_empty[kDecStages];   // step ring
-  uint64_t t_full[2], t_empty[2];                     // table buffers
-  uint64_t r_full[2], r_empty[2];                     // partial sums handed between step groups
+  uint64_t t_full[2], t_empty[2];                     // table buffers (and their tile records)
+  uint64_t r_full, r_empty;                           // partial sums handed from step groups 1.. to group 0
   int32_t abort;
+  DecRec rec[2];
 };
 static_assert(sizeof(DecCtrl) <= kDecCtrl, "decode control block");
 
@@ -121,54 +139,94 @@ __device__ __forceinline__ void dec_drain(uint64_t* bar, uint32_t parity) {
   }
 }
 
-// Producer (one lane): tables per tile, codes + activation boxes per step.
-// Tile t takes its steps starting at step t % ksteps (then wrapping): the
-// tiles in flight on all SMs start at different offsets of their 128 KB
-// streams instead of all reading the same offset at once.
+// A ring position (stage, phase) moved by `n` stages, -ds < n (a step group
+// moves back when the next tile's first step of the group precedes where its
+// last step left it).
+__device__ __forceinline__ void ring_move(int& pos, uint32_t& ph, int n, int ds) {
+  pos += n;
+  while (pos >= ds) { pos -= ds; ph ^= 1u; }
+  while (pos < 0) { pos += ds; ph ^= 1u; }
+}
+
+// Bounded wait taken by lane 0 and its result given to the whole warp (the
+// producer warp's lanes then take the same path).
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* dev_err, int lane) {
+  bool ok = true;
+  if (lane == 0) ok = mbar_wait(bar, parity, abort, dev_err);
+  return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+}
+
+// Producer (one warp; lane 0 issues the copies): per tile its record, tables
+// and scale codes, per step codes + activation box; an end record last.
 template <bool GLU>
-__device__ void dec_producer(const DecParams& p, uint8_t* smem, DecCtrl* c, int num_tiles) {
+__device__ void dec_producer(const DecParams& p, uint8_t* smem, DecCtrl* c, int num_tiles, int lane) {
   constexpr int NPROJ = GLU ? 2 : 1;
   volatile int* abort_flag = &c->abort;
-  uint32_t cs = 0, cph = 0;
+  int cs = 0;
+  uint32_t cph = 0;
   int issued = 0, tissued = 0;
   bool aborted = false;
   for (int t = blockIdx.x; t < num_tiles && !aborted; t += gridDim.x) {
     const DecTile ti = dec_tile(p, t);
-    if (!ti.ok) continue;
+    if (!ti.ok) {
+      if (lane == 0) atomicOr(p.dev_err, kDevErrNoTier);
+      continue;
+    }
     const uint32_t tabn = ti.bits == 3 ? 256u : 512u;
     const int tb = tissued & 1;
-    if (!mbar_wait(&c->t_empty[tb], ((tissued >> 1) & 1) ^ 1, abort_flag, p.dev_err)) { aborted = true; break; }
-    const uint32_t scb = 128u * static_cast<uint32_t>(p.k_pad / p.block);   // the tile's scale codes, one projection
-    mbar_arrive_expect_tx(&c->t_full[tb], NPROJ * (tabn * 16u + scb));
-    for (int j = 0; j < NPROJ; ++j) {
-      bulk_load(smem + p.off_tab + (tb * NPROJ + j) * p.tab_bytes, p.tab[ti.tier][j] + static_cast<size_t>(ti.local) * tabn,
-                tabn * 16u, &c->t_full[tb]);
-      bulk_load(smem + p.off_sc + (tb * NPROJ + j) * p.sc_bytes,
-                p.bs[ti.tier][j] + (static_cast<size_t>(ti.local) * p.rows_pad + static_cast<size_t>(ti.m) * 128) * (scb / 128u),
-                scb, &c->t_full[tb]);
+    if (!warp_wait(&c->t_empty[tb], ((tissued >> 1) & 1) ^ 1, abort_flag, p.dev_err, lane)) { aborted = true; break; }
+    DecRec* rec = &c->rec[tb];
+    if (lane < kDecBlock) {
+      const int sl = __ldg(p.sorted_ids + static_cast<int64_t>(ti.b) * kDecBlock + lane);
+      rec->slot[lane] = sl;
+      rec->w[lane] = (!GLU && sl < p.num_slots) ? __ldg(p.topk_w + sl) : 0.f;
+    }
+    if (lane == 0) {
+      rec->b = ti.b; rec->m = ti.m; rec->bits = ti.bits; rec->end = 0;
+    }
+    __syncwarp();
+    const uint32_t scb = 128u * static_cast<uint32_t>(p.k_pad >> p.block_log2);   // the tile's scale codes, one projection
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&c->t_full[tb], NPROJ * (tabn * 16u + scb));
+      for (int j = 0; j < NPROJ; ++j) {
+        bulk_load(smem + p.off_tab + (tb * NPROJ + j) * p.tab_bytes,
+                  p.tab[ti.tier][j] + static_cast<size_t>(ti.local) * tabn, tabn * 16u, &c->t_full[tb]);
+        bulk_load(smem + p.off_sc + (tb * NPROJ + j) * p.sc_bytes,
+                  p.bs[ti.tier][j] + (static_cast<size_t>(ti.local) * p.rows_pad + static_cast<size_t>(ti.m) * 128) * (scb / 128u),
+                  scb, &c->t_full[tb]);
+      }
     }
     ++tissued;
     const size_t tile_base = (static_cast<size_t>(ti.local) * p.m_tiles + ti.m) * p.ksteps * kStepBytes;
-    const int rot = t % p.ksteps;
-    for (int k = 0; k < p.ksteps; ++k) {
-      const int s = k + rot < p.ksteps ? k + rot : k + rot - p.ksteps;
+    for (int s = 0; s < p.ksteps; ++s) {
       // a spinning wait: the ring refills the moment a stage frees (a sleeping
       // poll here lets the ring drain and the consumers starve)
-      if (!mbar_wait(&c->c_empty[cs], cph ^ 1, abort_flag, p.dev_err)) { aborted = true; break; }
-      uint8_t* st = smem + kDecCtrl + cs * p.stage_bytes;
-      mbar_arrive_expect_tx(&c->c_full[cs], NPROJ * 4u * 2048u + kDecXBytes);
-      tma_load_2d(st, &p.tm_b, &c->c_full[cs], s * 128, ti.b * kDecBlock);
-      tma_load_2d(st + kDecXBytes / 2, &p.tm_b, &c->c_full[cs], s * 128 + 64, ti.b * kDecBlock);
-      for (int j = 0; j < NPROJ; ++j)
-        for (int q = 0; q < 4; ++q)
-          bulk_load(st + kDecXBytes + j * kDecProjStride + q * kDecBlockStride,
-                    p.idx_t[ti.tier][j] + tile_base + static_cast<size_t>(s) * kStepBytes + q * 2048u, 2048u,
-                    &c->c_full[cs]);
+      if (!warp_wait(&c->c_empty[cs], cph ^ 1, abort_flag, p.dev_err, lane)) { aborted = true; break; }
+      if (lane == 0) {
+        uint8_t* st = smem + kDecCtrl + cs * p.stage_bytes;
+        mbar_arrive_expect_tx(&c->c_full[cs], NPROJ * kStepBytes + kDecXBytes);
+        tma_load_3d(st, &p.tm_b, &c->c_full[cs], 0, ti.b * kDecBlock, 2 * s);
+        for (int j = 0; j < NPROJ; ++j)
+          bulk_load(st + kDecXBytes + j * kDecProjStride,
+                    p.idx_t[ti.tier][j] + tile_base + static_cast<size_t>(s) * kStepBytes, kStepBytes, &c->c_full[cs]);
+      }
       ++issued;
-      if (++cs == static_cast<uint32_t>(p.ds)) { cs = 0; cph ^= 1; }
+      if (++cs == p.ds) { cs = 0; cph ^= 1; }
     }
   }
-  if (aborted) {
+  if (!aborted) {
+    // the end record: the consumers stop at it
+    const int tb = tissued & 1;
+    if (warp_wait(&c->t_empty[tb], ((tissued >> 1) & 1) ^ 1, abort_flag, p.dev_err, lane)) {
+      if (lane == 0) {
+        c->rec[tb].end = 1;
+        mbar_arrive(&c->t_full[tb]);
+      }
+      return;
+    }
+    aborted = true;
+  }
+  if (aborted && lane == 0) {
     // let every copy already issued land before the CTA (and its smem) goes away
     for (int i = 1; i <= p.ds && i <= issued; ++i) {
       const int qq = issued - i;
@@ -181,188 +239,182 @@ __device__ void dec_producer(const DecParams& p, uint8_t* smem, DecCtrl* c, int 
   }
 }
 
-// Consumer warp `cw`: rows 16*(cw % kSbWarps) .. +15 of each tile, the steps s
-// with s % kSbGroups == cw / kSbWarps.  Groups 1.. hand their partial sums to
-// group 0 through shared memory (two buffers); group 0 adds them in group order
-// and runs the epilogue.
+// Consumer warp `cw` = (rq, kg): rows 32*rq .. 32*rq+31 of each tile, the
+// steps k with k % kDecKG == kg.
 template <bool GLU, bool BF16>
 __device__ void dec_consumer(const DecParams& p, uint8_t* smem, DecCtrl* c, int num_tiles, int cw, int lane) {
   constexpr int NPROJ = GLU ? 2 : 1;
+  constexpr int NACC = NPROJ * 2 * 4;                       // accumulators per lane
   volatile int* abort_flag = &c->abort;
   const int g = lane >> 2, q = lane & 3;
-  const int warp = cw % kSbWarps, grp = cw / kSbWarps;
-  float* red = reinterpret_cast<float*>(smem + p.off_red);   // [2][kSbGroups-1][kSbWarps][NPROJ][4][32]
-  const uint32_t spr = static_cast<uint32_t>(p.k_pad / p.block);
-  uint32_t cs = 0, cph = 0;
-  int tused = 0;
+  const int rq = cw % kDecRQ, kg = cw / kDecRQ;
+  float* red = reinterpret_cast<float*>(smem + p.off_red);   // [kDecKG-1][kDecRQ][NACC][32]
+  const uint32_t spr = static_cast<uint32_t>(p.k_pad >> p.block_log2);
+  // this lane's 16-byte chunks of token g's 32 inputs of block q (two 64-input
+  // boxes, 128-B swizzle by row)
+  uint32_t xo[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t cc = static_cast<uint32_t>((q & 1) * 4 + i);
+    xo[i] = (q >> 1) * 1024u + g * 128u + ((cc ^ static_cast<uint32_t>(g)) << 4);
+  }
+  const uint32_t row_w = static_cast<uint32_t>(rq * kDecRows + g);   // the lane's first row in the tile
+  // where rows row_w + 8i sit in block q of a step (the tiled copy's r ^ 2q)
+  const uint32_t code_off = q * 2048u + static_cast<uint32_t>(rq * kDecRows + (g ^ (2 * q))) * 16u;
+  int cpos = 0;
+  uint32_t cph = 0;
+  ring_move(cpos, cph, kg, p.ds);                           // the group's first stage
+  int tused = 0, rused = 0;
   uint16_t* out16 = reinterpret_cast<uint16_t*>(p.out);
-  for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
-    const DecTile ti = dec_tile(p, t);
-    if (!ti.ok) {
-      if (warp == 0 && lane == 0) atomicOr(p.dev_err, kDevErrNoTier);
-      continue;
-    }
+  for (;;) {
     const int tb = tused & 1;
     if (!mbar_wait(&c->t_full[tb], (tused >> 1) & 1, abort_flag, p.dev_err)) return;
+    const DecRec& rec = c->rec[tb];
+    if (rec.end) return;
+    const int tile_b = rec.b, tile_m = rec.m, tile_bits = rec.bits;
+    // this lane's tokens 2q, 2q+1 of the block (read before the record is released)
+    const int slot0 = rec.slot[2 * q], slot1 = rec.slot[2 * q + 1];
+    const float w0 = rec.w[2 * q], w1 = rec.w[2 * q + 1];
     const uint8_t* tabs = smem + p.off_tab + tb * NPROJ * p.tab_bytes;
-    const int r_lo = ti.m * 128 + warp * 16 + g;            // rows r_lo and r_lo + 8 of the expert
-    const uint8_t* sb[NPROJ];                                // this lane's row r_lo in the tile's scale codes (smem)
-#pragma unroll
-    for (int j = 0; j < NPROJ; ++j) sb[j] = smem + p.off_sc + (tb * NPROJ + j) * p.sc_bytes + (warp * 16 + g) * spr;
-    // kSbAcc independent accumulator sets per projection (chunk c goes to set c %
-    // kSbAcc), added in set order at the end: short dependency chains of MMAs
-    float acc[NPROJ][kSbAcc][4];
+    const uint8_t* scb = smem + p.off_sc + tb * NPROJ * p.sc_bytes + row_w * spr;
+    float acc[NPROJ][2][4];
 #pragma unroll
     for (int j = 0; j < NPROJ; ++j)
 #pragma unroll
-      for (int a = 0; a < kSbAcc; ++a)
+      for (int s = 0; s < 2; ++s)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) acc[j][a][i] = 0.f;
+        for (int i = 0; i < 4; ++i) acc[j][s][i] = 0.f;
     bool aborted = false;
+    int k = kg;
     auto run = [&](auto bits_c) {
       constexpr int BITS = decltype(bits_c)::value;
-      // scale codes of the next step, loaded one step ahead
-      uint32_t scn[NPROJ][2];
-      auto load_sc = [&](int s) {
-        const uint32_t sci = static_cast<uint32_t>((s * 128 + q * 32) / p.block);
-#pragma unroll
-        for (int j = 0; j < NPROJ; ++j) {
-          scn[j][0] = sb[j][sci];
-          scn[j][1] = sb[j][8 * spr + sci];
-        }
-      };
-      const int rot = t % p.ksteps;
-      auto step_at = [&](int k) { return k + rot < p.ksteps ? k + rot : k + rot - p.ksteps; };
-      if (grp < p.ksteps) load_sc(step_at(grp));
 #pragma unroll 1
-      for (int k = 0; k < p.ksteps; ++k) {
-        if (k % kSbGroups != grp) {           // another group's step: only the ring position moves
-          if (++cs == static_cast<uint32_t>(p.ds)) { cs = 0; cph ^= 1; }
-          continue;
-        }
-        uint32_t sc[NPROJ][2];
-#pragma unroll
-        for (int j = 0; j < NPROJ; ++j) { sc[j][0] = scn[j][0]; sc[j][1] = scn[j][1]; }
-        if (k + kSbGroups < p.ksteps) load_sc(step_at(k + kSbGroups));
-        if (!mbar_wait(&c->c_full[cs], cph, abort_flag, p.dev_err)) { aborted = true; return; }
-        const uint8_t* st = smem + kDecCtrl + cs * p.stage_bytes;
-        // token g's 32 inputs of block q: half q/2 of the step, 16-byte chunks (q%2)*4 .. +3, swizzled by row
+      for (; k < p.ksteps; k += kDecKG) {
+        const uint32_t sci = static_cast<uint32_t>(k * 128 + q * 32) >> p.block_log2;
+        if (!mbar_wait(&c->c_full[cpos], cph, abort_flag, p.dev_err)) { aborted = true; return; }
+        const uint8_t* st = smem + kDecCtrl + cpos * p.stage_bytes;
         uint32_t xr[16];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const uint32_t cc = static_cast<uint32_t>((q & 1) * 4 + i);
-          const uint4 v = *reinterpret_cast<const uint4*>(st + (q >> 1) * 1024 + g * 128 + ((cc ^ g) << 4));
+          const uint4 v = *reinterpret_cast<const uint4*>(st + xo[i]);
           xr[4 * i] = v.x; xr[4 * i + 1] = v.y; xr[4 * i + 2] = v.z; xr[4 * i + 3] = v.w;
         }
 #pragma unroll
         for (int j = 0; j < NPROJ; ++j) {
-          const uint8_t* cb = st + kDecXBytes + j * kDecProjStride + q * kDecBlockStride + (warp * 16 + g) * 16;
-          const uint4 w0 = *reinterpret_cast<const uint4*>(cb);
-          const uint4 w1 = *reinterpret_cast<const uint4*>(cb + 128);
+          const uint8_t* cb = st + kDecXBytes + j * kDecProjStride + code_off;
+          const uint8_t* sj = scb + j * p.sc_bytes + sci;
           const uint4* tab = reinterpret_cast<const uint4*>(tabs + j * p.tab_bytes);
-          const uint4 t0 = tab[sc[j][0]], t1 = tab[sc[j][1]];
-          uint4 h0 = t0, h1 = t1;
-          if constexpr (BITS == 4) {
-            h0 = tab[256 + sc[j][0]];
-            h1 = tab[256 + sc[j][1]];
-          }
-          const uint32_t wa[4] = {w0.x, w0.y, w0.z, w0.w}, wb[4] = {w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-          for (int jw = 0; jw < 4; ++jw) {
-            const uint4 oa = dec8<BITS>(wa[jw], t0, h0);   // row g: inputs 8jw .. 8jw+7 of block q
-            const uint4 ob = dec8<BITS>(wb[jw], t1, h1);   // row g + 8
-            mma16816<BF16>(acc[j][(2 * jw) % kSbAcc], oa.x, ob.x, oa.y, ob.y, xr[4 * jw], xr[4 * jw + 1]);
-            mma16816<BF16>(acc[j][(2 * jw + 1) % kSbAcc], oa.z, ob.z, oa.w, ob.w, xr[4 * jw + 2], xr[4 * jw + 3]);
+          for (int s = 0; s < 2; ++s) {
+            // rows 16 s + g and 16 s + g + 8 of the warp's 32
+            const uint4 w0 = *reinterpret_cast<const uint4*>(cb + (16 * s) * 16);
+            const uint4 w1 = *reinterpret_cast<const uint4*>(cb + (16 * s + 8) * 16);
+            const uint32_t c0 = sj[(16 * s) * spr], c1 = sj[(16 * s + 8) * spr];
+            const uint4 t0 = tab[c0], t1 = tab[c1];
+            uint4 h0 = t0, h1 = t1;
+            if constexpr (BITS == 4) {
+              h0 = tab[256 + c0];
+              h1 = tab[256 + c1];
+            }
+            const uint32_t wa[4] = {w0.x, w0.y, w0.z, w0.w}, wb[4] = {w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+            for (int jw = 0; jw < 4; ++jw) {
+              const uint4 oa = dec8<BITS>(wa[jw], t0, h0);   // row 16s + g: inputs 8jw .. 8jw+7 of block q
+              const uint4 ob = dec8<BITS>(wb[jw], t1, h1);   // row 16s + g + 8
+              mma16816<BF16>(acc[j][s], oa.x, ob.x, oa.y, ob.y, xr[4 * jw], xr[4 * jw + 1]);
+              mma16816<BF16>(acc[j][s], oa.z, ob.z, oa.w, ob.w, xr[4 * jw + 2], xr[4 * jw + 3]);
+            }
           }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&c->c_empty[cs]);
-        if (++cs == static_cast<uint32_t>(p.ds)) { cs = 0; cph ^= 1; }
+        if (lane == 0) mbar_arrive(&c->c_empty[cpos]);
+        ring_move(cpos, cph, kDecKG, p.ds);
       }
     };
-    if (ti.bits == 3) run(std::integral_constant<int, 3>{});
+    if (tile_bits == 3) run(std::integral_constant<int, 3>{});
     else run(std::integral_constant<int, 4>{});
     if (aborted) return;
+    // the group's first step of the next tile: ksteps + kg stages past this tile's start
+    ring_move(cpos, cph, p.ksteps + kg - k, p.ds);
     __syncwarp();
     if (lane == 0) mbar_arrive(&c->t_empty[tb]);
-    const int par = tused & 1, use = tused >> 1;
     ++tused;
-#pragma unroll
-    for (int j = 0; j < NPROJ; ++j)
-#pragma unroll
-      for (int a = 1; a < kSbAcc; ++a)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) acc[j][0][i] += acc[j][a][i];
-    if constexpr (kSbGroups > 1) {
-      float* rb = red + static_cast<size_t>(par) * (kSbGroups - 1) * kSbWarps * NPROJ * 128;
-      if (grp > 0) {
-        // hand the partial sums to group 0 (the buffer of this parity is free once
-        // group 0 has read what was written into it two tiles ago)
-        if (!mbar_wait(&c->r_empty[par], (use & 1) ^ 1, abort_flag, p.dev_err)) return;
-        float* dst = rb + ((grp - 1) * kSbWarps + warp) * NPROJ * 128;
+    if constexpr (kDecKG > 1) {
+      const int ru = rused++;
+      if (kg > 0) {
+        // hand the partial sums to group 0 (the buffer is free once group 0 has
+        // read what was written into it for the previous tile)
+        if (!mbar_wait(&c->r_empty, (ru & 1) ^ 1, abort_flag, p.dev_err)) return;
+        float* dst = red + static_cast<size_t>((kg - 1) * kDecRQ + rq) * NACC * 32;
 #pragma unroll
         for (int j = 0; j < NPROJ; ++j)
 #pragma unroll
-          for (int i = 0; i < 4; ++i) dst[(j * 4 + i) * 32 + lane] = acc[j][0][i];
+          for (int s = 0; s < 2; ++s)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) dst[((j * 2 + s) * 4 + i) * 32 + lane] = acc[j][s][i];
         __syncwarp();
-        if (lane == 0) mbar_arrive(&c->r_full[par]);
+        if (lane == 0) mbar_arrive(&c->r_full);
         continue;
       }
-      if (!mbar_wait(&c->r_full[par], use & 1, abort_flag, p.dev_err)) return;
-      for (int gg = 1; gg < kSbGroups; ++gg) {
-        const float* src = rb + ((gg - 1) * kSbWarps + warp) * NPROJ * 128;
+      if (!mbar_wait(&c->r_full, ru & 1, abort_flag, p.dev_err)) return;
+#pragma unroll
+      for (int gg = 1; gg < kDecKG; ++gg) {
+        const float* src = red + static_cast<size_t>((gg - 1) * kDecRQ + rq) * NACC * 32;
 #pragma unroll
         for (int j = 0; j < NPROJ; ++j)
 #pragma unroll
-          for (int i = 0; i < 4; ++i) acc[j][0][i] += src[(j * 4 + i) * 32 + lane];
+          for (int s = 0; s < 2; ++s)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[j][s][i] += src[((j * 2 + s) * 4 + i) * 32 + lane];
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&c->r_empty[par]);
+      if (lane == 0) mbar_arrive(&c->r_empty);
     }
-    // epilogue: c0, c1 = (row g, tokens 2q, 2q+1), c2, c3 = (row g+8, same tokens)
+    // epilogue: acc[.][s][0..1] = (row 16s + g, tokens 2q, 2q+1), [2..3] = (row 16s + g + 8, same tokens)
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int n = 2 * q + (i & 1);
-      const int row = r_lo + (i >> 1) * 8;
-      const int slot = __ldg(p.sorted_ids + static_cast<int64_t>(ti.b) * kDecBlock + n);
-      if (slot >= p.num_slots || row >= p.rows_store) continue;
-      float r;
-      int64_t o;
-      if constexpr (GLU) {
-        const float gg = acc[0][0][i];
-        r = __fdividef(gg, 1.0f + __expf(-gg)) * acc[1][0][i];   // silu(gate) * up, as the tcgen05 epilogue
-        o = (static_cast<int64_t>(ti.b) * kDecBlock + n) * p.ld_out + row;
-      } else {
-        r = acc[0][0][i] * __ldg(p.topk_w + slot);
-        o = static_cast<int64_t>(slot) * p.ld_out + row;
+    for (int s = 0; s < 2; ++s)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int n = 2 * q + (i & 1);
+        const int row = tile_m * kTileM + static_cast<int>(row_w) + 16 * s + (i >> 1) * 8;
+        const int sl = (i & 1) ? slot1 : slot0;
+        if (sl >= p.num_slots || row >= p.rows_store) continue;
+        float r;
+        int64_t o;
+        if constexpr (GLU) {
+          const float gv = acc[0][s][i];
+          r = __fdividef(gv, 1.0f + __expf(-gv)) * acc[1][s][i];   // silu(gate) * up, as the tcgen05 epilogue
+          o = (static_cast<int64_t>(tile_b) * kDecBlock + n) * p.ld_out + row;
+        } else {
+          r = acc[0][s][i] * ((i & 1) ? w1 : w0);
+          o = static_cast<int64_t>(sl) * p.ld_out + row;
+        }
+        out16[o] = static_cast<uint16_t>(pack2<BF16>(r, 0.f) & 0xFFFFu);
       }
-      out16[o] = static_cast<uint16_t>(pack2<BF16>(r, 0.f) & 0xFFFFu);
-    }
   }
 }
 
 template <bool GLU, bool BF16>
-__global__ void __launch_bounds__((kSbConsumers + 1) * 32, 1) hex_decode_kernel(const __grid_constant__ DecParams p) {
+__global__ void __launch_bounds__(kDecThreads, 2) hex_decode_kernel(const __grid_constant__ DecParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   DecCtrl* c = reinterpret_cast<DecCtrl*>(smem);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kDecStages; ++i) { mbar_init(&c->c_full[i], 1); mbar_init(&c->c_empty[i], kSbWarps); }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&c->t_full[i], 1); mbar_init(&c->t_empty[i], kSbConsumers);
-      mbar_init(&c->r_full[i], kSbWarps * (kSbGroups - 1)); mbar_init(&c->r_empty[i], kSbWarps);
-    }
+    for (int i = 0; i < kDecStages; ++i) { mbar_init(&c->c_full[i], 1); mbar_init(&c->c_empty[i], kDecRQ); }
+    for (int i = 0; i < 2; ++i) { mbar_init(&c->t_full[i], 1); mbar_init(&c->t_empty[i], kDecConsumers); }
+    mbar_init(&c->r_full, kDecRQ * (kDecKG - 1));
+    mbar_init(&c->r_empty, kDecRQ);
     c->abort = 0;
     fence_mbar_init();
   }
-  if (warp == kSbConsumers && lane == 0) prefetch_tmap(&p.tm_b);
+  if (warp == kDecConsumers && lane == 0) prefetch_tmap(&p.tm_b);
   __syncthreads();
   pdl_launch_dependents();
   pdl_wait();   // the plan and the B rows come from the previous kernels
   const int num_tiles = (__ldg(p.npp) / kDecBlock) * p.m_tiles;
-  if (warp == kSbConsumers) {
-    if (lane == 0) dec_producer<GLU>(p, smem, c, num_tiles);
+  if (warp == kDecConsumers) {
+    dec_producer<GLU>(p, smem, c, num_tiles, lane);
   } else {
     dec_consumer<GLU, BF16>(p, smem, c, num_tiles, warp, lane);
   }
@@ -387,7 +439,7 @@ static cudaError_t launch_dec(const DecParams& p, int grid, cudaStream_t st, boo
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid));
-  cfg.blockDim = dim3((kSbConsumers + 1) * 32);
+  cfg.blockDim = dim3(kDecThreads);
   cfg.dynamicSmemBytes = p.smem_bytes;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -398,19 +450,24 @@ static cudaError_t launch_dec(const DecParams& p, int grid, cudaStream_t st, boo
   return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
-// Shared-memory carve-up for one projection pair (2) or one projection (1).
-bool plan_decode(DecParams& p, int nproj) {
+// Shared-memory carve-up for one projection pair (2) or one projection (1),
+// for `per_sm` CTAs on an SM (1 or 2).  p.block and the tiers' bits must be set.
+bool plan_decode(DecParams& p, int nproj, int per_sm) {
+  int max_bits = 3;
+  for (int t = 0; t < p.num_tiers; ++t) max_bits = std::max(max_bits, static_cast<int>(p.bits[t]));
+  p.block_log2 = p.block == 128 ? 7 : 5;
   p.stage_bytes = (kDecXBytes + nproj * kDecProjStride + 1023u) / 1024u * 1024u;
-  p.tab_bytes = 512u * 16u;
+  p.tab_bytes = (max_bits == 3 ? 256u : 512u) * 16u;
   p.sc_bytes = (128u * static_cast<uint32_t>(p.k_pad / p.block) + 127u) / 128u * 128u;
-  const uint32_t fixed = 2u * nproj * (p.tab_bytes + p.sc_bytes) + 2u * (kSbGroups - 1) * kSbWarps * nproj * 128u * 4u;
-  const uint32_t budget = 227u * 1024u - 1024u - kDecCtrl;   // dynamic smem per CTA, minus alignment slack
-  if (fixed + 2u * p.stage_bytes > budget) return false;
+  const uint32_t red = static_cast<uint32_t>(kDecKG - 1) * kDecRQ * nproj * 8u * 32u * 4u;
+  const uint32_t fixed = 2u * nproj * (p.tab_bytes + p.sc_bytes) + red;
+  const uint32_t budget = (per_sm == 2 ? 113u : 227u) * 1024u - 1024u - kDecCtrl;   // per CTA, minus alignment slack
+  if (fixed + static_cast<uint32_t>(kDecKG + 1) * p.stage_bytes > budget) return false;
   p.ds = static_cast<int32_t>(std::min<uint32_t>(kDecStages, (budget - fixed) / p.stage_bytes));
   p.off_tab = kDecCtrl + p.ds * p.stage_bytes;
   p.off_sc = p.off_tab + 2u * nproj * p.tab_bytes;
   p.off_red = p.off_sc + 2u * nproj * p.sc_bytes;
-  p.smem_bytes = p.off_red + 2u * (kSbGroups - 1) * kSbWarps * nproj * 128u * 4u + 1024u;
+  p.smem_bytes = p.off_red + red + 1024u;
   return true;
 }
 

@@ -35,7 +35,8 @@
 //   warps 6..   decoders, groups of 8 taking 128-input sub-blocks in turn: per
 //               32-input block one 16-byte load of its 32 codes (a nibble
 //               each; a warp's loads cover 512 contiguous bytes, free of bank
-//               conflicts), one code-table load and prmt lookups of the codes
+//               conflicts: the tiled copy permutes rows only inside groups of
+//               8), one code-table load and prmt lookups of the codes
 //               into one of two 16-register buffers, written to
 //               TMEM with tcgen05.st while the other buffer's store drains; a
 //               half-stage goes to the MMA once both its stores are done
@@ -528,9 +529,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
           }
           uint32_t w[16];
           if (mine_k) {
-            // this row's 4 words of each 32-input block: [proj][sub][block][row] x 16 B
-            const uint4* w4 = reinterpret_cast<const uint4*>(xring + xs * p.sz_idx) + (proj * spi + sub) * 512 + row;
-            const uint4 v0 = w4[0], v1 = w4[128], v2 = w4[256], v3 = w4[384];
+            // this row's 4 words of each 32-input block: [proj][sub][block][row ^ 2 block] x 16 B
+            const uint4* w4 = reinterpret_cast<const uint4*>(xring + xs * p.sz_idx) + (proj * spi + sub) * 512;
+            const uint4 v0 = w4[row], v1 = w4[128 + (row ^ 2)], v2 = w4[256 + (row ^ 4)], v3 = w4[384 + (row ^ 6)];
             w[0] = v0.x; w[1] = v0.y; w[2] = v0.z; w[3] = v0.w;
             w[4] = v1.x; w[5] = v1.y; w[6] = v1.z; w[7] = v1.w;
             w[8] = v2.x; w[9] = v2.y; w[10] = v2.z; w[11] = v2.w;

@@ -236,6 +236,109 @@ __device__ void plan_runs(const int32_t* counts, int32_t* blk_start, int64_t S, 
     sid[i] = static_cast<int32_t>(S);
 }
 
+// Small batches (decode: up to kAlignSmall slots, up to kAlignSmall experts, no
+// ragged slot space): one CTA of kAlignSmall threads, one slot each, with a
+// short loop body (a cold kernel of this size is bound by instruction fetch,
+// not by its work).  Keys e * 2048 + s are sorted ascending with a bitonic
+// network in shared memory, which orders the slots by expert and, within an
+// expert, by slot: the same stable order as the kernels below.  A slot's place
+// is its expert's first padded row plus its rank among the expert's slots.
+constexpr int kAlignSmall = 1024;
+
+// Exclusive prefix sums of a and b over the CTA's threads (in thread order),
+// and their totals.  All kAlignSmall threads.
+__device__ __forceinline__ void small_scan2(int32_t a, int32_t b, int32_t& ea, int32_t& eb, int32_t& ta, int32_t& tb,
+                                            int32_t* wsum) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int32_t ia = a, ib = b;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int32_t ua = __shfl_up_sync(0xffffffffu, ia, o), ub = __shfl_up_sync(0xffffffffu, ib, o);
+    if (lane >= o) { ia += ua; ib += ub; }
+  }
+  if (lane == 31) { wsum[warp] = ia; wsum[32 + warp] = ib; }
+  __syncthreads();
+  if (warp == 0) {
+    int32_t va = wsum[lane], vb = wsum[32 + lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int32_t ua = __shfl_up_sync(0xffffffffu, va, o), ub = __shfl_up_sync(0xffffffffu, vb, o);
+      if (lane >= o) { va += ua; vb += ub; }
+    }
+    wsum[64 + lane] = va;        // inclusive prefix over warps
+    wsum[96 + lane] = vb;
+  }
+  __syncthreads();
+  const int32_t wa = warp ? wsum[64 + warp - 1] : 0, wb = warp ? wsum[96 + warp - 1] : 0;
+  ea = wa + ia - a;
+  eb = wb + ib - b;
+  ta = wsum[64 + 31];
+  tb = wsum[96 + 31];
+}
+
+template <bool I64>
+__global__ void __launch_bounds__(kAlignSmall, 1)
+    align_small_kernel(const void* __restrict__ ids, int32_t S, int32_t E, int32_t bm, int32_t* __restrict__ sid,
+                       int32_t* __restrict__ eid, int32_t* __restrict__ npp, int32_t* dev_err) {
+  __shared__ uint32_t key[kAlignSmall];
+  __shared__ int32_t cnt[kAlignSmall];      // per expert: slots, then its first place in the sorted keys
+  __shared__ int32_t bstart[kAlignSmall];   // per expert: first block
+  __shared__ int32_t wsum[128];
+  const int t = threadIdx.x;
+  pdl_wait();
+  cnt[t] = 0;
+  __syncthreads();
+  uint32_t k = 0xFFFFFFFFu;                 // past every valid key: bad ids sort last and are dropped
+  if (t < S) {
+    const int64_t v = I64 ? __ldg(static_cast<const int64_t*>(ids) + t)
+                          : static_cast<int64_t>(__ldg(static_cast<const int32_t*>(ids) + t));
+    if (v < 0 || v >= E) {
+      atomicOr(dev_err, kDevErrExpertId);
+    } else {
+      k = (static_cast<uint32_t>(v) << 11) | static_cast<uint32_t>(t);
+      atomicAdd(&cnt[v], 1);
+    }
+  }
+  key[t] = k;
+  int n = 1;
+  while (n < S) n <<= 1;
+  __syncthreads();
+#pragma unroll 1
+  for (int size = 2; size <= n; size <<= 1) {
+#pragma unroll 1
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      const int u = t ^ stride;
+      if (t < n && u > t) {
+        const uint32_t a = key[t], b = key[u];
+        if ((a > b) == ((t & size) == 0)) { key[t] = b; key[u] = a; }
+      }
+      __syncthreads();
+    }
+  }
+  const int32_t c = t < E ? cnt[t] : 0;
+  const int32_t nb = (c + bm - 1) / bm;
+  int32_t c0, b0, valid, total_blocks;
+  small_scan2(c, nb, c0, b0, valid, total_blocks, wsum);
+  if (t < E) {
+    cnt[t] = c0;
+    bstart[t] = b0;
+    for (int j = c; j < nb * bm; ++j) sid[b0 * bm + j] = static_cast<int32_t>(S);   // the run's padding
+    for (int j = 0; j < nb; ++j) eid[b0 + j] = t;
+  }
+  __syncthreads();
+  if (t < valid) {
+    const uint32_t kk = key[t];
+    const int e = static_cast<int>(kk >> 11), s = static_cast<int>(kk & 2047u);
+    sid[bstart[e] * bm + (t - cnt[e])] = s;
+  }
+  const int64_t max_blocks = (S + bm - 1) / bm + (E < S ? E : S);
+  for (int64_t b = total_blocks + t; b < max_blocks; b += kAlignSmall) eid[b] = -1;
+  for (int64_t i = static_cast<int64_t>(total_blocks) * bm + t; i < max_blocks * bm; i += kAlignSmall)
+    sid[i] = static_cast<int32_t>(S);
+  if (t == 0) npp[0] = total_blocks * bm;
+  pdl_launch_dependents();
+}
+
 // One CTA: count, plan, scatter.
 template <bool I64>
 __global__ void __launch_bounds__(kAlignThreads, 1)
@@ -412,6 +515,13 @@ cudaError_t launch_align(const void* ids, bool ids64, int64_t S, int32_t E, int3
   cfg.numAttrs = pdl ? 1 : 0;
   const size_t hist_bytes = static_cast<size_t>(kAlignWarps) * E * sizeof(int32_t);
   const size_t need = align_scratch_bytes(S, E);
+  if (!seg_counts && S <= kAlignSmall && E <= kAlignSmall) {
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(kAlignSmall);
+    const int32_t S32 = static_cast<int32_t>(S);
+    return ids64 ? cudaLaunchKernelEx(&cfg, align_small_kernel<true>, ids, S32, E, bm, sid, eid, npp, dev_err)
+                 : cudaLaunchKernelEx(&cfg, align_small_kernel<false>, ids, S32, E, bm, sid, eid, npp, dev_err);
+  }
   if (need == 0 || !scratch || scratch_bytes < need) {
     cfg.gridDim = dim3(1);
     cfg.dynamicSmemBytes = hist_bytes + 2 * E * sizeof(int32_t);
@@ -504,8 +614,13 @@ cudaError_t launch_dequant(const hexmoe_parts& parts, int bits, int block, int n
 // ---------------------------------------------------------------------------
 // Tiled index copy (hexmoe_tile_index): one thread per output word, in output
 // order (coalesced stores).  Output word o = ((((e * m_tiles + m) * ksteps + s)
-// * 4 + b) * 128 + r) * 4 + j holds, one per nibble, the 8 codes of inputs
-// s*128 + b*32 + j*8 .. +7 of row m*128 + r of expert e.  A stored 32-input
+// * 4 + b) * 128 + p) * 4 + j holds, one per nibble, the 8 codes of inputs
+// s*128 + b*32 + j*8 .. +7 of row m*128 + (p ^ 2b) of expert e: within block b
+// the rows are permuted by flipping bits 1-2 of the row index with b, so that
+// a kernel reading rows g (+ 8i) of blocks 0..3 from one contiguous 8 KB step
+// (lane = (g, b)) hits 8 distinct shared-memory bank groups per quarter warp,
+// while 32 consecutive rows of one block stay 32 consecutive 16-byte chunks.
+// A stored 32-input
 // block is `bits` little-endian words with code i at bits [i*bits, i*bits+bits)
 // (hex_ref.pack, hex_ref.py:49-61): 4-bit words are already nibble-packed;
 // 3-bit word j is the 24 bits from bit 24*j, which never reach past the
@@ -516,7 +631,8 @@ __global__ void tile_index_kernel(const uint32_t* __restrict__ idx, int bits, in
   const int64_t wpr = static_cast<int64_t>(cols_pad) / 32 * bits;
   for (int64_t o = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; o < total;
        o += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int j = static_cast<int>(o & 3), r = static_cast<int>((o >> 2) & 127), b = static_cast<int>((o >> 9) & 3);
+    const int j = static_cast<int>(o & 3), b = static_cast<int>((o >> 9) & 3);
+    const int r = static_cast<int>((o >> 2) & 127) ^ (2 * b);   // the row stored at this position
     const int64_t rest = o >> 11;
     const int s = static_cast<int>(rest % ksteps);
     const int64_t em = rest / ksteps;

@@ -52,9 +52,11 @@ def test_tile_index_layout_vs_oracle_codes(oracle, bits):
                "hexmoe_tile_index")
     torch.cuda.synchronize()
     got = out.cpu().numpy().view(np.uint32).reshape(n, rows_pad // 128, cols_pad // 128, 4, 128, 4)
-    # nibble i of word j of (e, m, s, b, r) = code of input s*128 + b*32 + j*8 + i of row m*128 + r
+    # nibble i of word j of (e, m, s, b, p) = code of input s*128 + b*32 + j*8 + i of row m*128 + (p ^ 2b)
     c = codes.reshape(n, rows_pad // 128, 128, cols_pad // 128, 4, 4, 8).transpose(0, 1, 3, 4, 2, 5, 6)
     want = np.bitwise_or.reduce(c.astype(np.uint32) << (4 * np.arange(8, dtype=np.uint32)), axis=-1)
+    perm = np.arange(128)[None, :] ^ (2 * np.arange(4)[:, None])        # [b, p] -> stored row
+    want = np.take_along_axis(want, perm[None, None, None, :, :, None], axis=4)
     assert np.array_equal(got, want)
 
 
