@@ -13,8 +13,10 @@ rows dispatched to their experts' GPUs over NVLink peer memory, pre-summed
 partials returned), value = all ranks' tokens over the slowest rank's time.
 Synthetic seeded data (blackhole_b200.hex_data): no dataset exists on this
 path.  Steps are replayed from a CUDA graph with inputs in HBM, timed with CUDA
-events on the launching stream; a 256 MiB buffer is written between timed
-steps (cold L2, 126 MB).  `e2e` is the same step through the public API
+events on the launching stream; between timed steps a 256 MiB buffer is
+written and a second one read (cold L2, 126 MB, holding no dirty lines that the
+step would have to write back: a decode step follows other layers' weight reads,
+which leave clean lines).  `e2e` is the same step through the public API
 (hex_moe / EPMoE) with the inputs copied from pinned host memory and the
 output copied back inside the timed region.  `roofline` is for the dominant
 kernel, the gate/up grouped GEMM of the 1-GPU layer, timed alone (tensor-bound).
@@ -556,9 +558,11 @@ def main() -> None:
     pk = peaks()
     stream = torch.cuda.current_stream(dev)
     flush_buf = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    flush_read = torch.ones(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
 
     def flush():
         flush_buf.fill_(rank & 0xFF)
+        flush_read.sum()
 
     if args.profile == "decode":
         from blackhole_b200.hex_moe import auto_block_m
@@ -694,7 +698,7 @@ def main() -> None:
             "config": {"workload": f"cfg3 prefill: E={E} H={H} I={I} top-{K_TOP}, SwiGLU, mixed 3/4-bit HEX (half the "
                                    f"experts each), fp8 e4m3 block-{BLOCK} scales, {T} tokens per GPU",
                        "tokens": T, "block_m": 128, "parallelism": par,
-                       "l2": "flushed between timed steps (256 MiB write)", "timed_wall_s": t1 - t0},
+                       "l2": "flushed between timed steps (256 MiB written, then 256 MiB read)", "timed_wall_s": t1 - t0},
             "e2e": {"value": world * T / (e2e_step_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_step_ms},
             "gpu_launches": launches * args.steps, "roofline": roof, "clocks": clk, "device_error_word": err,
