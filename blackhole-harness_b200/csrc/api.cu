@@ -201,6 +201,25 @@ int plan_gemm(GemmParams& p, bool glu, int bm, int k_pad, int block) {
   return HEXMOE_OK;
 }
 
+// Tile height and CTAs per SM of a small-batch launch (rows_pad, k_pad, block
+// and bits of p set): the tallest tiles (128, 64, 32 rows) that still give
+// two CTAs per SM a tile each for the plan's most blocks, else 32-row tiles
+// (never more step groups than steps); two CTAs per SM once there are more
+// tiles than SMs and the carve-up fits, else one with the deeper ring.
+bool plan_small(DecParams& p, int nproj, int64_t max_blocks, int num_sms, int& per_sm) {
+  const int ksteps = p.k_pad / kKStep;
+  int rq = 4;
+  for (int c : {4, 2, 1}) {
+    if (c < 4 && 8 / c > ksteps) break;             // more step groups than steps
+    rq = c;
+    if (max_blocks * (p.rows_pad / (32 * c)) >= 2 * num_sms) break;
+  }
+  p.m128 = p.rows_pad / kTileM;
+  p.m_tiles = p.rows_pad / (32 * rq);
+  per_sm = max_blocks * p.m_tiles > num_sms && plan_decode(p, nproj, 2, rq) ? 2 : 1;
+  return per_sm == 2 || plan_decode(p, nproj, 1, rq);
+}
+
 struct DeviceGuard {
   int prev = -1;
   explicit DeviceGuard(int dev) {
@@ -253,9 +272,8 @@ int run_gate_up(const hexmoe_layer* layer, const void* xs, bool bf16, int64_t to
     q.rows_pad = d.inter_pad; q.rows_store = d.inter_pad; q.k_pad = d.hidden_pad;
     q.block = d.block; q.m_tiles = d.inter_pad / kTileM; q.ksteps = d.hidden_pad / kKStep;
     q.out = act; q.ld_out = d.inter_pad; q.topk_w = nullptr; q.dev_err = dev_err;
-    // two CTAs per SM once the plan can give every SM more than one tile
-    const int per_sm = max_blocks * q.m_tiles > layer->num_sms && plan_decode(q, 2, 2) ? 2 : 1;
-    if (per_sm == 1 && !plan_decode(q, 2, 1))
+    int per_sm = 1;
+    if (!plan_small(q, 2, max_blocks, layer->num_sms, per_sm))
       return fail(HEXMOE_E_UNSUPPORTED, "hidden %d does not fit the small-batch kernel", d.hidden_pad);
     if (int rc = make_tmap_chunks(&q.tm_b, xs, dt16, d.hidden, static_cast<uint64_t>(max_blocks) * bm, 2ull * d.hidden,
                                   kDecBlock, "x_sorted tensor map"))
@@ -318,8 +336,8 @@ int run_down(const hexmoe_layer* layer, const void* act, bool bf16, int64_t toke
     r.rows_pad = d.hidden_pad; r.rows_store = d.hidden; r.k_pad = d.inter_pad;
     r.block = d.block; r.m_tiles = d.hidden_pad / kTileM; r.ksteps = d.inter_pad / kKStep;
     r.out = y; r.ld_out = d.hidden; r.topk_w = topk_weights; r.dev_err = dev_err;
-    const int per_sm = max_blocks * r.m_tiles > layer->num_sms && plan_decode(r, 1, 2) ? 2 : 1;
-    if (per_sm == 1 && !plan_decode(r, 1, 1))
+    int per_sm = 1;
+    if (!plan_small(r, 1, max_blocks, layer->num_sms, per_sm))
       return fail(HEXMOE_E_UNSUPPORTED, "inter %d does not fit the small-batch kernel", d.inter_pad);
     if (int rc = make_tmap_chunks(&r.tm_b, act, dt16, d.inter_pad, static_cast<uint64_t>(max_blocks) * bm,
                                   2ull * d.inter_pad, kDecBlock, "act tensor map"))

@@ -10,7 +10,9 @@
 //   down:           y[slot, o]  = (act_row . Wd[e, o]) * topk_weight[slot]
 //
 // Persistent CTAs over the tiles (align block b of <= 8 slots of one expert,
-// 128 weight rows m), kDecRQ x kDecKG consumer warps + 1 producer warp; two
+// 32 RQ weight rows m, RQ = 1, 2 or 4: the smallest tiles while there are few
+// of them, so that small batches spread over the SMs), RQ x (8 / RQ) consumer
+// warps + 1 producer warp; two
 // CTAs per SM (each with half the shared memory) once there are more tiles
 // than SMs, since the consumers are bound by instruction latency more than by
 // issue, and one CTA with the deeper ring while there are few tiles:
@@ -18,13 +20,13 @@
 //              level table times each fp8 scale code and the expert scale,
 //              rounded to the operand type) and the tile's fp8 scale codes into
 //              one of two buffers; per 128-input step the tile's codes (one
-//              8 KB bulk copy per projection from the layer's tiled nibble
+//              RQ x 2 KB bulk copy per projection from the layer's tiled nibble
 //              copy) and the block's 8 activation rows (one 3-D TMA box: two
 //              halves of 64 inputs, 128-B swizzle) into a ring of stages; few
 //              copies per stage, since issuing a copy costs the one producer
 //              thread about as much as a 2 KB copy takes to stream
 //   consumers  warp (rq, kg) owns rows 32 rq .. 32 rq + 31 of the tile (two
-//              16-row MMA tiles) and the steps k with k % kDecKG == kg; per step
+//              16-row MMA tiles) and the steps k with k % (8 / RQ) == kg; per step
 //              a lane decodes 4 rows x 32 inputs per projection with prmt
 //              lookups into operand pairs and issues the MMAs; at the end of a
 //              tile the step groups 1.. hand their sums to group 0 through
@@ -43,9 +45,9 @@
 // registers are its own decoded pairs and its B registers its own 32
 // consecutive inputs of token g.
 //
-// Shared-memory banks.  In the tiled copy, block q of a step holds row r at
-// position r ^ 2q, so the 8 lanes of a quarter warp (rows g, g+1, blocks
-// 0..3) read 8 distinct 16-byte bank groups of the contiguous 8 KB step; table
+// Shared-memory banks.  In the tiled copy, block q of a 32-row slice holds row
+// r at position r ^ 2q, so the 8 lanes of a quarter warp (rows g, g+1, blocks
+// 0..3) read 8 distinct 16-byte bank groups of the contiguous 2 KB slice; table
 // entries are shared by the 4 lanes of a row (one scale code per row and 128
 // inputs), at most 2 rows per quarter warp.
 // Every wait is bounded: a lost arrival sets the device error word and the
@@ -60,16 +62,11 @@
 
 namespace hexmoe {
 
-constexpr uint32_t kDecProjStride = kStepBytes;             // one projection of a step: 4 blocks x 128 rows x 16 B
+constexpr uint32_t kDecSlice = 2048;                         // 32 rows x 128 inputs of codes (one slice of a step)
 constexpr uint32_t kDecXBytes = 2 * 8 * 128;                 // 8 rows x 128 inputs (two swizzled boxes)
 constexpr uint32_t kDecCtrl = 1024;                          // barriers
 constexpr int kDecRows = 32;                                 // weight rows per consumer warp
-constexpr int kDecRQ = kTileM / kDecRows;                    // consumer warps covering a tile's rows
-#ifndef HEXMOE_DEC_KG
-#define HEXMOE_DEC_KG 2
-#endif
-constexpr int kDecKG = HEXMOE_DEC_KG;                        // step groups taking the 128-input steps in turn
-constexpr int kDecConsumers = kDecRQ * kDecKG;
+constexpr int kDecConsumers = 8;                             // RQ row slices x 8 / RQ step groups
 constexpr int kDecThreads = (kDecConsumers + 1) * 32;
 
 // A tile as the producer hands it to the consumers with the tile's tables
@@ -82,7 +79,7 @@ struct DecRec {
 };
 
 struct DecCtrl {
-  uint64_t c_full[kDecStages], c_empty[kDecStages];   // step ring
+  uint64_t c_full[kDecStages], c_empty[kDecStages];   // step ring (released by the RQ warps of a step group)
   uint64_t t_full[2], t_empty[2];                     // table buffers (and their tile records)
   uint64_t r_full, r_empty;                           // partial sums handed from step groups 1.. to group 0
   int32_t abort;
@@ -158,9 +155,10 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
 
 // Producer (one warp; lane 0 issues the copies): per tile its record, tables
 // and scale codes, per step codes + activation box; an end record last.
-template <bool GLU>
+template <bool GLU, int RQ>
 __device__ void dec_producer(const DecParams& p, uint8_t* smem, DecCtrl* c, int num_tiles, int lane) {
   constexpr int NPROJ = GLU ? 2 : 1;
+  constexpr uint32_t kProj = RQ * kDecSlice;           // one projection's codes of a step
   volatile int* abort_flag = &c->abort;
   int cs = 0;
   uint32_t cph = 0;
@@ -185,30 +183,34 @@ __device__ void dec_producer(const DecParams& p, uint8_t* smem, DecCtrl* c, int 
       rec->b = ti.b; rec->m = ti.m; rec->bits = ti.bits; rec->end = 0;
     }
     __syncwarp();
-    const uint32_t scb = 128u * static_cast<uint32_t>(p.k_pad >> p.block_log2);   // the tile's scale codes, one projection
+    const uint32_t scb = static_cast<uint32_t>(RQ * kDecRows) * static_cast<uint32_t>(p.k_pad >> p.block_log2);  // tile's scale codes, one projection
     if (lane == 0) {
       mbar_arrive_expect_tx(&c->t_full[tb], NPROJ * (tabn * 16u + scb));
       for (int j = 0; j < NPROJ; ++j) {
         bulk_load(smem + p.off_tab + (tb * NPROJ + j) * p.tab_bytes,
                   p.tab[ti.tier][j] + static_cast<size_t>(ti.local) * tabn, tabn * 16u, &c->t_full[tb]);
         bulk_load(smem + p.off_sc + (tb * NPROJ + j) * p.sc_bytes,
-                  p.bs[ti.tier][j] + (static_cast<size_t>(ti.local) * p.rows_pad + static_cast<size_t>(ti.m) * 128) * (scb / 128u),
+                  p.bs[ti.tier][j] + (static_cast<size_t>(ti.local) * p.rows_pad + static_cast<size_t>(ti.m) * (RQ * kDecRows)) *
+                                         static_cast<size_t>(p.k_pad >> p.block_log2),
                   scb, &c->t_full[tb]);
       }
     }
     ++tissued;
-    const size_t tile_base = (static_cast<size_t>(ti.local) * p.m_tiles + ti.m) * p.ksteps * kStepBytes;
+    // the tile's rows in the tiled copy: 128-row tile r0 / 128, slices from (r0 % 128) / 32
+    const int r0 = ti.m * RQ * kDecRows;
+    const size_t tile_base = (static_cast<size_t>(ti.local) * p.m128 + (r0 >> 7)) * p.ksteps * kStepBytes +
+                             static_cast<size_t>((r0 & 127) >> 5) * kDecSlice;
     for (int s = 0; s < p.ksteps; ++s) {
       // a spinning wait: the ring refills the moment a stage frees (a sleeping
       // poll here lets the ring drain and the consumers starve)
       if (!warp_wait(&c->c_empty[cs], cph ^ 1, abort_flag, p.dev_err, lane)) { aborted = true; break; }
       if (lane == 0) {
         uint8_t* st = smem + kDecCtrl + cs * p.stage_bytes;
-        mbar_arrive_expect_tx(&c->c_full[cs], NPROJ * kStepBytes + kDecXBytes);
+        mbar_arrive_expect_tx(&c->c_full[cs], NPROJ * kProj + kDecXBytes);
         tma_load_3d(st, &p.tm_b, &c->c_full[cs], 0, ti.b * kDecBlock, 2 * s);
         for (int j = 0; j < NPROJ; ++j)
-          bulk_load(st + kDecXBytes + j * kDecProjStride,
-                    p.idx_t[ti.tier][j] + tile_base + static_cast<size_t>(s) * kStepBytes, kStepBytes, &c->c_full[cs]);
+          bulk_load(st + kDecXBytes + j * kProj, p.idx_t[ti.tier][j] + tile_base + static_cast<size_t>(s) * kStepBytes,
+                    kProj, &c->c_full[cs]);
       }
       ++issued;
       if (++cs == p.ds) { cs = 0; cph ^= 1; }
@@ -240,15 +242,17 @@ __device__ void dec_producer(const DecParams& p, uint8_t* smem, DecCtrl* c, int 
 }
 
 // Consumer warp `cw` = (rq, kg): rows 32*rq .. 32*rq+31 of each tile, the
-// steps k with k % kDecKG == kg.
-template <bool GLU, bool BF16>
-__device__ void dec_consumer(const DecParams& p, uint8_t* smem, DecCtrl* c, int num_tiles, int cw, int lane) {
+// steps k with k % KG == kg.
+template <bool GLU, bool BF16, int RQ>
+__device__ void dec_consumer(const DecParams& p, uint8_t* smem, DecCtrl* c, int cw, int lane) {
   constexpr int NPROJ = GLU ? 2 : 1;
+  constexpr int KG = kDecConsumers / RQ;
+  constexpr uint32_t kProj = RQ * kDecSlice;
   constexpr int NACC = NPROJ * 2 * 4;                       // accumulators per lane
   volatile int* abort_flag = &c->abort;
   const int g = lane >> 2, q = lane & 3;
-  const int rq = cw % kDecRQ, kg = cw / kDecRQ;
-  float* red = reinterpret_cast<float*>(smem + p.off_red);   // [kDecKG-1][kDecRQ][NACC][32]
+  const int rq = cw % RQ, kg = cw / RQ;
+  float* red = reinterpret_cast<float*>(smem + p.off_red);   // [KG-1][RQ][NACC][32]
   const uint32_t spr = static_cast<uint32_t>(p.k_pad >> p.block_log2);
   // this lane's 16-byte chunks of token g's 32 inputs of block q (two 64-input
   // boxes, 128-B swizzle by row)
@@ -259,8 +263,8 @@ __device__ void dec_consumer(const DecParams& p, uint8_t* smem, DecCtrl* c, int 
     xo[i] = (q >> 1) * 1024u + g * 128u + ((cc ^ static_cast<uint32_t>(g)) << 4);
   }
   const uint32_t row_w = static_cast<uint32_t>(rq * kDecRows + g);   // the lane's first row in the tile
-  // where rows row_w + 8i sit in block q of a step (the tiled copy's r ^ 2q)
-  const uint32_t code_off = q * 2048u + static_cast<uint32_t>(rq * kDecRows + (g ^ (2 * q))) * 16u;
+  // where rows row_w + 8i sit in block q of the warp's slice (the tiled copy's r ^ 2q)
+  const uint32_t code_off = rq * kDecSlice + q * 512u + static_cast<uint32_t>(g ^ (2 * q)) * 16u;
   int cpos = 0;
   uint32_t cph = 0;
   ring_move(cpos, cph, kg, p.ds);                           // the group's first stage
@@ -289,7 +293,7 @@ __device__ void dec_consumer(const DecParams& p, uint8_t* smem, DecCtrl* c, int 
     auto run = [&](auto bits_c) {
       constexpr int BITS = decltype(bits_c)::value;
 #pragma unroll 1
-      for (; k < p.ksteps; k += kDecKG) {
+      for (; k < p.ksteps; k += KG) {
         const uint32_t sci = static_cast<uint32_t>(k * 128 + q * 32) >> p.block_log2;
         if (!mbar_wait(&c->c_full[cpos], cph, abort_flag, p.dev_err)) { aborted = true; return; }
         const uint8_t* st = smem + kDecCtrl + cpos * p.stage_bytes;
@@ -301,7 +305,7 @@ __device__ void dec_consumer(const DecParams& p, uint8_t* smem, DecCtrl* c, int 
         }
 #pragma unroll
         for (int j = 0; j < NPROJ; ++j) {
-          const uint8_t* cb = st + kDecXBytes + j * kDecProjStride + code_off;
+          const uint8_t* cb = st + kDecXBytes + j * kProj + code_off;
           const uint8_t* sj = scb + j * p.sc_bytes + sci;
           const uint4* tab = reinterpret_cast<const uint4*>(tabs + j * p.tab_bytes);
 #pragma unroll
@@ -328,7 +332,7 @@ __device__ void dec_consumer(const DecParams& p, uint8_t* smem, DecCtrl* c, int 
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&c->c_empty[cpos]);
-        ring_move(cpos, cph, kDecKG, p.ds);
+        ring_move(cpos, cph, KG, p.ds);
       }
     };
     if (tile_bits == 3) run(std::integral_constant<int, 3>{});
@@ -339,13 +343,13 @@ __device__ void dec_consumer(const DecParams& p, uint8_t* smem, DecCtrl* c, int 
     __syncwarp();
     if (lane == 0) mbar_arrive(&c->t_empty[tb]);
     ++tused;
-    if constexpr (kDecKG > 1) {
+    if constexpr (KG > 1) {
       const int ru = rused++;
       if (kg > 0) {
         // hand the partial sums to group 0 (the buffer is free once group 0 has
         // read what was written into it for the previous tile)
         if (!mbar_wait(&c->r_empty, (ru & 1) ^ 1, abort_flag, p.dev_err)) return;
-        float* dst = red + static_cast<size_t>((kg - 1) * kDecRQ + rq) * NACC * 32;
+        float* dst = red + static_cast<size_t>((kg - 1) * RQ + rq) * NACC * 32;
 #pragma unroll
         for (int j = 0; j < NPROJ; ++j)
 #pragma unroll
@@ -358,8 +362,8 @@ __device__ void dec_consumer(const DecParams& p, uint8_t* smem, DecCtrl* c, int 
       }
       if (!mbar_wait(&c->r_full, ru & 1, abort_flag, p.dev_err)) return;
 #pragma unroll
-      for (int gg = 1; gg < kDecKG; ++gg) {
-        const float* src = red + static_cast<size_t>((gg - 1) * kDecRQ + rq) * NACC * 32;
+      for (int gg = 1; gg < KG; ++gg) {
+        const float* src = red + static_cast<size_t>((gg - 1) * RQ + rq) * NACC * 32;
 #pragma unroll
         for (int j = 0; j < NPROJ; ++j)
 #pragma unroll
@@ -376,7 +380,7 @@ __device__ void dec_consumer(const DecParams& p, uint8_t* smem, DecCtrl* c, int 
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int n = 2 * q + (i & 1);
-        const int row = tile_m * kTileM + static_cast<int>(row_w) + 16 * s + (i >> 1) * 8;
+        const int row = tile_m * (RQ * kDecRows) + static_cast<int>(row_w) + 16 * s + (i >> 1) * 8;
         const int sl = (i & 1) ? slot1 : slot0;
         if (sl >= p.num_slots || row >= p.rows_store) continue;
         float r;
@@ -394,17 +398,18 @@ __device__ void dec_consumer(const DecParams& p, uint8_t* smem, DecCtrl* c, int 
   }
 }
 
-template <bool GLU, bool BF16>
+template <bool GLU, bool BF16, int RQ>
 __global__ void __launch_bounds__(kDecThreads, 2) hex_decode_kernel(const __grid_constant__ DecParams p) {
+  constexpr int KG = kDecConsumers / RQ;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   DecCtrl* c = reinterpret_cast<DecCtrl*>(smem);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kDecStages; ++i) { mbar_init(&c->c_full[i], 1); mbar_init(&c->c_empty[i], kDecRQ); }
+    for (int i = 0; i < kDecStages; ++i) { mbar_init(&c->c_full[i], 1); mbar_init(&c->c_empty[i], RQ); }
     for (int i = 0; i < 2; ++i) { mbar_init(&c->t_full[i], 1); mbar_init(&c->t_empty[i], kDecConsumers); }
-    mbar_init(&c->r_full, kDecRQ * (kDecKG - 1));
-    mbar_init(&c->r_empty, kDecRQ);
+    mbar_init(&c->r_full, RQ * (KG - 1));
+    mbar_init(&c->r_empty, RQ);
     c->abort = 0;
     fence_mbar_init();
   }
@@ -414,15 +419,15 @@ __global__ void __launch_bounds__(kDecThreads, 2) hex_decode_kernel(const __grid
   pdl_wait();   // the plan and the B rows come from the previous kernels
   const int num_tiles = (__ldg(p.npp) / kDecBlock) * p.m_tiles;
   if (warp == kDecConsumers) {
-    dec_producer<GLU>(p, smem, c, num_tiles, lane);
+    dec_producer<GLU, RQ>(p, smem, c, num_tiles, lane);
   } else {
-    dec_consumer<GLU, BF16>(p, smem, c, num_tiles, warp, lane);
+    dec_consumer<GLU, BF16, RQ>(p, smem, c, warp, lane);
   }
 }
 
-template <bool GLU, bool BF16>
+template <bool GLU, bool BF16, int RQ>
 static cudaError_t launch_dec(const DecParams& p, int grid, cudaStream_t st, bool pdl) {
-  auto kern = hex_decode_kernel<GLU, BF16>;
+  auto kern = hex_decode_kernel<GLU, BF16, RQ>;
   static std::atomic<int> configured_bytes[64] = {};
   static std::mutex mu;
   int dev = 0;
@@ -451,18 +456,21 @@ static cudaError_t launch_dec(const DecParams& p, int grid, cudaStream_t st, boo
 }
 
 // Shared-memory carve-up for one projection pair (2) or one projection (1),
-// for `per_sm` CTAs on an SM (1 or 2).  p.block and the tiers' bits must be set.
-bool plan_decode(DecParams& p, int nproj, int per_sm) {
+// for `per_sm` CTAs on an SM (1 or 2) and tiles of 32 rq rows (1, 2 or 4).
+// p.block and the tiers' bits must be set.
+bool plan_decode(DecParams& p, int nproj, int per_sm, int rq) {
   int max_bits = 3;
   for (int t = 0; t < p.num_tiers; ++t) max_bits = std::max(max_bits, static_cast<int>(p.bits[t]));
+  const int kg = kDecConsumers / rq;
+  p.rq = rq;
   p.block_log2 = p.block == 128 ? 7 : 5;
-  p.stage_bytes = (kDecXBytes + nproj * kDecProjStride + 1023u) / 1024u * 1024u;
+  p.stage_bytes = (kDecXBytes + nproj * rq * kDecSlice + 1023u) / 1024u * 1024u;
   p.tab_bytes = (max_bits == 3 ? 256u : 512u) * 16u;
-  p.sc_bytes = (128u * static_cast<uint32_t>(p.k_pad / p.block) + 127u) / 128u * 128u;
-  const uint32_t red = static_cast<uint32_t>(kDecKG - 1) * kDecRQ * nproj * 8u * 32u * 4u;
+  p.sc_bytes = (static_cast<uint32_t>(rq * kDecRows) * static_cast<uint32_t>(p.k_pad / p.block) + 127u) / 128u * 128u;
+  const uint32_t red = static_cast<uint32_t>(kg - 1) * rq * nproj * 8u * 32u * 4u;
   const uint32_t fixed = 2u * nproj * (p.tab_bytes + p.sc_bytes) + red;
   const uint32_t budget = (per_sm == 2 ? 113u : 227u) * 1024u - 1024u - kDecCtrl;   // per CTA, minus alignment slack
-  if (fixed + static_cast<uint32_t>(kDecKG + 1) * p.stage_bytes > budget) return false;
+  if (fixed + static_cast<uint32_t>(std::min(kg, 4) + 1) * p.stage_bytes > budget) return false;
   p.ds = static_cast<int32_t>(std::min<uint32_t>(kDecStages, (budget - fixed) / p.stage_bytes));
   p.off_tab = kDecCtrl + p.ds * p.stage_bytes;
   p.off_sc = p.off_tab + 2u * nproj * p.tab_bytes;
@@ -471,9 +479,17 @@ bool plan_decode(DecParams& p, int nproj, int per_sm) {
   return true;
 }
 
+template <int RQ>
+static cudaError_t launch_dec_rq(const DecParams& p, bool glu, bool bf16, int grid, cudaStream_t st, bool pdl) {
+  if (glu) return bf16 ? launch_dec<true, true, RQ>(p, grid, st, pdl) : launch_dec<true, false, RQ>(p, grid, st, pdl);
+  return bf16 ? launch_dec<false, true, RQ>(p, grid, st, pdl) : launch_dec<false, false, RQ>(p, grid, st, pdl);
+}
+
 cudaError_t launch_decode_gemm(const DecParams& p, bool glu, bool bf16, int grid, cudaStream_t st, bool pdl) {
-  if (glu) return bf16 ? launch_dec<true, true>(p, grid, st, pdl) : launch_dec<true, false>(p, grid, st, pdl);
-  return bf16 ? launch_dec<false, true>(p, grid, st, pdl) : launch_dec<false, false>(p, grid, st, pdl);
+  if (p.rq == 1) return launch_dec_rq<1>(p, glu, bf16, grid, st, pdl);
+  if (p.rq == 2) return launch_dec_rq<2>(p, glu, bf16, grid, st, pdl);
+  if (p.rq == 4) return launch_dec_rq<4>(p, glu, bf16, grid, st, pdl);
+  return cudaErrorInvalidValue;
 }
 
 }  // namespace hexmoe

@@ -529,9 +529,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
           }
           uint32_t w[16];
           if (mine_k) {
-            // this row's 4 words of each 32-input block: [proj][sub][block][row ^ 2 block] x 16 B
-            const uint4* w4 = reinterpret_cast<const uint4*>(xring + xs * p.sz_idx) + (proj * spi + sub) * 512;
-            const uint4 v0 = w4[row], v1 = w4[128 + (row ^ 2)], v2 = w4[256 + (row ^ 4)], v3 = w4[384 + (row ^ 6)];
+            // this row's 4 words of each 32-input block: [proj][sub][32-row slice][block][row ^ 2 block] x 16 B
+            const uint4* w4 = reinterpret_cast<const uint4*>(xring + xs * p.sz_idx) + (proj * spi + sub) * 512 +
+                              (row >> 5) * 128;
+            const int rs = row & 31;
+            const uint4 v0 = w4[rs], v1 = w4[32 + (rs ^ 2)], v2 = w4[64 + (rs ^ 4)], v3 = w4[96 + (rs ^ 6)];
             w[0] = v0.x; w[1] = v0.y; w[2] = v0.z; w[3] = v0.w;
             w[4] = v1.x; w[5] = v1.y; w[6] = v1.z; w[7] = v1.w;
             w[8] = v2.x; w[9] = v2.y; w[10] = v2.z; w[11] = v2.w;

@@ -78,11 +78,11 @@ struct GemmParams {
 cudaError_t launch_gemm(const GemmParams& p, bool glu, bool bf16, int grid, cudaStream_t stream, bool pdl);
 
 // The small-batch grouped GEMM (decode_gemm.cu): align blocks of kDecBlock
-// slots; persistent CTAs over the tiles (block, 128 weight rows), a producer
-// warp streaming 128-input steps through a shared-memory ring, consumer warps
-// of 32 rows each.
+// slots; persistent CTAs over the tiles (block, 32, 64 or 128 weight rows), a
+// producer warp streaming 128-input steps through a shared-memory ring, 8
+// consumer warps of 32 rows each.
 constexpr int kDecBlock = 8;
-constexpr int kDecStages = 8;    // deepest step ring
+constexpr int kDecStages = 16;   // deepest step ring
 struct DecParams {
   CUtensorMap tm_b;                     // plan-ordered B rows (x_sorted or act): boxes of 64 inputs x 8 rows, 128-B swizzle
   const uint8_t* idx_t[kMaxTiers][2];   // tiled index streams (hexmoe_tile_index layout)
@@ -98,6 +98,8 @@ struct DecParams {
   int32_t num_slots;
   int32_t rows_pad, rows_store, k_pad, block, m_tiles, ksteps;
   int32_t block_log2;                   // log2(block), set by plan_decode
+  int32_t rq;                           // tile height in 32-row slices (1, 2, 4): m_tiles = rows_pad / (32 rq)
+  int32_t m128;                         // rows_pad / 128 (the tiled copy's row tiles)
   int32_t ds;                           // ring depth (stages)
   uint32_t stage_bytes, off_tab, tab_bytes, off_sc, sc_bytes, off_red, smem_bytes;   // shared-memory carve-up
   void* out;                            // gate/up: act [plan rows, ld_out]; down: y [S, ld_out]
@@ -106,8 +108,8 @@ struct DecParams {
   int32_t* dev_err;
 };
 // The shared-memory carve-up (block and tier bits set) for per_sm (1 or 2) CTAs
-// on an SM; false when it does not fit.
-bool plan_decode(DecParams& p, int nproj, int per_sm);
+// on an SM and tiles of 32 rq rows; false when it does not fit.
+bool plan_decode(DecParams& p, int nproj, int per_sm, int rq);
 cudaError_t launch_decode_gemm(const DecParams& p, bool glu, bool bf16, int grid, cudaStream_t st, bool pdl);
 // Code tables of one projection of a tier (kernels.cu): out [n][256 or 512] uint4.
 cudaError_t launch_code_tables(const float* levels, const float* es, int bits, int n, bool bf16, uint4* out,

@@ -613,13 +613,16 @@ cudaError_t launch_dequant(const hexmoe_parts& parts, int bits, int block, int n
 
 // ---------------------------------------------------------------------------
 // Tiled index copy (hexmoe_tile_index): one thread per output word, in output
-// order (coalesced stores).  Output word o = ((((e * m_tiles + m) * ksteps + s)
-// * 4 + b) * 128 + p) * 4 + j holds, one per nibble, the 8 codes of inputs
-// s*128 + b*32 + j*8 .. +7 of row m*128 + (p ^ 2b) of expert e: within block b
-// the rows are permuted by flipping bits 1-2 of the row index with b, so that
-// a kernel reading rows g (+ 8i) of blocks 0..3 from one contiguous 8 KB step
-// (lane = (g, b)) hits 8 distinct shared-memory bank groups per quarter warp,
-// while 32 consecutive rows of one block stay 32 consecutive 16-byte chunks.
+// order (coalesced stores).  Output word o = (((((e * m_tiles + m) * ksteps +
+// s) * 4 + h) * 4 + b) * 32 + p) * 4 + j holds, one per nibble, the 8 codes of
+// inputs s*128 + b*32 + j*8 .. +7 of row m*128 + h*32 + (p ^ 2b) of expert e.
+// A 128-row step is 8 KB of contiguous memory and so is each 32-row slice h of
+// it (2 KB), so a kernel can stream tiles of 32, 64 or 128 rows with one copy
+// per step; within block b of a slice the rows are permuted by flipping bits
+// 1-2 of the row index with b, so that a kernel reading rows g (+ 8i) of blocks
+// 0..3 at once (lane = (g, b)) hits 8 distinct shared-memory bank groups per
+// quarter warp, while the 32 rows of one block stay 32 consecutive 16-byte
+// chunks.
 // A stored 32-input
 // block is `bits` little-endian words with code i at bits [i*bits, i*bits+bits)
 // (hex_ref.pack, hex_ref.py:49-61): 4-bit words are already nibble-packed;
@@ -631,8 +634,8 @@ __global__ void tile_index_kernel(const uint32_t* __restrict__ idx, int bits, in
   const int64_t wpr = static_cast<int64_t>(cols_pad) / 32 * bits;
   for (int64_t o = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; o < total;
        o += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int j = static_cast<int>(o & 3), b = static_cast<int>((o >> 9) & 3);
-    const int r = static_cast<int>((o >> 2) & 127) ^ (2 * b);   // the row stored at this position
+    const int j = static_cast<int>(o & 3), b = static_cast<int>((o >> 7) & 3);
+    const int r = static_cast<int>(((o >> 9) & 3) * 32 + (((o >> 2) & 31) ^ (2 * b)));   // the row stored here
     const int64_t rest = o >> 11;
     const int s = static_cast<int>(rest % ksteps);
     const int64_t em = rest / ksteps;
@@ -681,19 +684,31 @@ __global__ void combine_kernel(const YT* __restrict__ y, int64_t T, int32_t k, i
     const int64_t t = i / hv;
     const int h8 = static_cast<int>(i % hv) * 8;
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int j = 0; j < k; ++j) {
-      int64_t r = t * k + j;
-      if (rows) {
-        r = __ldg(rows + r);
-        if (r < 0 || r >= y_rows) {
-          if (h8 == 0) atomicOr(&g_dev_err, kDevErrExpertId);
-          continue;
-        }
-      }
-      const uint4 v = *reinterpret_cast<const uint4*>(y + r * ld_y + h8);
-      const YT* e = reinterpret_cast<const YT*>(&v);
+    for (int j0 = 0; j0 < k; j0 += 8) {
+      // up to 8 rows loaded before the first is added (loads in flight together), added in slot order
+      uint4 v[8];
+      bool ok[8];
 #pragma unroll
-      for (int q = 0; q < 8; ++q) acc[q] += static_cast<float>(e[q]);
+      for (int u = 0; u < 8; ++u) {
+        const int j = j0 + u;
+        int64_t r = t * k + j;
+        ok[u] = j < k;
+        if (ok[u] && rows) {
+          r = __ldg(rows + r);
+          if (r < 0 || r >= y_rows) {
+            if (h8 == 0) atomicOr(&g_dev_err, kDevErrExpertId);
+            ok[u] = false;
+          }
+        }
+        v[u] = ok[u] ? *reinterpret_cast<const uint4*>(y + r * ld_y + h8) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (!ok[u]) continue;
+        const YT* e = reinterpret_cast<const YT*>(&v[u]);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc[q] += static_cast<float>(e[q]);
+      }
     }
     const int64_t o = t * H + h8;
     if (OUT == HEXMOE_F32) {

@@ -127,14 +127,14 @@ HEXMOE_API int hexmoe_layer_destroy(hexmoe_layer* layer);
 /* The tiled index layout the grouped GEMM reads.  idx: [n, rows_pad,
  * cols_pad/32*bits] u32, the stored HEX stream (hex_ref.pack,
  * hex_ref.py:49-61: per 32-input block `bits` little-endian words).  out:
- * [n, rows_pad/128, cols_pad/128, 4, 128, 4] u32 (n*rows_pad*cols_pad/2
- * bytes): for weight-row tile m, 128-input step s, 32-input block b of the
- * step and position p of the block, 4 words whose nibble i of word j holds
- * the code of input s*128 + b*32 + j*8 + i of tile row p ^ (2*b) (3-bit codes
- * with bit 3 clear; the row permutation spreads the shared-memory banks of the
- * kernels that read several blocks of one row at once).  One step of one tile
- * is 8 KB of contiguous memory.  rows_pad and cols_pad: multiples of 128.
- * Asynchronous on `stream`. */
+ * [n, rows_pad/128, cols_pad/128, 4, 4, 32, 4] u32 (n*rows_pad*cols_pad/2
+ * bytes): for weight-row tile m, 128-input step s, 32-row slice h, 32-input
+ * block b of the step and position p, 4 words whose nibble i of word j holds
+ * the code of input s*128 + b*32 + j*8 + i of tile row h*32 + (p ^ (2*b))
+ * (3-bit codes with bit 3 clear; the row permutation spreads the shared-memory
+ * banks of the kernels that read several blocks of one row at once).  One step
+ * of one tile is 8 KB of contiguous memory, each 32-row slice of it 2 KB.
+ * rows_pad and cols_pad: multiples of 128.  Asynchronous on `stream`. */
 HEXMOE_API int hexmoe_tile_index(const uint32_t* idx, int32_t bits, int32_t n, int32_t rows_pad,
                                  int32_t cols_pad, uint32_t* out, void* stream);
 

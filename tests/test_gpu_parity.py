@@ -51,12 +51,12 @@ def test_tile_index_layout_vs_oracle_codes(oracle, bits):
     _lib.check(_lib.lib.hexmoe_tile_index(idx.data_ptr(), bits, n, rows_pad, cols_pad, out.data_ptr(), None),
                "hexmoe_tile_index")
     torch.cuda.synchronize()
-    got = out.cpu().numpy().view(np.uint32).reshape(n, rows_pad // 128, cols_pad // 128, 4, 128, 4)
-    # nibble i of word j of (e, m, s, b, p) = code of input s*128 + b*32 + j*8 + i of row m*128 + (p ^ 2b)
-    c = codes.reshape(n, rows_pad // 128, 128, cols_pad // 128, 4, 4, 8).transpose(0, 1, 3, 4, 2, 5, 6)
+    got = out.cpu().numpy().view(np.uint32).reshape(n, rows_pad // 128, cols_pad // 128, 4, 4, 32, 4)
+    # nibble i of word j of (e, m, s, h, b, p) = code of input s*128 + b*32 + j*8 + i of row m*128 + h*32 + (p ^ 2b)
+    c = codes.reshape(n, rows_pad // 128, 4, 32, cols_pad // 128, 4, 4, 8).transpose(0, 1, 4, 2, 5, 3, 6, 7)
     want = np.bitwise_or.reduce(c.astype(np.uint32) << (4 * np.arange(8, dtype=np.uint32)), axis=-1)
-    perm = np.arange(128)[None, :] ^ (2 * np.arange(4)[:, None])        # [b, p] -> stored row
-    want = np.take_along_axis(want, perm[None, None, None, :, :, None], axis=4)
+    perm = np.arange(32)[None, :] ^ (2 * np.arange(4)[:, None])         # [b, p] -> stored row of the slice
+    want = np.take_along_axis(want, perm[None, None, None, None, :, :, None], axis=5)
     assert np.array_equal(got, want)
 
 
