@@ -27,6 +27,7 @@ EXPORTS = (
     "hexmoe_tile_index", "hexmoe_combine_rows", "hexmoe_forward_slots",
     "hexmoe_ep_init", "hexmoe_ep_handle", "hexmoe_ep_connect", "hexmoe_ep_workspace_bytes", "hexmoe_ep_dispatch",
     "hexmoe_ep_experts", "hexmoe_ep_combine", "hexmoe_ep_forward", "hexmoe_ep_destroy",
+    "hexmoe_quantize_workspace_bytes", "hexmoe_quantize",
 )
 EP_MAX_WORLD = 8          # HEXMOE_EP_MAX_WORLD
 EP_HANDLE_BYTES = 64      # HEXMOE_EP_HANDLE_BYTES
@@ -85,6 +86,8 @@ def _load() -> ctypes.CDLL:
         "hexmoe_ep_combine": (ctypes.c_int, [P, I64_, P, I32_, P]),
         "hexmoe_ep_forward": (ctypes.c_int, [P, P, P, I32_, I64_, P, P, I32_, P, I32_, I32_, P, SZ, P]),
         "hexmoe_ep_destroy": (ctypes.c_int, [P]),
+        "hexmoe_quantize_workspace_bytes": (SZ, [I32_, I32_, I32_, I32_, I64_, I32_]),
+        "hexmoe_quantize": (ctypes.c_int, [P, I32_, I32_, I32_, I32_, I32_, P, P, I64_, I32_, P, P, P, P, P, SZ, P]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
