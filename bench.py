@@ -24,7 +24,9 @@ kernel, the gate/up grouped GEMM of the 1-GPU layer, timed alone (tensor-bound).
 Other objects of the line: `decode` (cfg2: all-3-bit, T = 64 with the decode
 roofline against HBM, and the 1/8/32/64 sweep), `prefill_T16384` (cfg3 at
 16384 tokens on one GPU), `cfg4_slice` (one GPU's share of cfg4 at 8 GPUs: 16
-experts of H=4096, I=1536, 1024 tokens routed over them); at N>1 `ep` (per-phase
+experts of H=4096, I=1536, 1024 tokens routed over them), `quantize` (the GPU
+HEX quantizer on 96 matrices of 768 x 2048 against the numpy restatement of the
+reference's quantize on one); at N>1 `ep` (per-phase
 times, per-rank expert time, and a bit-exactness check of rank 0's output),
 `cfg4_ep` and `cfg5_ep` (cfg4: 128 experts of H=4096, 8192 tokens over the
 GPUs, 16 experts per GPU at N=8; cfg5: Zipf-skewed routing, 32768 tokens over
@@ -370,6 +372,32 @@ def cfg4_slice(dev, steps: int, flush, stream, pk) -> dict:
             "tokens_per_s": T4 / (t * 1e-3), "ms": t, "TFLOPs": fl / t / 1e9, "bf16_frac": fl / t / 1e9 / pk["bf16_tflops"]}
 
 
+def quantize_block(dev, steps: int, flush, stream, pk) -> dict:
+    """The GPU HEX quantizer (hexmoe_quantize) on a stack shaped as cfg2's gate
+    projections (96 experts of 768 x 2048, 8 levels, 128-input scale blocks,
+    the reference's 2^17-value fit sample), against the reference algorithm
+    restated in numpy (oracle/hexquant.py) on one of the matrices."""
+    import torch
+
+    import hexquant
+    from blackhole_b200.quant import quantize_stack
+    g = torch.Generator(device="cpu").manual_seed(81)
+    W = (torch.randn(E, I, H, generator=g) * 0.02).to(dev)
+    quantize_stack(W[:2], 8, BLOCK)                     # warm-up (and the cub sort's first launch)
+    torch.cuda.synchronize()
+    ms = time_steps(lambda: quantize_stack(W, 8, BLOCK), max(3, steps // 4), flush, stream)
+    t = sum(ms) / len(ms)
+    w0 = W[0].cpu().numpy()
+    t0 = time.perf_counter()
+    hexquant.quantize(w0, 8, BLOCK)
+    cpu_s = time.perf_counter() - t0
+    nbytes = W.numel() * 4
+    return {"workload": f"quantize {E} matrices of {I}x{H} (cfg2 gate projections), 8 levels, fp8 block-{BLOCK} scales, "
+                        "k-means on the reference's 2^17-value sample, 20 iterations",
+            "ms": t, "matrices_per_s": E / (t * 1e-3), "input_GBps": nbytes / t / 1e6,
+            "cpu_numpy_s_per_matrix": cpu_s, "cpu_numpy_matrices_per_s": 1.0 / cpu_s}
+
+
 def read_traffic(key: str):
     """DRAM bytes per launch of a kernel from the committed ncu summary, if any."""
     p = ROOT / "profiles" / "traffic.json"
@@ -682,6 +710,10 @@ def main() -> None:
             extras["decode"] = decode_block(dev, max(args.steps, 10), flush, stream, pk)
             extras["prefill_T16384"] = prefill_one_gpu(dev, layer, 16384, max(5, args.steps // 2), flush, stream, pk)
             extras["cfg4_slice"] = cfg4_slice(dev, max(5, args.steps // 2), flush, stream, pk)
+            try:
+                extras["quantize"] = quantize_block(dev, args.steps, flush, stream, pk)
+            except Exception as e:  # noqa: BLE001  (reported, not required)
+                extras["quantize"] = {"error": f"{type(e).__name__}: {e}"}
             torch.cuda.empty_cache()
             try:
                 extras["cpu_baseline"] = cpu_baseline()

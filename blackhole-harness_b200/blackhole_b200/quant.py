@@ -31,6 +31,18 @@ def sample_positions(size: int, seed: int = 0, sample: int = SAMPLE) -> np.ndarr
     return np.random.default_rng(seed).integers(0, size, sample)
 
 
+_SAMPLES: dict = {}
+
+
+def _sample_on(size: int, dev) -> torch.Tensor | None:
+    """sample_positions(size) on `dev`, drawn once per (size, device)."""
+    key = (size, str(dev))
+    if key not in _SAMPLES:
+        pos = sample_positions(size)
+        _SAMPLES[key] = torch.as_tensor(pos, dtype=torch.int64, device=dev) if pos is not None else None
+    return _SAMPLES[key]
+
+
 def quantize_stack(W: torch.Tensor, levels: int = 8, block: int = 32, energy: torch.Tensor | None = None,
                    iters: int = ITERS) -> dict:
     """HEX-quantize every matrix of W [n, out, in] (CUDA, cast to f32) as the
@@ -57,8 +69,7 @@ def quantize_stack(W: torch.Tensor, levels: int = 8, block: int = 32, energy: to
         en = (en.expand(n, cols) if en.dim() == 1 else en).contiguous()
         if en.shape != (n, cols):
             raise ValueError(f"energy must be [in] or [n, in], got {tuple(energy.shape)}")
-    pos = sample_positions(out * cols)
-    sidx = torch.as_tensor(pos, dtype=torch.int64, device=dev) if pos is not None else None
+    sidx = _sample_on(out * cols, dev)
     ns = 0 if sidx is None else sidx.numel()
     bits = 3 if levels == 8 else 4
     idx = torch.empty(n, out, cols // 32 * bits, dtype=torch.int32, device=dev)
