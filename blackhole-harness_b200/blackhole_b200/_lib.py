@@ -86,8 +86,9 @@ def _load() -> ctypes.CDLL:
         "hexmoe_ep_combine": (ctypes.c_int, [P, I64_, P, I32_, P]),
         "hexmoe_ep_forward": (ctypes.c_int, [P, P, P, I32_, I64_, P, P, I32_, P, I32_, I32_, P, SZ, P]),
         "hexmoe_ep_destroy": (ctypes.c_int, [P]),
-        "hexmoe_quantize_workspace_bytes": (SZ, [I32_, I32_, I32_, I32_, I64_, I32_]),
-        "hexmoe_quantize": (ctypes.c_int, [P, I32_, I32_, I32_, I32_, I32_, P, P, I64_, I32_, P, P, P, P, P, SZ, P]),
+        "hexmoe_quantize_workspace_bytes": (SZ, [I32_, I32_, I32_, I32_, I64_, I32_, I32_]),
+        "hexmoe_quantize": (ctypes.c_int, [P, I32_, I32_, I32_, I32_, I32_, P, P, I64_, I32_, P, P, P, P, P, P, P, SZ,
+                                           P]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)

@@ -270,14 +270,153 @@ __global__ void quant_pack_kernel(const float* __restrict__ W, int n, int out, i
   }
 }
 
+// GPTQ onto the table (gptq_table, hex.py:256-282): one CTA per (matrix, 128
+// rows), one thread per row (rows never interact: the sweep couples columns
+// only).  Per 128-column block: the rows' current values and the block of U
+// (the upper Cholesky factor of the damped inverse Hessian) in shared memory;
+// columns in order, each rounded onto levels x scale (nearest level of the
+// clipped scaled value), its error e = (w - q) / U[j, j] spread over the
+// block's later columns (w -= e U[j, :]) and kept in place of the column; then
+// the later columns of the matrix take the block's errors at once
+// (W[:, b1:] -= E U[b0:b1, b1:], an FP32 product over shared-memory panels of
+// U).  The codes chosen are the GPTQ indices (nearest(Q / scale) of the
+// reference gives back the same level).  W_work: the matrix with dead inputs
+// zeroed, updated in place.
+constexpr int kGptqRows = 128;
+constexpr int kGptqCols = 128;
+constexpr int kGptqPitch = kGptqCols + 1;   // row pitch of the rows' block (floats): conflict-free per-thread rows
+
+__global__ void gptq_init_kernel(const float* __restrict__ W, const uint8_t* __restrict__ dead, int n, int out, int in,
+                                 float* __restrict__ Ww) {
+  const int64_t total = static_cast<int64_t>(n) * out * in;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t e = i / (static_cast<int64_t>(out) * in);
+    const int col = static_cast<int>(i % in);
+    Ww[i] = __ldg(dead + e * in + col) ? 0.0f : __ldg(W + i);
+  }
+}
+
+__global__ void __launch_bounds__(kGptqRows) gptq_kernel(float* __restrict__ Ww, const float* __restrict__ U,
+                                                         const uint8_t* __restrict__ dead,
+                                                         const float* __restrict__ blk,
+                                                         const float* __restrict__ levels, int out, int in, int block,
+                                                         int L, uint8_t* __restrict__ codes) {
+  extern __shared__ float gsm[];
+  float* rows = gsm;                                   // [kGptqRows][kGptqPitch]: values, then errors
+  float* ub = gsm + kGptqRows * kGptqPitch;            // [kGptqCols][kGptqCols]: U block, then U panels
+  __shared__ float lv[16], mids[16];
+  const int e = blockIdx.y;
+  const int r0 = blockIdx.x * kGptqRows;
+  const int t = threadIdx.x;
+  const int row = r0 + t;
+  const bool live_row = row < out;
+  if (t < L) lv[t] = __ldg(levels + static_cast<int64_t>(e) * L + t);
+  __syncthreads();
+  if (t < L - 1) mids[t] = __fdiv_rn(__fadd_rn(lv[t + 1], lv[t]), 2.0f);
+  float* wrow = Ww + (static_cast<int64_t>(e) * out + (live_row ? row : 0)) * in;
+  const float* ue = U + static_cast<int64_t>(e) * in * in;
+  const float* srow = blk + (static_cast<int64_t>(e) * out + (live_row ? row : 0)) * (in / block);
+  uint8_t* crow = codes + (static_cast<int64_t>(e) * out + (live_row ? row : 0)) * in;
+  float* my = rows + t * kGptqPitch;
+  for (int b0 = 0; b0 < in; b0 += kGptqCols) {
+    const int bw = min(kGptqCols, in - b0);
+    __syncthreads();
+    for (int i = t; i < kGptqCols * kGptqCols; i += blockDim.x) {
+      const int j = i / kGptqCols, c = i - j * kGptqCols;
+      ub[i] = (j < bw && c < bw) ? __ldg(ue + static_cast<int64_t>(b0 + j) * in + b0 + c) : 0.0f;
+    }
+    for (int c = 0; c < bw; ++c) my[c] = live_row ? wrow[b0 + c] : 0.0f;
+    __syncthreads();
+    // the block's columns in order (each thread its own row)
+    for (int j = 0; j < bw; ++j) {
+      const float w = my[j];
+      const float s = __ldg(srow + (b0 + j) / block);
+      const float x = fminf(fmaxf(__fdiv_rn(w, s), -1.0f), 1.0f);
+      int k = 0;
+      for (int l = 0; l < L - 1; ++l) k += mids[l] < x ? 1 : 0;
+      const float q = __fmul_rn(lv[k], s);
+      const float err = __fdiv_rn(__fadd_rn(w, -q), ub[j * kGptqCols + j]);
+      if (live_row) crow[b0 + j] = static_cast<uint8_t>(k);
+      my[j] = err;
+      const float* uj = ub + j * kGptqCols;
+      for (int c = j + 1; c < bw; ++c) my[c] = __fmaf_rn(-err, uj[c], my[c]);
+    }
+    // the later columns: W[row, c] -= sum_j E[row, j] U[b0 + j, c], panels of 128 columns
+    for (int p0 = b0 + bw; p0 < in; p0 += kGptqCols) {
+      const int pw = min(kGptqCols, in - p0);
+      __syncthreads();
+      for (int i = t; i < kGptqCols * kGptqCols; i += blockDim.x) {
+        const int j = i / kGptqCols, c = i - j * kGptqCols;
+        ub[i] = (j < bw && c < pw) ? __ldg(ue + static_cast<int64_t>(b0 + j) * in + p0 + c) : 0.0f;
+      }
+      __syncthreads();
+      for (int c0 = 0; c0 < pw; c0 += 32) {
+        float acc[32];
+#pragma unroll
+        for (int c = 0; c < 32; ++c) acc[c] = 0.0f;
+        for (int j = 0; j < bw; ++j) {
+          const float ej = my[j];
+          const float4* u4 = reinterpret_cast<const float4*>(ub + j * kGptqCols + c0);
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const float4 v = u4[c];
+            acc[4 * c] = __fmaf_rn(ej, v.x, acc[4 * c]);
+            acc[4 * c + 1] = __fmaf_rn(ej, v.y, acc[4 * c + 1]);
+            acc[4 * c + 2] = __fmaf_rn(ej, v.z, acc[4 * c + 2]);
+            acc[4 * c + 3] = __fmaf_rn(ej, v.w, acc[4 * c + 3]);
+          }
+        }
+        if (live_row) {
+#pragma unroll
+          for (int c = 0; c < 32; ++c)
+            if (c0 + c < pw) wrow[p0 + c0 + c] = __fadd_rn(wrow[p0 + c0 + c], -acc[c]);
+        }
+      }
+    }
+  }
+  // dead inputs: Q = 0 there, so the nearest level of 0
+  __syncthreads();
+  if (live_row) {
+    int k0 = 0;
+    for (int l = 0; l < L - 1; ++l) k0 += mids[l] < 0.0f ? 1 : 0;
+    const uint8_t* de = dead + static_cast<int64_t>(e) * in;
+    for (int c = 0; c < in; ++c)
+      if (__ldg(de + c)) crow[c] = static_cast<uint8_t>(k0);
+  }
+}
+
+// Pack chosen codes u8 [n, out, in] as the layout's bit stream.
+__global__ void quant_pack_codes_kernel(const uint8_t* __restrict__ codes, int64_t rows, int in, int bits,
+                                        uint32_t* __restrict__ idx_out) {
+  const int n32 = in / 32;
+  const int64_t total = rows * n32;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / n32;
+    const int c0 = static_cast<int>(i - r * n32) * 32;
+    uint32_t words[4] = {0u, 0u, 0u, 0u};
+    for (int j = 0; j < 32; ++j) {
+      const uint32_t a = __ldg(codes + r * in + c0 + j);
+      const int off = j * bits, wi = off >> 5, sh = off & 31;
+      words[wi] |= a << sh;
+      if (sh + bits > 32) words[wi + 1] |= a >> (32 - sh);
+    }
+    uint32_t* dst = idx_out + r * (n32 * bits) + static_cast<int64_t>(c0 / 32) * bits;
+    for (int k = 0; k < bits; ++k) dst[k] = words[k];
+  }
+}
+
+constexpr size_t kGptqSmem = sizeof(float) * (kGptqRows * kGptqPitch + kGptqCols * kGptqCols);
+
 struct QuantLayout {
-  size_t blk, xs, ws, sorted, off, temp, temp_bytes, total;
+  size_t blk, xs, ws, sorted, off, temp, temp_bytes, gw, gcodes, total;
   int64_t ns;
 };
 
 size_t up256(size_t v) { return (v + 255) / 256 * 256; }
 
-QuantLayout quant_layout(int n, int out, int in, int block, int64_t sample, bool weighted) {
+QuantLayout quant_layout(int n, int out, int in, int block, int64_t sample, bool weighted, bool gptq) {
   QuantLayout q{};
   const int64_t size = static_cast<int64_t>(out) * in;
   q.ns = sample > 0 && sample < size ? sample : size;
@@ -292,6 +431,9 @@ QuantLayout quant_layout(int n, int out, int in, int block, int64_t sample, bool
                                           static_cast<int>(n * q.ns), n, static_cast<const int*>(nullptr),
                                           static_cast<const int*>(nullptr) + 1);
   q.temp = off; q.temp_bytes = tb; off = up256(off + tb);
+  const size_t nw = gptq ? static_cast<size_t>(n) * out * in : 0;
+  q.gw = off; off = up256(off + sizeof(float) * nw);
+  q.gcodes = off; off = up256(off + nw);
   q.total = off;
   return q;
 }
@@ -309,16 +451,17 @@ using namespace hexmoe;
 extern "C" {
 
 size_t hexmoe_quantize_workspace_bytes(int32_t n, int32_t out, int32_t in, int32_t block, int64_t sample,
-                                       int32_t weighted) {
+                                       int32_t weighted, int32_t gptq) {
   if (n <= 0 || out <= 0 || in <= 0 || (block != 32 && block != 128) || in % block) return 0;
   if (static_cast<int64_t>(n) * (sample > 0 ? sample : static_cast<int64_t>(out) * in) >= (1ll << 31)) return 0;
-  return quant_layout(n, out, in, block, sample, weighted != 0).total;
+  return quant_layout(n, out, in, block, sample, weighted != 0, gptq != 0).total;
 }
 
 int hexmoe_quantize(const float* W, int32_t n, int32_t out, int32_t in, int32_t levels, int32_t block,
-                    const float* energy, const int64_t* sample_idx, int64_t sample, int32_t iters, uint32_t* idx_out,
-                    uint8_t* block_scale_out, float* expert_scale_out, float* levels_out, void* workspace,
-                    size_t workspace_bytes, void* stream) {
+                    const float* energy, const int64_t* sample_idx, int64_t sample, int32_t iters,
+                    const float* hinv_u, const uint8_t* dead, uint32_t* idx_out, uint8_t* block_scale_out,
+                    float* expert_scale_out, float* levels_out, void* workspace, size_t workspace_bytes,
+                    void* stream) {
   if (n <= 0 || out <= 0 || in <= 0) return report_error(HEXMOE_E_ARG, "hexmoe_quantize: n, out and in must be positive");
   if (levels != 8 && levels != 16) return report_error(HEXMOE_E_ARG, "hexmoe_quantize: levels must be 8 or 16");
   if (block != 32 && block != 128) return report_error(HEXMOE_E_ARG, "hexmoe_quantize: block must be 32 or 128");
@@ -334,7 +477,9 @@ int hexmoe_quantize(const float* W, int32_t n, int32_t out, int32_t in, int32_t 
     return report_error(HEXMOE_E_ARG, "hexmoe_quantize: null pointer");
   if (reinterpret_cast<uintptr_t>(W) % 16 || reinterpret_cast<uintptr_t>(workspace) % 256)
     return report_error(HEXMOE_E_ARG, "hexmoe_quantize: W must be 16-byte and workspace 256-byte aligned");
-  const QuantLayout q = quant_layout(n, out, in, block, sample, energy != nullptr);
+  if ((hinv_u == nullptr) != (dead == nullptr))
+    return report_error(HEXMOE_E_ARG, "hexmoe_quantize: hinv_u and dead go together");
+  const QuantLayout q = quant_layout(n, out, in, block, sample, energy != nullptr, hinv_u != nullptr);
   if (workspace_bytes < q.total) return report_error(HEXMOE_E_ARG, "hexmoe_quantize: workspace too small");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   char* ws = static_cast<char*>(workspace);
@@ -356,7 +501,19 @@ int hexmoe_quantize(const float* W, int32_t n, int32_t out, int32_t in, int32_t 
   if (e != cudaSuccess) return report_cuda_error(e, "hexmoe_quantize: sample sort");
   quant_fit_kernel<<<n, kFitThreads, 0, st>>>(xs, wts, sorted, q.ns, levels, iters, levels_out);
   const int64_t np32 = static_cast<int64_t>(n) * out * (in / 32);
-  quant_pack_kernel<<<grid_for(np32, 128), 128, 0, st>>>(W, n, out, in, block, blk, levels_out, bits, idx_out);
+  if (!hinv_u) {
+    quant_pack_kernel<<<grid_for(np32, 128), 128, 0, st>>>(W, n, out, in, block, blk, levels_out, bits, idx_out);
+  } else {
+    float* gw = reinterpret_cast<float*>(ws + q.gw);
+    uint8_t* gcodes = reinterpret_cast<uint8_t*>(ws + q.gcodes);
+    gptq_init_kernel<<<grid_for(static_cast<int64_t>(n) * out * in, 256), 256, 0, st>>>(W, dead, n, out, in, gw);
+    e = cudaFuncSetAttribute(gptq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kGptqSmem));
+    if (e != cudaSuccess) return report_cuda_error(e, "hexmoe_quantize: GPTQ shared memory");
+    gptq_kernel<<<dim3((out + kGptqRows - 1) / kGptqRows, n), kGptqRows, kGptqSmem, st>>>(
+        gw, hinv_u, dead, blk, levels_out, out, in, block, levels, gcodes);
+    quant_pack_codes_kernel<<<grid_for(np32, 128), 128, 0, st>>>(gcodes, static_cast<int64_t>(n) * out, in, bits,
+                                                                 idx_out);
+  }
   e = cudaGetLastError();
   if (e != cudaSuccess) return report_cuda_error(e, "hexmoe_quantize: launch");
   return HEXMOE_OK;

@@ -326,26 +326,32 @@ HEXMOE_API int hexmoe_route_topk(const void* logits, int32_t logits_dtype, int64
                       float* topk_weights, int32_t* topk_ids, void* stream);
 
 /* ---- The quantizer: the producer side of the HEX format.
- * Replaces blackhole/anatomy/hex.py:207-227 `quantize(W, L, block, energy)`
- * (without a Hessian: block_scales 60-70, fit_table 73-90, nearest 93-95,
- * pack_bits 136-150), batched over a stack of n matrices and equal to it bit for
- * bit.  W [n, out, in] f32 (16-byte aligned), in a multiple of `block` (32 or
- * 128); levels 8 or 16.  energy (optional) [n, in] f32: the per-input mean x^2
- * that weights the table fit by energy * block_scale^2.  sample_idx (optional)
- * [sample] int64 flat positions in [out, in]: the values the table is fitted
- * on (the reference draws 2^17 of them with numpy default_rng(0) when a matrix
- * has more); null fits every value.  iters: Lloyd iterations (20 in the
- * reference).  Outputs, in the layout of one tier's projection: idx_out [n,
- * out, in/32*bits] u32, block_scale_out [n, out, in/block] u8 (fp8 e4m3
- * codes), expert_scale_out [n] f32, levels_out [n, levels] f32.  Workspace:
- * hexmoe_quantize_workspace_bytes (256-byte aligned).  Asynchronous on
+ * Replaces blackhole/anatomy/hex.py:207-227 `quantize(W, L, block, energy, H)`
+ * (block_scales 60-70, fit_table 73-90, nearest 93-95, GPTQ onto the table
+ * gptq_table 256-282, pack_bits 136-150), batched over a stack of n matrices.
+ * Without a Hessian it equals the reference bit for bit.  W [n, out, in] f32
+ * (16-byte aligned), in a multiple of `block` (32 or 128); levels 8 or 16.
+ * energy (optional) [n, in] f32: the per-input mean x^2 that weights the table
+ * fit by energy * block_scale^2.  sample_idx (optional) [sample] int64 flat
+ * positions in [out, in]: the values the table is fitted on (the reference
+ * draws 2^17 of them with numpy default_rng(0) when a matrix has more); null
+ * fits every value.  iters: Lloyd iterations (20 in the reference).
+ * hinv_u / dead (optional, together): GPTQ rounding instead of nearest, with
+ * hinv_u [n, in, in] f32 the upper Cholesky factor of each matrix's damped
+ * inverse Hessian and dead [n, in] u8 its dead inputs (hex.py:234-253 prepares
+ * both from H; blackhole_b200.quant does it on the device).  Outputs, in the
+ * layout of one tier's projection: idx_out [n, out, in/32*bits] u32,
+ * block_scale_out [n, out, in/block] u8 (fp8 e4m3 codes), expert_scale_out [n]
+ * f32, levels_out [n, levels] f32.  Workspace: hexmoe_quantize_workspace_bytes
+ * (256-byte aligned; gptq != 0 when hinv_u is given).  Asynchronous on
  * `stream`. */
 HEXMOE_API size_t hexmoe_quantize_workspace_bytes(int32_t n, int32_t out, int32_t in, int32_t block,
-                                                  int64_t sample, int32_t weighted);
+                                                  int64_t sample, int32_t weighted, int32_t gptq);
 HEXMOE_API int hexmoe_quantize(const float* W, int32_t n, int32_t out, int32_t in, int32_t levels, int32_t block,
                                const float* energy, const int64_t* sample_idx, int64_t sample, int32_t iters,
-                               uint32_t* idx_out, uint8_t* block_scale_out, float* expert_scale_out,
-                               float* levels_out, void* workspace, size_t workspace_bytes, void* stream);
+                               const float* hinv_u, const uint8_t* dead, uint32_t* idx_out,
+                               uint8_t* block_scale_out, float* expert_scale_out, float* levels_out,
+                               void* workspace, size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

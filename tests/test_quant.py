@@ -60,13 +60,11 @@ def test_fp8_encode_rule():
 def test_quantize_argument_errors_before_any_device_work():
     from blackhole_b200 import _lib
     L = _lib.lib
-    assert L.hexmoe_quantize(None, 1, 8, 64, 5, 32, None, None, 0, 20, None, None, None, None, None, 0, None) == \
-        _lib.HEXMOE_E_ARG                                                      # levels
-    assert L.hexmoe_quantize(None, 1, 8, 96, 8, 128, None, None, 0, 20, None, None, None, None, None, 0, None) == \
-        _lib.HEXMOE_E_ARG                                                      # in % block
-    assert L.hexmoe_quantize(None, 1, 8, 64, 8, 32, None, None, 0, 20, None, None, None, None, None, 0, None) == \
-        _lib.HEXMOE_E_ARG                                                      # null pointers
-    assert L.hexmoe_quantize_workspace_bytes(1, 8, 96, 128, 0, 0) == 0     # in % block
+    A = (None, None, 0, 20, None, None, None, None, None, None, None, 0, None)
+    assert L.hexmoe_quantize(None, 1, 8, 64, 5, 32, *A) == _lib.HEXMOE_E_ARG     # levels
+    assert L.hexmoe_quantize(None, 1, 8, 96, 8, 128, *A) == _lib.HEXMOE_E_ARG    # in % block
+    assert L.hexmoe_quantize(None, 1, 8, 64, 8, 32, *A) == _lib.HEXMOE_E_ARG     # null pointers
+    assert L.hexmoe_quantize_workspace_bytes(1, 8, 96, 128, 0, 0, 0) == 0       # in % block
 
 
 @pytest.mark.gpu
@@ -130,3 +128,65 @@ def test_quantized_parts_dequantize_to_the_restatement():
         want = lev[idx] * np.repeat(s, block, axis=1)
         got = outw[e].cpu().numpy()
         assert np.array_equal(got.view(np.uint32), want.astype(np.float32).view(np.uint32)), e
+
+
+def _q_from(idx: np.ndarray, lev: np.ndarray, codes: np.ndarray, es: float, block: int) -> np.ndarray:
+    s = hexquant.FP8[codes].astype(np.float32) * np.float32(es)
+    return lev[idx] * np.repeat(s, block, axis=1)
+
+
+def test_gptq_restatement_matches_reference_golden():
+    from quant_cases import GPTQ_CASES, gptq_inputs
+    z = golden("quant.npz")
+    for name, (seed, out, n, L, block, rows) in GPTQ_CASES.items():
+        W, H = gptq_inputs(seed, out, n, rows)
+        assert hashlib.sha256(W.tobytes() + H.tobytes()).digest() == z[f"{name}/sha256"].tobytes()
+        lev, es, codes, idx = hexquant.quantize(W, L, block, H=H)
+        assert np.array_equal(lev, z[f"{name}/levels"]) and np.array_equal(codes, z[f"{name}/block_scale"])
+        assert np.array_equal(idx, z[f"{name}/codes"]), name
+
+
+@pytest.mark.gpu
+def test_gptq_matches_reference():
+    """GPTQ onto the table on the GPU against the reference's outputs: the table
+    and block scales (which GPTQ does not touch) bit for bit; the indices, whose
+    error feedback sums in float32 in another order than the reference's, agree
+    on at least 99 % of the weights, and the GPTQ objective trace((W-Q) H (W-Q)^T)
+    is within 1 % of the reference's and below nearest rounding's."""
+    from quant_cases import GPTQ_CASES, gptq_inputs
+
+    from blackhole_b200.quant import quantize
+    z = golden("quant.npz")
+    for name, (seed, out, n, L, block, rows) in GPTQ_CASES.items():
+        W, H = gptq_inputs(seed, out, n, rows)
+        got = quantize(torch.from_numpy(W).to(DEV), L, block, H=torch.from_numpy(H).to(DEV))
+        torch.cuda.synchronize()
+        lev = got["levels"].cpu().numpy()
+        codes = got["block_scale"].cpu().numpy()
+        es = got["expert_scale"].cpu().numpy()[0]
+        assert np.array_equal(lev, z[f"{name}/levels"]) and np.array_equal(codes, z[f"{name}/block_scale"]), name
+        bits = int(np.log2(L))
+        words = got["idx"].view(torch.int32).cpu().numpy().view(np.uint32)
+        mine = _unpack(words, bits, n)
+        ref = z[f"{name}/codes"]
+        agree = float((mine == ref).mean())
+        assert agree >= 0.99, (name, agree)
+        e_mine = hexquant.gptq_error(W, _q_from(mine, lev, codes, es, block), H)
+        e_ref = hexquant.gptq_error(W, _q_from(ref, lev, codes, es, block), H)
+        _, _, _, near = hexquant.quantize(W, L, block)
+        e_near = hexquant.gptq_error(W, _q_from(near, lev, codes, es, block), H)
+        assert abs(e_mine - e_ref) <= 0.01 * e_ref and e_mine < e_near, (name, e_mine, e_ref, e_near)
+
+
+def _unpack(words: np.ndarray, bits: int, n: int) -> np.ndarray:
+    out = words.shape[0]
+    w = words.reshape(out, -1, bits).astype(np.uint64)
+    vals = []
+    for i in range(32):
+        off = i * bits
+        wi, sh = off // 32, off % 32
+        v = w[:, :, wi] >> np.uint64(sh)
+        if sh + bits > 32:
+            v |= w[:, :, wi + 1] << np.uint64(32 - sh)
+        vals.append(v & np.uint64((1 << bits) - 1))
+    return np.stack(vals, -1).reshape(out, -1)[:, :n].astype(np.uint8)
