@@ -151,7 +151,8 @@ int plan_gemm(GemmParams& p, bool glu, int bm, int k_pad, int block) {
   const int nproj = glu ? 2 : 1;
   const uint32_t spr = static_cast<uint32_t>(k_pad / block);
   p.sz_scale = static_cast<uint32_t>(align_up(128u * spr, 1024));
-  p.off_tab = 8192;                                    // after control block, fp8 table, tile records
+  p.off_tab = glu ? 8192 : 8192 + 2048;                // after control block, fp8 table, tile records (+ down's
+                                                       // 2 KB epilogue staging)
   p.off_scale = static_cast<uint32_t>(align_up(p.off_tab + 2u * nproj * 512u * 16u, 1024));
   p.off_idx = static_cast<uint32_t>(align_up(p.off_scale + 2u * nproj * p.sz_scale, 1024));
   p.sz_b = static_cast<uint32_t>(align_up(2u * bm * 128u, 1024));
@@ -666,6 +667,7 @@ int hexmoe_down(const hexmoe_layer* layer, const void* act, int32_t act_dtype, i
   if (tokens == 0) return HEXMOE_OK;
   if (!act || !topk_weights || !sorted_ids || !expert_ids || !npp || !y)
     return fail(HEXMOE_E_ARG, "hexmoe_down: null pointer");
+  if (reinterpret_cast<uintptr_t>(y) % 16) return fail(HEXMOE_E_ARG, "hexmoe_down: y must be 16-byte aligned");
   int32_t* dev_err = device_error_word();
   if (!dev_err) return fail(HEXMOE_E_CUDA, "device error word unavailable");
   return run_down(layer, act, act_dtype == HEXMOE_BF16, tokens, topk, topk_weights, sorted_ids, expert_ids, npp,

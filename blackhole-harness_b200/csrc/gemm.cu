@@ -78,6 +78,7 @@ struct TileRec {
   uint8_t pad_to_1280[1280 - 40 - 128 - 1024];
 };
 static_assert(sizeof(TileRec) == 1280 && kOffRec + kRecs * 1280 <= 8192, "tile records");
+constexpr uint32_t kOffStage = 8192;  // down epilogue: per warp 8 tokens x 32 rows of 16-bit outputs (4 x 512 B)
 
 struct TileInfo {
   int32_t b, m, tier, local, bits;
@@ -421,10 +422,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
       if (!mbar_wait_idle(&c->t_full[ab], (acc_it / p.nbuf) & 1, abort_flag, p.dev_err)) break;
       ++acc_it;
       tc_fence_after();
-      // Lanes pair up on adjacent outputs (o, o + 1): one shuffle per two values,
-      // then each lane stores one packed pair, the even lane for token n and the
-      // odd lane for token n + 1.  Down reads the block's slot ids and top-k
-      // weights from the tile record (the same address for the whole warp).
+      // gate/up: lanes pair up on adjacent outputs (o, o + 1): one shuffle per two
+      // values, then each lane stores one packed pair, the even lane for token n
+      // and the odd lane for token n + 1.  Down (whose per-slot rows are the
+      // larger write, scattered over the slots): the warp's 32 rows of 8 tokens
+      // go through a 512-byte staging tile in shared memory, and each lane stores
+      // 8 consecutive outputs of one token as one 16-byte vector.  Down reads the
+      // block's slot ids and top-k weights from the tile record (the same
+      // address for the whole warp).
       const bool odd = lane & 1;
       const int o_pair = m * 128 + row - (odd ? 1 : 0);
       const bool store_pair = o_pair < p.rows_store;          // rows_store is even
@@ -463,15 +468,34 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
             v[j] = __uint_as_float(g[j]) * recs[ri].w[n0 + j];
           }
         }
+        if constexpr (GLU) {
 #pragma unroll
-        for (int j = 0; j < 16; j += 2) {
-          const float keep = odd ? v[j + 1] : v[j];
-          const float other = __shfl_xor_sync(0xffffffffu, odd ? v[j] : v[j + 1], 1);
-          const int n = n0 + j + (odd ? 1 : 0);
-          if (n < cnt && store_pair) {
-            const size_t orow = GLU ? static_cast<size_t>(b) * p.bm + n : static_cast<size_t>(recs[ri].slot[n]);
-            *reinterpret_cast<uint32_t*>(out16 + orow * p.ld_out + o_pair) =
-                odd ? pack2<BF16>(other, keep) : pack2<BF16>(keep, other);
+          for (int j = 0; j < 16; j += 2) {
+            const float keep = odd ? v[j + 1] : v[j];
+            const float other = __shfl_xor_sync(0xffffffffu, odd ? v[j] : v[j + 1], 1);
+            const int n = n0 + j + (odd ? 1 : 0);
+            if (n < cnt && store_pair) {
+              const size_t orow = static_cast<size_t>(b) * p.bm + n;
+              *reinterpret_cast<uint32_t*>(out16 + orow * p.ld_out + o_pair) =
+                  odd ? pack2<BF16>(other, keep) : pack2<BF16>(keep, other);
+            }
+          }
+        } else {
+          uint16_t* stg = reinterpret_cast<uint16_t*>(smem + kOffStage) + (warp - 2) * 256;   // [8 tokens][32 rows]
+          const int tok = lane >> 2, part = lane & 3;
+          const int o8 = m * 128 + q * 32 + part * 8;                   // this lane's 8 outputs (rows_store % 8 == 0)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            __syncwarp();
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj)
+              stg[jj * 32 + lane] = static_cast<uint16_t>(pack2<BF16>(v[8 * h + jj], 0.f) & 0xFFFFu);
+            __syncwarp();
+            const int n = n0 + 8 * h + tok;
+            if (n < cnt && o8 < p.rows_store) {
+              const uint4 val = *reinterpret_cast<const uint4*>(stg + tok * 32 + part * 8);
+              *reinterpret_cast<uint4*>(out16 + static_cast<size_t>(recs[ri].slot[n]) * p.ld_out + o8) = val;
+            }
           }
         }
       }
