@@ -13,17 +13,17 @@ Forward for the T tokens of this rank (global expert ids in topk_ids):
   2. experts: each rank runs its experts on the received slots, one slot per
      row at top-1, giving w * down(silu(gate x) * up x) rounded to the row
      dtype per slot, exactly as the single-GPU layer rounds each slot;
-  3. return: per received row, the fp32 sum of its slots in j order, rounded
-     once to the row dtype, goes back to the row's source rank;
-  4. combine: out[t] = the returned partials of token t summed in rank order in
-     fp32, rounded once.
-With one rank this is the single-GPU layer bit for bit; with several it
-differs from it only in the rounding of the per-rank partial sums.
+  3. return: every slot's row goes back to its source rank, to the place of
+     slot (t, j) there;
+  4. combine: out[t] = the k slot rows of token t summed in j order in fp32,
+     rounded once: the single-GPU layer's combine.
+So the output equals the single-GPU layer's bit for bit, for any number of
+ranks.
 
 On GPUs (EPMoE with local tiers) the four steps are the library's hexmoe_ep_*
 kernels over CUDA-IPC peer memory: stores straight into the owner's region over
-NVLink, epoch flags instead of host synchronisation, so a forward can be
-captured in a CUDA graph.  The only collective on the host is the one-time
+NVLink (the return from the down GEMM's own epilogue), epoch flags instead of
+host synchronisation, so a forward can be captured in a CUDA graph.  The only collective on the host is the one-time
 exchange of the IPC handles at construction.  An expert id outside 0..E-1 is
 dropped and sets the device error word (hexmoe_device_status) on the GPU path.
 
@@ -311,29 +311,19 @@ class EPMoE:
         row = row_base[src_of_slot] + recv_rec[:, 0]
         e = recv_rec[:, 1]
         wr = recv_rec[:, 2].to(torch.int32).view(torch.float32)
-        n_rows = recv_x.shape[0]
-        part = torch.zeros(n_rows, H, dtype=torch.float32)
-        if row.numel():
-            y = self.expert_fn(recv_x[row], wr, e).to(rdt).float()
-            # 4. per received row, its slots in j order (contiguous, in order): level by level
-            first = torch.ones_like(row, dtype=torch.bool)
-            first[1:] = row[1:] != row[:-1]
-            start = torch.nonzero(first).flatten()
-            level = torch.arange(row.numel()) - torch.repeat_interleave(start, torch.diff(
-                torch.cat([start, torch.tensor([row.numel()])])))
-            for lv in range(int(level.max()) + 1):
-                sel = level == lv
-                part[row[sel]] += y[sel]
-        back_rows = part.to(rdt)
-        ret = torch.empty(sum(sent_rows), H, dtype=rdt)
-        self._a2a(ret, back_rows, sent_rows, got_rows)
-        # 5. combine in rank order
-        out = torch.zeros(T, H, dtype=torch.float32)
+        y = self.expert_fn(recv_x[row], wr, e).to(rdt) if row.numel() else torch.empty(0, H, dtype=rdt)
+        # 4. every slot's row back to its source, in the order the source sent the slots
+        ret = torch.empty(sum(sent_slots), H, dtype=rdt)
+        self._a2a(ret, y.contiguous(), sent_slots, got_slots)
+        per = torch.zeros(T, k, H, dtype=torch.float32)
         base = 0
-        for d in range(world):
-            tok = plan.rows[d]
-            out[tok] += ret[base:base + len(tok)].float()
-            base += len(tok)
+        for t_idx, j_idx in plan.slots:
+            per[t_idx, j_idx] = ret[base:base + t_idx.numel()].float()
+            base += t_idx.numel()
+        # 5. the single-GPU combine: the k slot rows in j order, fp32, rounded once
+        out = torch.zeros(T, H, dtype=torch.float32)
+        for j in range(k):
+            out = out + per[:, j]
         return out.to(x.dtype)
 
     # ------------------------------------------------------------------ entry
@@ -352,17 +342,13 @@ class EPMoE:
 
 def reference_combine(y_slots: torch.Tensor, ids: torch.Tensor, shard: ExpertShard, out_dtype) -> torch.Tensor:
     """What EPMoE returns, from the single-GPU layer's per-slot rows y [T * k, H]
-    (hexmoe_forward_slots): per rank (in rank order) the fp32 sum of the token's
-    slots it owns in j order, rounded to y's dtype, then the fp32 sum of those
-    partials, rounded to out_dtype.  Any device."""
+    (hexmoe_forward_slots): per token the fp32 sum of its k slot rows in j
+    order, rounded once to out_dtype, which is the single-GPU layer's own
+    combine whatever the sharding (`shard` and the ids only fix the shapes).
+    Any device."""
     T, k = ids.shape
     yv = y_slots.view(T, k, -1).float()
-    owner = shard.owner(ids.to(torch.int64))
     out = torch.zeros(T, yv.shape[2], dtype=torch.float32, device=y_slots.device)
-    for d in range(shard.world):
-        part = torch.zeros_like(out)
-        for j in range(k):
-            m = (owner[:, j] == d).to(torch.float32)[:, None]
-            part = torch.where(m > 0, part + yv[:, j], part)
-        out = out + part.to(y_slots.dtype).float()
+    for j in range(k):
+        out = out + yv[:, j]
     return out.to(out_dtype)

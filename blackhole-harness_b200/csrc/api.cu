@@ -300,7 +300,7 @@ int run_gate_up(const hexmoe_layer* layer, const void* xs, bool bf16, int64_t to
 
 int run_down(const hexmoe_layer* layer, const void* act, bool bf16, int64_t tokens, int32_t topk,
              const float* topk_weights, const int32_t* sid, const int32_t* eid, const int32_t* npp, int32_t bm,
-             void* y, int32_t* dev_err, cudaStream_t st, bool pdl) {
+             void* y, int32_t* dev_err, cudaStream_t st, bool pdl, const SlotOut* slot_out = nullptr) {
   const hexmoe_layer_desc& d = layer->desc;
   const int64_t S = tokens * topk;
   const int64_t max_blocks = (S + bm - 1) / bm + std::min<int64_t>(d.num_experts, S);
@@ -323,6 +323,7 @@ int run_down(const hexmoe_layer* layer, const void* act, bool bf16, int64_t toke
   q.m_tiles = d.hidden_pad / kTileM;
   q.out = y; q.ld_out = d.hidden;
   q.topk_w = topk_weights;
+  if (slot_out) q.slot_out = *slot_out;
   q.dev_err = dev_err;
   if (bm == kDecBlock) {
     DecParams r{};
@@ -336,7 +337,7 @@ int run_down(const hexmoe_layer* layer, const void* act, bool bf16, int64_t toke
     r.sorted_ids = sid; r.expert_ids = eid; r.npp = npp; r.num_slots = static_cast<int32_t>(S);
     r.rows_pad = d.hidden_pad; r.rows_store = d.hidden; r.k_pad = d.inter_pad;
     r.block = d.block; r.m_tiles = d.hidden_pad / kTileM; r.ksteps = d.inter_pad / kKStep;
-    r.out = y; r.ld_out = d.hidden; r.topk_w = topk_weights; r.dev_err = dev_err;
+    r.out = y; r.ld_out = d.hidden; r.topk_w = topk_weights; r.slot_out = q.slot_out; r.dev_err = dev_err;
     int per_sm = 1;
     if (!plan_small(r, 1, max_blocks, layer->num_sms, per_sm))
       return fail(HEXMOE_E_UNSUPPORTED, "inter %d does not fit the small-batch kernel", d.inter_pad);
@@ -530,7 +531,8 @@ namespace {
 int forward_impl(const hexmoe_layer* layer, const void* x, int32_t x_dtype, int64_t tokens, int32_t topk,
                  const float* topk_weights, const void* topk_ids, int32_t ids_dtype, void* out, int32_t out_dtype,
                  void* slots_out, int32_t block_m, void* workspace, size_t workspace_bytes, void* stream,
-                 const int32_t* slot_row = nullptr, const int32_t* seg_counts = nullptr, int64_t seg_len = 0) {
+                 const int32_t* slot_row = nullptr, const int32_t* seg_counts = nullptr, int64_t seg_len = 0,
+                 const SlotOut* slot_out = nullptr) {
   if (!layer) return fail(HEXMOE_E_ARG, "hexmoe_forward: null layer");
   const hexmoe_layer_desc& d = layer->desc;
   if (tokens < 0 || topk <= 0 || topk > d.num_experts) return fail(HEXMOE_E_ARG, "tokens %lld / topk %d", static_cast<long long>(tokens), topk);
@@ -575,7 +577,7 @@ int forward_impl(const hexmoe_layer* layer, const void* x, int32_t x_dtype, int6
   if (e != cudaSuccess) return cuda_fail(e, "gather launch");
   int rc = run_gate_up(layer, xs, bf16, tokens, topk, sid, eid, npp, bm, act, dev_err, st, true);
   if (rc) return rc;
-  rc = run_down(layer, act, bf16, tokens, topk, topk_weights, sid, eid, npp, bm, y, dev_err, st, true);
+  rc = run_down(layer, act, bf16, tokens, topk, topk_weights, sid, eid, npp, bm, y, dev_err, st, true, slot_out);
   if (rc) return rc;
   if (slots_out) return HEXMOE_OK;
 
@@ -599,7 +601,7 @@ size_t hexmoe::slots_workspace_bytes(const hexmoe_layer* layer, int64_t num_slot
 int hexmoe::forward_slot_space(const hexmoe_layer* layer, const void* x, int32_t x_dtype, int64_t num_slots,
                                const int32_t* slot_expert, const float* slot_weight, const int32_t* slot_row,
                                const int32_t* seg_counts, int64_t seg_len, void* y, int32_t block_m, void* workspace,
-                               size_t workspace_bytes, cudaStream_t st, void** y_used) {
+                               size_t workspace_bytes, cudaStream_t st, void** y_used, const SlotOut* slot_out) {
   if (!layer) return fail(HEXMOE_E_ARG, "forward_slot_space: null layer");
   if (!y) {
     // the per-slot rows go to the workspace's own y region
@@ -611,7 +613,7 @@ int hexmoe::forward_slot_space(const hexmoe_layer* layer, const void* x, int32_t
   if (y_used) *y_used = y;
   return forward_impl(layer, x, x_dtype, num_slots, 1, slot_weight, slot_expert, HEXMOE_I32, y,
                       x_dtype == HEXMOE_F16 ? HEXMOE_F16 : HEXMOE_BF16, y, block_m, workspace, workspace_bytes, st,
-                      slot_row, seg_counts, seg_len);
+                      slot_row, seg_counts, seg_len, slot_out);
 }
 
 extern "C" {

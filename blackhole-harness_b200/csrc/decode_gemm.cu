@@ -375,6 +375,14 @@ __device__ void dec_consumer(const DecParams& p, uint8_t* smem, DecCtrl* c, int 
       if (lane == 0) mbar_arrive(&c->r_empty);
     }
     // epilogue: acc[.][s][0..1] = (row 16s + g, tokens 2q, 2q+1), [2..3] = (row 16s + g + 8, same tokens)
+    uint16_t* drow[2] = {nullptr, nullptr};   // down: the output rows of tokens 2q, 2q+1
+    if constexpr (!GLU) {
+      const int sl[2] = {slot0, slot1};
+#pragma unroll
+      for (int u = 0; u < 2; ++u)
+        if (sl[u] < p.num_slots)
+          drow[u] = slot_out_row(p.slot_out, out16, p.ld_out, p.slot_out.row ? __ldg(p.slot_out.row + sl[u]) : sl[u]);
+    }
 #pragma unroll
     for (int s = 0; s < 2; ++s)
 #pragma unroll
@@ -383,17 +391,15 @@ __device__ void dec_consumer(const DecParams& p, uint8_t* smem, DecCtrl* c, int 
         const int row = tile_m * (RQ * kDecRows) + static_cast<int>(row_w) + 16 * s + (i >> 1) * 8;
         const int sl = (i & 1) ? slot1 : slot0;
         if (sl >= p.num_slots || row >= p.rows_store) continue;
-        float r;
-        int64_t o;
         if constexpr (GLU) {
           const float gv = acc[0][s][i];
-          r = __fdividef(gv, 1.0f + __expf(-gv)) * acc[1][s][i];   // silu(gate) * up, as the tcgen05 epilogue
-          o = (static_cast<int64_t>(tile_b) * kDecBlock + n) * p.ld_out + row;
+          const float r = __fdividef(gv, 1.0f + __expf(-gv)) * acc[1][s][i];   // silu(gate) * up, as the tcgen05 epilogue
+          out16[(static_cast<int64_t>(tile_b) * kDecBlock + n) * p.ld_out + row] =
+              static_cast<uint16_t>(pack2<BF16>(r, 0.f) & 0xFFFFu);
         } else {
-          r = acc[0][s][i] * ((i & 1) ? w1 : w0);
-          o = static_cast<int64_t>(sl) * p.ld_out + row;
+          const float r = acc[0][s][i] * ((i & 1) ? w1 : w0);
+          drow[i & 1][row] = static_cast<uint16_t>(pack2<BF16>(r, 0.f) & 0xFFFFu);
         }
-        out16[o] = static_cast<uint16_t>(pack2<BF16>(r, 0.f) & 0xFFFFu);
       }
   }
 }
@@ -423,6 +429,7 @@ __global__ void __launch_bounds__(kDecThreads, 2) hex_decode_kernel(const __grid
   } else {
     dec_consumer<GLU, BF16, RQ>(p, smem, c, warp, lane);
   }
+  if (!GLU && p.slot_out.fence) __threadfence_system();   // peer stores visible before the return flags
 }
 
 template <bool GLU, bool BF16, int RQ>

@@ -16,10 +16,12 @@
 //   rec_row    [world][seg_len] int32: per received slot, its row (src*cap + pos)
 //   rec_exp    [world][seg_len] int32: per received slot, its global expert
 //   rec_w      [world][seg_len] f32:   per received slot, its top-k weight
-//   rowslot    [world][cap+1] int32: first slot of every received row (the
-//              slots of one row are contiguous, in the token's j order)
-//   ret        [world][cap][H] 16-bit: the partial sums each destination rank
-//              returns for this rank's tokens, in the order they were sent
+//   rec_dst    [world][seg_len] int32: per received slot, where its output row
+//              goes: src * cap * topk + t * topk + j (token t's j-th slot at
+//              source src)
+//   ret        [cap * topk][H] 16-bit: the per-slot output rows of this rank's
+//              tokens, row t * topk + j, stored by whichever rank owns the
+//              slot's expert
 //
 // One forward, all on the caller's stream, no host synchronisation:
 //   plan      (a CTA per 256 tokens) per token and destination rank, the row
@@ -30,19 +32,22 @@
 //             writes the counts and raises disp[me] = epoch on every rank
 //   wait      (1 CTA) disp[src] >= epoch for every source (bounded)
 //   experts   the layer over the received slots (align over the ragged slot
-//             space, gather through rec_row, gate/up, down) -> per-slot rows
-//   return    (all SMs) per received row, its slots summed in j order in fp32,
-//             rounded once, stored into the source's ret; the last CTA raises
-//             ret[me] = epoch on every rank
-//   wait      ret[d] >= epoch for every destination (bounded)
-//   combine   out[t] = sum over ranks d in rank order of ret[d][pos(t, d)],
-//             fp32, rounded once
+//             space, gather through rec_row, gate/up, down); the down GEMM's
+//             epilogue stores each slot's row (top-k weight applied, rounded
+//             once) straight into its source's ret over NVLink, so the return
+//             runs under the GEMM, and every thread ends with a system fence
+//   signal    (1 CTA) ret flag[me] = epoch on every rank
+//   wait      ret flag[d] >= epoch for every destination (bounded)
+//   combine   out[t] = sum over j of ret[t * topk + j] in fp32, rounded once:
+//             the single-GPU layer's combine over the same per-slot rows, so
+//             the output equals the single-GPU layer's bit for bit
 //
-// Buffers are single: a source writes rank d's receive rows for epoch e only
-// after its own combine of epoch e-1 saw d's return of e-1, which d raised
-// after its experts and return had read everything of e-1; and d writes a
-// source's ret for epoch e only after it saw that source's dispatch of e,
-// issued after the source's combine of e-1 had read ret.  So every rank must
+// Buffers are single: a source writes rank d's receive rows and slot records
+// for epoch e only after its own combine of epoch e-1 saw d's return flag of
+// e-1, which d raised after its down GEMM (the last reader of them) of e-1 had
+// finished; and d writes a source's ret for epoch e only after it saw that
+// source's dispatch of e, issued after the source's combine of e-1 had read
+// ret.  So every rank must
 // run every forward (the same sequence of calls on every rank).  Every wait is
 // bounded (2 s): a missing peer sets the device error word (timeout) instead of
 // hanging the GPU.
@@ -64,7 +69,7 @@ struct EpArgs {
   int32_t rank, world, E, P, H, topk;
   int64_t cap, seg_len;
   // region offsets
-  uint64_t o_disp, o_ret_flag, o_rows, o_slots, o_x, o_row, o_exp, o_w, o_rowslot, o_ret;
+  uint64_t o_disp, o_ret_flag, o_rows, o_slots, o_x, o_row, o_exp, o_w, o_dst, o_ret;
   // this rank's private state
   int64_t* epoch;
   uint32_t* done;               // [3]: CTAs finished in send / return / plan
@@ -73,6 +78,7 @@ struct EpArgs {
   int32_t* soff;                // [cap][world]: first slot offset of token t at rank d within its plan CTA
   int64_t* plan_tot;            // [plan CTAs][kEpMaxWorld]: each plan CTA's totals (rows << 32 | slots)
   int64_t* plan_off;            // [plan CTAs][kEpMaxWorld]: their exclusive offsets over CTAs
+  int32_t* cmap;                // [cap * topk]: the combine's row of slot (t, j): t * topk + j, -1 = bad expert id
   int32_t* dev_err;
 };
 
@@ -108,7 +114,9 @@ __device__ __forceinline__ void token_counts(const EpArgs& a, const void* ids, i
   for (int j = 0; j < a.topk; ++j) {
     const int64_t e = I64 ? __ldg(static_cast<const int64_t*>(ids) + t * a.topk + j)
                           : static_cast<int64_t>(__ldg(static_cast<const int32_t*>(ids) + t * a.topk + j));
-    if (e < 0 || e >= a.E) {
+    const bool bad = e < 0 || e >= a.E;
+    a.cmap[t * a.topk + j] = bad ? -1 : static_cast<int32_t>(t * a.topk + j);
+    if (bad) {
       atomicOr(a.dev_err, kDevErrExpertId);
       continue;
     }
@@ -256,7 +264,7 @@ __global__ void __launch_bounds__(kSendThreads) ep_send_kernel(EpArgs a, const X
       at<int32_t>(R, a.o_row)[seg + my_so + rk] = static_cast<int32_t>(a.rank * a.cap + my_pos);
       at<int32_t>(R, a.o_exp)[seg + my_so + rk] = static_cast<int32_t>(e);
       at<float>(R, a.o_w)[seg + my_so + rk] = __ldg(w + t * a.topk + lane);
-      if (rk == 0) at<int32_t>(R, a.o_rowslot)[static_cast<int64_t>(a.rank) * (a.cap + 1) + my_pos] = my_so;
+      at<int32_t>(R, a.o_dst)[seg + my_so + rk] = static_cast<int32_t>((a.rank * a.cap + t) * a.topk + lane);
     }
   }
   // the last CTA to finish publishes the counts and raises the dispatch flags
@@ -274,7 +282,6 @@ __global__ void __launch_bounds__(kSendThreads) ep_send_kernel(EpArgs a, const X
     const int32_t rows = a.tot[2 * d], slots = a.tot[2 * d + 1];
     at<int32_t>(R, a.o_rows)[a.rank] = rows;
     at<int32_t>(R, a.o_slots)[a.rank] = slots;
-    at<int32_t>(R, a.o_rowslot)[static_cast<int64_t>(a.rank) * (a.cap + 1) + rows] = slots;
     __threadfence_system();
     st_release_sys(at<uint64_t>(R, a.o_disp) + a.rank, static_cast<uint64_t>(epoch));
   }
@@ -303,121 +310,18 @@ __global__ void ep_wait_kernel(EpArgs a, uint64_t o_flags) {
   __syncthreads();
 }
 
-// ---------------------------------------------------------------- return
-// A warp per received row: its slots' rows of y summed in slot (j) order in
-// fp32, rounded once to the row type and stored into the source's ret.
-template <typename YT>
-__global__ void __launch_bounds__(kSendThreads) ep_return_kernel(EpArgs a, const YT* __restrict__ y) {
-  const int lane = threadIdx.x & 31;
-  const int64_t epoch = *a.epoch;
-  int64_t start[kEpMaxWorld + 1];
-  start[0] = 0;
+// ---------------------------------------------------------------- signal
+// After the down GEMM, whose threads all ended with a system-scope fence after
+// their peer stores: ret flag[this rank] = epoch on every rank.
+__global__ void ep_signal_kernel(EpArgs a) {
+  const int d = threadIdx.x;
+  if (d < a.world) {
+    const uint64_t epoch = static_cast<uint64_t>(*a.epoch);
+    uint8_t* R = a.self;
 #pragma unroll
-  for (int d = 0; d < kEpMaxWorld; ++d)
-    start[d + 1] = start[d] + (d < a.world ? __ldg(at<int32_t>(a.self, a.o_rows) + d) : 0);
-  const int64_t total = start[kEpMaxWorld];
-  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * kSendThreads) >> 5;
-  const int hv = a.H / 8;
-  for (int64_t g = (blockIdx.x * static_cast<int64_t>(kSendThreads) + threadIdx.x) >> 5; g < total; g += nwarps) {
-    int src = 0;
-#pragma unroll
-    for (int d = 1; d < kEpMaxWorld; ++d)
-      if (g >= start[d]) src = d;
-    const int64_t rho = g - start[src];
-    const int32_t* rs = at<int32_t>(a.self, a.o_rowslot) + static_cast<int64_t>(src) * (a.cap + 1);
-    const int32_t s0 = __ldg(rs + rho), s1 = __ldg(rs + rho + 1);
-    const YT* ybase = y + (static_cast<int64_t>(src) * a.seg_len) * a.H;
-    uint4* dst = at<uint4>(a.peer[src], a.o_ret) + (static_cast<int64_t>(a.rank) * a.cap + rho) * hv;
-    for (int c0 = 0; c0 < hv; c0 += 4 * 32) {
-      float acc[4][8];
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int q = 0; q < 8; ++q) acc[i][q] = 0.f;
-      // slots four at a time: their loads are all in flight before the first add
-      // (the adds themselves stay in slot order)
-      for (int s = s0; s < s1; s += 4) {
-        uint4 v[4][4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const uint4* row = reinterpret_cast<const uint4*>(ybase + static_cast<int64_t>(s + u) * a.H);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int c = c0 + i * 32 + lane;
-            v[u][i] = (s + u < s1 && c < hv) ? __ldg(row + c) : make_uint4(0, 0, 0, 0);
-          }
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          if (s + u >= s1) break;
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const YT* e = reinterpret_cast<const YT*>(&v[u][i]);
-#pragma unroll
-            for (int q = 0; q < 8; ++q) acc[i][q] += static_cast<float>(e[q]);
-          }
-        }
-      }
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int c = c0 + i * 32 + lane;
-        if (c < hv) {
-          constexpr bool kBf16 = std::is_same<YT, __nv_bfloat16>::value;
-          dst[c] = make_uint4(pack2<kBf16>(acc[i][0], acc[i][1]), pack2<kBf16>(acc[i][2], acc[i][3]),
-                              pack2<kBf16>(acc[i][4], acc[i][5]), pack2<kBf16>(acc[i][6], acc[i][7]));
-        }
-      }
-    }
-  }
-  __shared__ bool last;
-  __syncthreads();
-  if (threadIdx.x == 0) {
+    for (int q = 0; q < kEpMaxWorld; ++q) R = q == d ? a.peer[q] : R;
     __threadfence_system();
-    last = atomicAdd(a.done + 1, 1u) == gridDim.x - 1;
-  }
-  __syncthreads();
-  if (last && threadIdx.x < a.world) {
-    __threadfence_system();
-    st_release_sys(at<uint64_t>(a.peer[threadIdx.x], a.o_ret_flag) + a.rank, static_cast<uint64_t>(epoch));
-  }
-  if (last && threadIdx.x == 0) a.done[1] = 0;
-}
-
-// ---------------------------------------------------------------- combine
-// out[t, h] = sum over ranks d (in rank order) holding a row of t of ret[d][pos],
-// fp32, rounded once.
-template <typename YT, int OUT>
-__global__ void ep_combine_kernel(EpArgs a, int64_t T, void* __restrict__ out) {
-  const int hv = a.H / 8;
-  const int64_t total = T * hv;
-  const YT* ret = at<const YT>(a.self, a.o_ret);
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t t = i / hv;
-    const int c = static_cast<int>(i % hv);
-    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    const int64_t* off = a.plan_off + (t / kPlanThreads) * kEpMaxWorld;
-    for (int d = 0; d < a.world; ++d) {
-      int32_t p = __ldg(a.pos + t * a.world + d);
-      if (p < 0) continue;
-      p += static_cast<int32_t>(__ldg(off + d) >> 32);
-      const uint4 v = *(reinterpret_cast<const uint4*>(ret + (static_cast<int64_t>(d) * a.cap + p) * a.H) + c);
-      const YT* e = reinterpret_cast<const YT*>(&v);
-#pragma unroll
-      for (int q = 0; q < 8; ++q) acc[q] += static_cast<float>(e[q]);
-    }
-    const int64_t o = t * a.H + c * 8;
-    if (OUT == HEXMOE_F32) {
-      float4* dd = reinterpret_cast<float4*>(static_cast<float*>(out) + o);
-      dd[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-      dd[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
-    } else {
-      uint4 r;
-      uint32_t* rr = reinterpret_cast<uint32_t*>(&r);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) rr[q] = pack2<OUT == HEXMOE_BF16>(acc[2 * q], acc[2 * q + 1]);
-      *reinterpret_cast<uint4*>(static_cast<uint16_t*>(out) + o) = r;
-    }
+    st_release_sys(at<uint64_t>(R, a.o_ret_flag) + a.rank, epoch);
   }
 }
 
@@ -428,7 +332,7 @@ using namespace hexmoe;
 struct hexmoe_ep {
   int device, rank, world, E, P, H, topk, row_dtype;
   int64_t cap, seg_len;
-  uint64_t o_disp, o_ret_flag, o_rows, o_slots, o_x, o_row, o_exp, o_w, o_rowslot, o_ret;
+  uint64_t o_disp, o_ret_flag, o_rows, o_slots, o_x, o_row, o_exp, o_w, o_dst, o_ret;
   size_t region_bytes;
   uint8_t* region;
   uint8_t* peer[kEpMaxWorld];
@@ -437,7 +341,7 @@ struct hexmoe_ep {
   uint8_t* local;
   int64_t* epoch;
   uint32_t* done;
-  int32_t *tot, *pos, *soff;
+  int32_t *tot, *pos, *soff, *cmap;
   int64_t *plan_tot, *plan_off;
   int64_t last_tokens;
 };
@@ -453,10 +357,10 @@ EpArgs ep_args(const hexmoe_ep* ep, int32_t* dev_err) {
   a.rank = ep->rank; a.world = ep->world; a.E = ep->E; a.P = ep->P; a.H = ep->H; a.topk = ep->topk;
   a.cap = ep->cap; a.seg_len = ep->seg_len;
   a.o_disp = ep->o_disp; a.o_ret_flag = ep->o_ret_flag; a.o_rows = ep->o_rows; a.o_slots = ep->o_slots;
-  a.o_x = ep->o_x; a.o_row = ep->o_row; a.o_exp = ep->o_exp; a.o_w = ep->o_w; a.o_rowslot = ep->o_rowslot;
+  a.o_x = ep->o_x; a.o_row = ep->o_row; a.o_exp = ep->o_exp; a.o_w = ep->o_w; a.o_dst = ep->o_dst;
   a.o_ret = ep->o_ret;
   a.epoch = ep->epoch; a.done = ep->done; a.tot = ep->tot; a.pos = ep->pos; a.soff = ep->soff;
-  a.plan_tot = ep->plan_tot; a.plan_off = ep->plan_off;
+  a.plan_tot = ep->plan_tot; a.plan_off = ep->plan_off; a.cmap = ep->cmap;
   a.dev_err = dev_err;
   return a;
 }
@@ -513,14 +417,14 @@ int hexmoe_ep_init(int32_t rank, int32_t world, int32_t num_experts, int32_t hid
   ep->o_row = off; off = up256(off + W * ep->seg_len * 4);
   ep->o_exp = off; off = up256(off + W * ep->seg_len * 4);
   ep->o_w = off; off = up256(off + W * ep->seg_len * 4);
-  ep->o_rowslot = off; off = up256(off + W * (ep->cap + 1) * 4);
-  ep->o_ret = off; off = up256(off + W * ep->cap * hidden * 2);
+  ep->o_dst = off; off = up256(off + W * ep->seg_len * 4);
+  ep->o_ret = off; off = up256(off + static_cast<size_t>(ep->cap) * topk * hidden * 2);
   ep->region_bytes = off;
   cudaError_t e = cudaMalloc(&ep->region, ep->region_bytes);
   if (e != cudaSuccess) { delete ep; return report_cuda_error(e, "hexmoe_ep_init: region allocation"); }
   const size_t plan_ctas = static_cast<size_t>((ep->cap + kPlanThreads - 1) / kPlanThreads);
-  const size_t local_bytes =
-      up256(8 + 16) + up256(W * 2 * 4) + 2 * up256(ep->cap * W * 4) + 2 * up256(plan_ctas * kEpMaxWorld * 8);
+  const size_t local_bytes = up256(8 + 16) + up256(W * 2 * 4) + 2 * up256(ep->cap * W * 4) +
+                             2 * up256(plan_ctas * kEpMaxWorld * 8) + up256(static_cast<size_t>(ep->cap) * topk * 4);
   e = cudaMalloc(&ep->local, local_bytes);
   if (e == cudaSuccess) e = cudaMemset(ep->region, 0, header);
   if (e == cudaSuccess) e = cudaMemset(ep->local, 0, local_bytes);
@@ -539,7 +443,8 @@ int hexmoe_ep_init(int32_t rank, int32_t world, int32_t num_experts, int32_t hid
   ep->pos = reinterpret_cast<int32_t*>(ep->local + lo); lo += up256(ep->cap * W * 4);
   ep->soff = reinterpret_cast<int32_t*>(ep->local + lo); lo += up256(ep->cap * W * 4);
   ep->plan_tot = reinterpret_cast<int64_t*>(ep->local + lo); lo += up256(plan_ctas * kEpMaxWorld * 8);
-  ep->plan_off = reinterpret_cast<int64_t*>(ep->local + lo);
+  ep->plan_off = reinterpret_cast<int64_t*>(ep->local + lo); lo += up256(plan_ctas * kEpMaxWorld * 8);
+  ep->cmap = reinterpret_cast<int32_t*>(ep->local + lo);
   for (int d = 0; d < kEpMaxWorld; ++d) { ep->peer[d] = nullptr; ep->opened[d] = false; }
   ep->peer[rank] = ep->region;
   ep->connected = world == 1;
@@ -623,7 +528,6 @@ int hexmoe_ep_experts(hexmoe_ep* ep, const hexmoe_layer* local, int32_t block_m,
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return report_cuda_error(e, "hexmoe_ep_experts: wait launch");
   const int64_t S = static_cast<int64_t>(ep->world) * ep->seg_len;
-  void* y = nullptr;
   if (local) {
     const hexmoe_layer_desc* d = layer_desc(local);
     if (d->hidden != ep->H || d->num_experts != ep->E)
@@ -632,21 +536,23 @@ int hexmoe_ep_experts(hexmoe_ep* ep, const hexmoe_layer* local, int32_t block_m,
     if (!workspace || workspace_bytes < need)
       return report_error(HEXMOE_E_ARG, "hexmoe_ep_experts: workspace smaller than hexmoe_ep_workspace_bytes");
     uint8_t* R = ep->region;
+    // the down GEMM stores slot (src, t, j)'s row at ret row t * topk + j of rank src
+    SlotOut so{};
+    so.row = reinterpret_cast<const int32_t*>(R + ep->o_dst);
+    for (int r = 0; r < kEpMaxWorld; ++r)
+      so.base[r] = r < ep->world ? reinterpret_cast<uint16_t*>(ep->peer[r] + ep->o_ret) : nullptr;
+    so.seg_rows = static_cast<int32_t>(ep->cap * ep->topk);
+    so.fence = 1;
     int rc = forward_slot_space(local, R + ep->o_x, ep->row_dtype, S, reinterpret_cast<const int32_t*>(R + ep->o_exp),
                                 reinterpret_cast<const float*>(R + ep->o_w), reinterpret_cast<const int32_t*>(R + ep->o_row),
                                 reinterpret_cast<const int32_t*>(R + ep->o_slots), ep->seg_len, nullptr, block_m,
-                                workspace, workspace_bytes, st, &y);
+                                workspace, workspace_bytes, st, nullptr, &so);
     if (rc) return rc;
   }
-  // without local experts nothing can have been routed here: rows = 0 from every source
-  const int64_t rows_max = static_cast<int64_t>(ep->world) * ep->cap;
-  const int grid = grid_for(local ? rows_max : 1, kSendThreads / 32, 4);
-  if (ep->row_dtype == HEXMOE_BF16)
-    ep_return_kernel<__nv_bfloat16><<<grid, kSendThreads, 0, st>>>(a, static_cast<const __nv_bfloat16*>(y));
-  else
-    ep_return_kernel<__half><<<grid, kSendThreads, 0, st>>>(a, static_cast<const __half*>(y));
+  // without local experts nothing can have been routed here: only the flags
+  ep_signal_kernel<<<1, 32, 0, st>>>(a);
   e = cudaGetLastError();
-  if (e != cudaSuccess) return report_cuda_error(e, "hexmoe_ep_experts: return launch");
+  if (e != cudaSuccess) return report_cuda_error(e, "hexmoe_ep_experts: signal launch");
   return HEXMOE_OK;
 }
 
@@ -662,20 +568,10 @@ int hexmoe_ep_combine(hexmoe_ep* ep, int64_t tokens, void* out, int32_t out_dtyp
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const EpArgs a = ep_args(ep, dev_err);
   ep_wait_kernel<<<1, 32, 0, st>>>(a, ep->o_ret_flag);
-  if (tokens > 0) {
-    const int64_t total = tokens * (ep->H / 8);
-    const unsigned grid = static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, 148 * 8));
-    const bool bf = ep->row_dtype == HEXMOE_BF16;
-    if (out_dtype == HEXMOE_F32) {
-      if (bf) ep_combine_kernel<__nv_bfloat16, HEXMOE_F32><<<grid, 256, 0, st>>>(a, tokens, out);
-      else ep_combine_kernel<__half, HEXMOE_F32><<<grid, 256, 0, st>>>(a, tokens, out);
-    } else if (bf) {
-      ep_combine_kernel<__nv_bfloat16, HEXMOE_BF16><<<grid, 256, 0, st>>>(a, tokens, out);
-    } else {
-      ep_combine_kernel<__half, HEXMOE_F16><<<grid, 256, 0, st>>>(a, tokens, out);
-    }
-  }
   cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess && tokens > 0)
+    e = launch_combine(ep->region + ep->o_ret, ep->row_dtype, tokens, ep->topk, ep->H, ep->H, ep->cmap,
+                       tokens * ep->topk, out, out_dtype, st, false);
   if (e != cudaSuccess) return report_cuda_error(e, "hexmoe_ep_combine launch");
   return HEXMOE_OK;
 }

@@ -218,7 +218,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
         if (!GLU) {
           for (int r = lane; r < cnt; r += 32) {
             const int slot = __ldg(p.sorted_ids + static_cast<size_t>(ti.b) * p.bm + r);
-            rec->slot[r] = slot;
+            rec->slot[r] = p.slot_out.row ? __ldg(p.slot_out.row + slot) : slot;   // where its row goes
             rec->w[r] = __ldg(p.topk_w + slot);
           }
         }
@@ -494,7 +494,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
             const int n = n0 + 8 * h + tok;
             if (n < cnt && o8 < p.rows_store) {
               const uint4 val = *reinterpret_cast<const uint4*>(stg + tok * 32 + part * 8);
-              *reinterpret_cast<uint4*>(out16 + static_cast<size_t>(recs[ri].slot[n]) * p.ld_out + o8) = val;
+              *reinterpret_cast<uint4*>(slot_out_row(p.slot_out, out16, p.ld_out, recs[ri].slot[n]) + o8) = val;
             }
           }
         }
@@ -630,6 +630,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
     if (pending >= 0) tmem_st_wait();
   }
 
+  if (!GLU && p.slot_out.fence) __threadfence_system();   // peer stores visible before the return flags
   tc_fence_before();
   __syncthreads();
   tc_fence_after();

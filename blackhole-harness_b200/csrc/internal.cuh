@@ -27,6 +27,30 @@ constexpr uint32_t kTmemCols = 512;
 
 constexpr uint32_t kStepBytes = 8192;   // one 128-row x 128-input step of a tiled index stream
 
+// Where the down projection stores its per-slot rows.  row == nullptr: the
+// plain layout, slot s at y + s * ld_out.  Otherwise (the expert-parallel
+// return) slot s goes to global row g = row[s] of the concatenated per-slot
+// buffers of all ranks: base[g / seg_rows] + (g % seg_rows) * ld_out, a peer's
+// memory for another rank's tokens; fence: every thread of the kernel ends
+// with a system-scope fence, so its peer stores are visible before a later
+// kernel on the stream raises the return flags.
+struct SlotOut {
+  const int32_t* row;
+  uint16_t* base[HEXMOE_EP_MAX_WORLD];
+  int32_t seg_rows;
+  int32_t fence;
+};
+
+// The down epilogue's destination of slot id g (see SlotOut).
+__device__ __forceinline__ uint16_t* slot_out_row(const SlotOut& so, uint16_t* y, int64_t ld_out, int g) {
+  if (!so.row) return y + static_cast<int64_t>(g) * ld_out;
+  const int sg = g / so.seg_rows;
+  uint16_t* b = so.base[0];
+#pragma unroll
+  for (int i = 1; i < HEXMOE_EP_MAX_WORLD; ++i) b = sg == i ? so.base[i] : b;
+  return b + static_cast<int64_t>(g - sg * so.seg_rows) * ld_out;
+}
+
 // Everything the grouped-GEMM kernel needs; passed by value as a
 // __grid_constant__ parameter (tensor maps must live in parameter space).
 struct GemmParams {
@@ -70,6 +94,7 @@ struct GemmParams {
   void* out;                   // gate/up: act [max_blocks*bm, ld_out]; down: y [S, ld_out]
   int64_t ld_out;
   const float* topk_w;         // down: [S]
+  SlotOut slot_out;            // down: where each slot's row goes
   int32_t* dev_err;
 };
 
@@ -105,6 +130,7 @@ struct DecParams {
   void* out;                            // gate/up: act [plan rows, ld_out]; down: y [S, ld_out]
   int64_t ld_out;
   const float* topk_w;
+  SlotOut slot_out;                     // down: where each slot's row goes
   int32_t* dev_err;
 };
 // The shared-memory carve-up (block and tier bits set) for per_sm (1 or 2) CTAs
@@ -148,11 +174,13 @@ const hexmoe_layer_desc* layer_desc(const hexmoe_layer* layer);
 // seg_counts[g] slots of each seg_len-slot segment exist (the others are never
 // read or written).  Workspace: slots_workspace_bytes(layer, num_slots, block_m);
 // y == nullptr puts the rows into the workspace's own y region.  *y_used
-// (optional) receives where they went.
+// (optional) receives where they went.  slot_out (optional) routes the rows
+// elsewhere (SlotOut); y is then not written.
 int forward_slot_space(const hexmoe_layer* layer, const void* x, int32_t x_dtype, int64_t num_slots,
                        const int32_t* slot_expert, const float* slot_weight, const int32_t* slot_row,
                        const int32_t* seg_counts, int64_t seg_len, void* y, int32_t block_m, void* workspace,
-                       size_t workspace_bytes, cudaStream_t st, void** y_used = nullptr);
+                       size_t workspace_bytes, cudaStream_t st, void** y_used = nullptr,
+                       const SlotOut* slot_out = nullptr);
 size_t slots_workspace_bytes(const hexmoe_layer* layer, int64_t num_slots, int32_t block_m);
 int32_t* device_error_word();  // address of this device's error word (nullptr on failure)
 cudaError_t read_device_error(int32_t* value, bool clear);   // synchronous, current device

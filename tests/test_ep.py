@@ -4,11 +4,11 @@
 The reference has no multi-GPU path (its plugin refuses expert parallelism), so
 the bar is the single-process computation: every slot computed alone at top-1
 and rounded to the activation dtype (as the single-GPU layer's per-slot rows),
-then per owner rank the fp32 sum of the token's slots in top-k order rounded
-once, then those partials summed in rank order (ep.reference_combine).  EP must
-reproduce that bit for bit, and the oracle's moe_reference within the layer
-tolerance.  The same host protocol (one row per token and destination rank,
-pre-summed returns) is what the hexmoe_ep_* kernels run on GPUs.
+then per token the fp32 sum of its slots in top-k order rounded once (the
+single-GPU layer's combine, ep.reference_combine).  EP must reproduce that bit
+for bit at every world size, and the oracle's moe_reference within the layer
+tolerance.  The same host protocol (one row per token and destination rank out,
+one row per slot back) is what the hexmoe_ep_* kernels run on GPUs.
 """
 
 from __future__ import annotations
@@ -203,8 +203,10 @@ def test_plan_dispatch_rows_and_slots():
         [(0, 0), (0, 2)], [(1, 2), (2, 0)], [(0, 1), (2, 1), (2, 2)], [(1, 0), (1, 1)]]
 
 
-def test_reference_combine_single_rank_is_the_layer_combine():
-    """With one rank the EP combine is the single-GPU combine (slots in order, fp32, once rounded)."""
+@pytest.mark.parametrize("world", [1, 3, 8])
+def test_reference_combine_is_the_layer_combine(world):
+    """At any world size the EP combine is the single-GPU combine (slots in j
+    order, fp32, rounded once)."""
     from blackhole_b200.ep import ExpertShard, reference_combine
     g = torch.Generator().manual_seed(3)
     T, k = 9, 4
@@ -214,7 +216,8 @@ def test_reference_combine_single_rank_is_the_layer_combine():
     acc = want[:, 0]
     for j in range(1, k):
         acc = acc + want[:, j]
-    assert torch.equal(reference_combine(y, ids, ExpertShard(12, 0, 1), torch.bfloat16), acc.to(torch.bfloat16))
+    got = reference_combine(y, ids, ExpertShard(12, world - 1, world), torch.bfloat16)
+    assert torch.equal(got, acc.to(torch.bfloat16))
 
 
 def _leaving_worker(rank: int, world: int, port: int, out_q):

@@ -1,8 +1,8 @@
 """Expert parallelism over NVLink peer memory (hexmoe_ep_*): on every rank the EP
-layer equals the single-GPU layer's per-slot rows put through the EP combine, bit
-for bit (tests/ep_gpu_worker.py, one process per GPU), on two GPUs and, so that a
-one-GPU run covers the same kernels, as a single rank (which must equal the plain
-layer bit for bit).  NCCL only carries the one-time IPC handle exchange."""
+layer equals the plain single-GPU layer bit for bit (tests/ep_gpu_worker.py, one
+process per GPU), on two GPUs and, so that a one-GPU run covers the same
+kernels, as a single rank.  NCCL only carries the one-time IPC handle
+exchange."""
 
 from __future__ import annotations
 
@@ -39,8 +39,8 @@ def test_ep_two_gpus_matches_single_gpu():
 @pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU")
 def test_ep_one_rank_matches_single_gpu():
     """The expert-parallel kernels (plan, dispatch to itself, ragged align and
-    mapped gather, pre-summed return, combine) as a single rank: the result
-    equals the single-GPU layer bit for bit."""
+    mapped gather, the down GEMM's routed per-slot stores, combine) as a single
+    rank: the result equals the single-GPU layer bit for bit."""
     _run_workers(1, 29562)
 
 
