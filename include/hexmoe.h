@@ -259,18 +259,18 @@ HEXMOE_API int hexmoe_dequant(const hexmoe_parts* parts, int32_t bits, int32_t b
  * [r*P, (r+1)*P), P = ceil(num_experts / world), and runs them as a
  * hexmoe_layer built from its own tiers only (global expert ids kept).  Each
  * rank's context owns one device region that every other rank maps through
- * CUDA IPC; kernels store token rows, slot records and partial sums straight
- * into the owning rank's region with plain stores, and signal with epoch flags
+ * CUDA IPC; kernels store token rows, slot records and per-slot output rows
+ * straight into the owning rank's region with plain stores, and signal with epoch flags
  * (release / acquire at system scope).  Nothing synchronises with the host, so
  * a forward can be captured in a CUDA graph.
  *
  * Per forward: every token row crosses once per rank that owns one of its
  * experts (not once per slot); the owner runs its experts on the received
- * slots and returns, per row, the fp32 sum of that row's weighted slot
- * outputs in top-k order rounded once to the row dtype; the home rank adds the
- * returned partials in rank order in fp32 and rounds once.  (One GPU sums the
- * k slot outputs of a token in top-k order instead, so the two differ in the
- * rounding of the partial sums, within the layer tolerance.)
+ * slots, and its down GEMM stores each slot's weighted output row (rounded
+ * once to the row dtype) straight into the home rank's buffer at the slot's
+ * place; the home rank sums a token's k rows in top-k order in fp32 and rounds
+ * once.  That is the single-GPU layer's arithmetic: the output equals
+ * hexmoe_forward's bit for bit at every world size.
  *
  * Protocol rules: every rank calls init, exchanges handles (hexmoe_ep_handle,
  * gathered in rank order by the caller), connects, and then runs the same
@@ -287,9 +287,9 @@ typedef struct hexmoe_ep hexmoe_ep;
 /* Context of rank `rank` of `world` on the current device, for up to
  * max_tokens tokens per rank per forward, top-`topk` over num_experts global
  * experts of width `hidden`; rows travel as row_dtype (BF16 or F16).  Allocates
- * the shared region (2 x world x max_tokens x hidden x 2 bytes of rows plus
- * ~12 x world x max_tokens x topk bytes of slot records) and its private state;
- * synchronises the device. */
+ * the shared region ((world + topk) x max_tokens x hidden x 2 bytes of rows
+ * plus ~16 x world x max_tokens x topk bytes of slot records) and its private
+ * state; synchronises the device. */
 HEXMOE_API int hexmoe_ep_init(int32_t rank, int32_t world, int32_t num_experts, int32_t hidden, int32_t topk,
                               int64_t max_tokens, int32_t row_dtype, hexmoe_ep** out);
 /* The CUDA IPC handle (HEXMOE_EP_HANDLE_BYTES) of this rank's region. */
@@ -304,7 +304,8 @@ HEXMOE_API size_t hexmoe_ep_workspace_bytes(const hexmoe_ep* ep, const hexmoe_la
 HEXMOE_API int hexmoe_ep_dispatch(hexmoe_ep* ep, const void* x, int32_t x_dtype, int64_t tokens,
                                   const float* topk_weights, const void* topk_ids, int32_t ids_dtype, void* stream);
 /* Phase 2: wait for every rank's dispatch, run `local` (NULL on a rank that owns
- * no experts) on the received slots, return the partial sums to their ranks. */
+ * no experts) on the received slots; the down GEMM returns every slot's row to
+ * its home rank as it computes it. */
 HEXMOE_API int hexmoe_ep_experts(hexmoe_ep* ep, const hexmoe_layer* local, int32_t block_m, void* workspace,
                                  size_t workspace_bytes, void* stream);
 /* Phase 3: wait for every rank's return; out [T, hidden] (row_dtype or F32). */
