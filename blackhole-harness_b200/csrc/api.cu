@@ -233,13 +233,9 @@ struct DeviceGuard {
 };
 
 
-// xg (optional, 16-bit, tcgen05 tile heights only): the GEMM gathers its B
-// rows from xg [xg_rows, hidden] itself (slot s -> row slot_row[s], or s /
-// topk without a map) instead of reading the plan-ordered copy xs.
 int run_gate_up(const hexmoe_layer* layer, const void* xs, bool bf16, int64_t tokens, int32_t topk,
                 const int32_t* sid, const int32_t* eid, const int32_t* npp, int32_t bm, void* act, int32_t* dev_err,
-                cudaStream_t st, bool pdl, const void* xg = nullptr, int64_t xg_rows = 0,
-                const int32_t* slot_row = nullptr) {
+                cudaStream_t st, bool pdl) {
   const hexmoe_layer_desc& d = layer->desc;
   const int64_t S = tokens * topk;
   const int64_t max_blocks = (S + bm - 1) / bm + std::min<int64_t>(d.num_experts, S);
@@ -293,16 +289,9 @@ int run_gate_up(const hexmoe_layer* layer, const void* xs, bool bf16, int64_t to
     p.idx_t[t][0] = layer->idx_t[t][0];
     p.idx_t[t][1] = layer->idx_t[t][1];
   }
-  if (xg) {
-    p.gather = 1; p.topk = topk; p.slot_row = slot_row;
-    if (int rc = make_tmap(&p.tm_b, xg, dt16, 2, d.hidden, static_cast<uint64_t>(xg_rows), 2ull * d.hidden, 64, 1,
-                           CU_TENSOR_MAP_SWIZZLE_128B, "x tensor map (gather)"))
-      return rc;
-  } else if (int rc = make_tmap(&p.tm_b, xs, dt16, 2, d.hidden, static_cast<uint64_t>(max_blocks) * bm,
-                                2ull * d.hidden, 64, static_cast<uint32_t>(bm), CU_TENSOR_MAP_SWIZZLE_128B,
-                                "x_sorted tensor map")) {
+  if (int rc = make_tmap(&p.tm_b, xs, dt16, 2, d.hidden, static_cast<uint64_t>(max_blocks) * bm, 2ull * d.hidden, 64,
+                         static_cast<uint32_t>(bm), CU_TENSOR_MAP_SWIZZLE_128B, "x_sorted tensor map"))
     return rc;
-  }
   const int grid = static_cast<int>(std::min<int64_t>(layer->num_sms, max_blocks * p.m_tiles));
   cudaError_t e = launch_gemm(p, true, bf16, grid, st, pdl);
   if (e != cudaSuccess) return cuda_fail(e, "gate/up launch");
@@ -543,7 +532,7 @@ int forward_impl(const hexmoe_layer* layer, const void* x, int32_t x_dtype, int6
                  const float* topk_weights, const void* topk_ids, int32_t ids_dtype, void* out, int32_t out_dtype,
                  void* slots_out, int32_t block_m, void* workspace, size_t workspace_bytes, void* stream,
                  const int32_t* slot_row = nullptr, const int32_t* seg_counts = nullptr, int64_t seg_len = 0,
-                 const SlotOut* slot_out = nullptr, int64_t x_rows = 0) {
+                 const SlotOut* slot_out = nullptr) {
   if (!layer) return fail(HEXMOE_E_ARG, "hexmoe_forward: null layer");
   const hexmoe_layer_desc& d = layer->desc;
   if (tokens < 0 || topk <= 0 || topk > d.num_experts) return fail(HEXMOE_E_ARG, "tokens %lld / topk %d", static_cast<long long>(tokens), topk);
@@ -584,16 +573,9 @@ int forward_impl(const hexmoe_layer* layer, const void* x, int32_t x_dtype, int6
                                st, true, seg_counts, seg_len);
   if (e != cudaSuccess) return cuda_fail(e, "align launch");
 
-  // 16-bit activations at the tcgen05 tile heights: the gate/up GEMM gathers
-  // its rows from x itself; otherwise a gather pass writes the plan-ordered copy
-  const int64_t xg_rows = slot_row ? x_rows : tokens;
-  const bool gemm_gathers = bm != kDecBlock && x_dtype != HEXMOE_F32 && xg_rows > 0;
-  if (!gemm_gathers) {
-    e = launch_gather_rows(x, x_dtype, tokens, d.hidden, sid, npp, w.max_blocks * bm, topk, S, xs, st, true, slot_row);
-    if (e != cudaSuccess) return cuda_fail(e, "gather launch");
-  }
-  int rc = run_gate_up(layer, xs, bf16, tokens, topk, sid, eid, npp, bm, act, dev_err, st, true,
-                       gemm_gathers ? x : nullptr, xg_rows, slot_row);
+  e = launch_gather_rows(x, x_dtype, tokens, d.hidden, sid, npp, w.max_blocks * bm, topk, S, xs, st, true, slot_row);
+  if (e != cudaSuccess) return cuda_fail(e, "gather launch");
+  int rc = run_gate_up(layer, xs, bf16, tokens, topk, sid, eid, npp, bm, act, dev_err, st, true);
   if (rc) return rc;
   rc = run_down(layer, act, bf16, tokens, topk, topk_weights, sid, eid, npp, bm, y, dev_err, st, true, slot_out);
   if (rc) return rc;
@@ -619,8 +601,7 @@ size_t hexmoe::slots_workspace_bytes(const hexmoe_layer* layer, int64_t num_slot
 int hexmoe::forward_slot_space(const hexmoe_layer* layer, const void* x, int32_t x_dtype, int64_t num_slots,
                                const int32_t* slot_expert, const float* slot_weight, const int32_t* slot_row,
                                const int32_t* seg_counts, int64_t seg_len, void* y, int32_t block_m, void* workspace,
-                               size_t workspace_bytes, cudaStream_t st, void** y_used, const SlotOut* slot_out,
-                               int64_t x_rows) {
+                               size_t workspace_bytes, cudaStream_t st, void** y_used, const SlotOut* slot_out) {
   if (!layer) return fail(HEXMOE_E_ARG, "forward_slot_space: null layer");
   if (!y) {
     // the per-slot rows go to the workspace's own y region
@@ -632,7 +613,7 @@ int hexmoe::forward_slot_space(const hexmoe_layer* layer, const void* x, int32_t
   if (y_used) *y_used = y;
   return forward_impl(layer, x, x_dtype, num_slots, 1, slot_weight, slot_expert, HEXMOE_I32, y,
                       x_dtype == HEXMOE_F16 ? HEXMOE_F16 : HEXMOE_BF16, y, block_m, workspace, workspace_bytes, st,
-                      slot_row, seg_counts, seg_len, slot_out, x_rows);
+                      slot_row, seg_counts, seg_len, slot_out);
 }
 
 extern "C" {

@@ -546,7 +546,7 @@ int hexmoe_ep_experts(hexmoe_ep* ep, const hexmoe_layer* local, int32_t block_m,
     int rc = forward_slot_space(local, R + ep->o_x, ep->row_dtype, S, reinterpret_cast<const int32_t*>(R + ep->o_exp),
                                 reinterpret_cast<const float*>(R + ep->o_w), reinterpret_cast<const int32_t*>(R + ep->o_row),
                                 reinterpret_cast<const int32_t*>(R + ep->o_slots), ep->seg_len, nullptr, block_m,
-                                workspace, workspace_bytes, st, nullptr, &so, static_cast<int64_t>(ep->world) * ep->cap);
+                                workspace, workspace_bytes, st, nullptr, &so);
     if (rc) return rc;
   }
   // without local experts nothing can have been routed here: only the flags

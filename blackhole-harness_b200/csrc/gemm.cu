@@ -276,8 +276,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
     bool aborted = false;
     int cur = 0;
     const uint32_t b_bytes = static_cast<uint32_t>(p.bm) * 256u;
-    const bool gathers = p.gather && lane * 4 < p.bm;   // this lane gathers plan rows 4 lane .. 4 lane + 3
-    int32_t grow[4] = {0, 0, 0, 0};
     for (int t = blockIdx.x; t < num_tiles && !aborted; t += gridDim.x, ++cur) {
       const int ri = cur % kRecs;
       if (!mbar_wait_idle(&c->i_full[ri], (cur / kRecs) & 1, abort_flag, p.dev_err)) { aborted = true; break; }
@@ -285,27 +283,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) hex_gemm_kernel(const __grid_
       __syncwarp();
       if (lane == 0) mbar_arrive(&c->i_empty[ri]);
       if (!ok) continue;
-      if (gathers) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int s = __ldg(p.sorted_ids + static_cast<size_t>(b) * p.bm + lane * 4 + i);
-          grow[i] = s < p.num_slots ? (p.slot_row ? __ldg(p.slot_row + s) : s / p.topk) : 0;
-        }
-      }
       for (int kb = 0; kb < ksteps; ++kb) {
         if (!mbar_wait_idle(&c->b_empty[bs], bph ^ 1, abort_flag, p.dev_err)) { aborted = true; break; }
-        uint8_t* bdst = bring + bs * p.sz_b;
-        if (p.gather) {
-          // the stage's two 64-input halves, four rows per instruction, in the
-          // layout the two box loads below give (128-B rows, 128-B swizzle)
-          if (lane == 0) mbar_arrive_expect_tx(&c->b_full[bs], b_bytes);
-          __syncwarp();
-          if (gathers) {
-            tma_gather4(bdst + lane * 512, &p.tm_b, &c->b_full[bs], kb * kKStep, grow[0], grow[1], grow[2], grow[3]);
-            tma_gather4(bdst + p.bm * 128 + lane * 512, &p.tm_b, &c->b_full[bs], kb * kKStep + 64, grow[0], grow[1],
-                        grow[2], grow[3]);
-          }
-        } else if (lane == 0) {
+        if (lane == 0) {
+          uint8_t* bdst = bring + bs * p.sz_b;
           mbar_arrive_expect_tx(&c->b_full[bs], b_bytes);
           tma_load_2d(bdst, &p.tm_b, &c->b_full[bs], kb * kKStep, b * p.bm);
           tma_load_2d(bdst + p.bm * 128, &p.tm_b, &c->b_full[bs], kb * kKStep + 64, b * p.bm);

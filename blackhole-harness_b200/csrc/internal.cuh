@@ -54,11 +54,7 @@ __device__ __forceinline__ uint16_t* slot_out_row(const SlotOut& so, uint16_t* y
 // Everything the grouped-GEMM kernel needs; passed by value as a
 // __grid_constant__ parameter (tensor maps must live in parameter space).
 struct GemmParams {
-  CUtensorMap tm_b;                  // B rows in plan order: x_sorted [rows, H] (gate/up) or act [rows, I_pad] (down);
-                                     // gate/up with gather: x [rows, H] itself, box one row high
-  int32_t gather;                    // gate/up: 1 = B rows are gathered from x by TMA (tile::gather4): the x row
-  int32_t topk;                      //   of slot s is slot_row[s], or s / topk without a map (padding: row 0)
-  const int32_t* slot_row;
+  CUtensorMap tm_b;                  // B rows in plan order: x_sorted [rows, H] (gate/up) or act [rows, I_pad] (down)
   const uint8_t* idx_t[kMaxTiers][2];  // tiled index streams (hexmoe_tile_index layout)
   const uint8_t* bs[kMaxTiers][2];
   const float* es[kMaxTiers][2];
@@ -179,13 +175,12 @@ const hexmoe_layer_desc* layer_desc(const hexmoe_layer* layer);
 // read or written).  Workspace: slots_workspace_bytes(layer, num_slots, block_m);
 // y == nullptr puts the rows into the workspace's own y region.  *y_used
 // (optional) receives where they went.  slot_out (optional) routes the rows
-// elsewhere (SlotOut); y is then not written.  x_rows: the rows of x (0 =
-// unknown: the activations then go through the gather pass).
+// elsewhere (SlotOut); y is then not written.
 int forward_slot_space(const hexmoe_layer* layer, const void* x, int32_t x_dtype, int64_t num_slots,
                        const int32_t* slot_expert, const float* slot_weight, const int32_t* slot_row,
                        const int32_t* seg_counts, int64_t seg_len, void* y, int32_t block_m, void* workspace,
                        size_t workspace_bytes, cudaStream_t st, void** y_used = nullptr,
-                       const SlotOut* slot_out = nullptr, int64_t x_rows = 0);
+                       const SlotOut* slot_out = nullptr);
 size_t slots_workspace_bytes(const hexmoe_layer* layer, int64_t num_slots, int32_t block_m);
 int32_t* device_error_word();  // address of this device's error word (nullptr on failure)
 cudaError_t read_device_error(int32_t* value, bool clear);   // synchronous, current device
