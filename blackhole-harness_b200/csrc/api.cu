@@ -532,7 +532,7 @@ int forward_impl(const hexmoe_layer* layer, const void* x, int32_t x_dtype, int6
                  const float* topk_weights, const void* topk_ids, int32_t ids_dtype, void* out, int32_t out_dtype,
                  void* slots_out, int32_t block_m, void* workspace, size_t workspace_bytes, void* stream,
                  const int32_t* slot_row = nullptr, const int32_t* seg_counts = nullptr, int64_t seg_len = 0,
-                 const SlotOut* slot_out = nullptr) {
+                 const SlotOut* slot_out = nullptr, const GatherHook* gather = nullptr) {
   if (!layer) return fail(HEXMOE_E_ARG, "hexmoe_forward: null layer");
   const hexmoe_layer_desc& d = layer->desc;
   if (tokens < 0 || topk <= 0 || topk > d.num_experts) return fail(HEXMOE_E_ARG, "tokens %lld / topk %d", static_cast<long long>(tokens), topk);
@@ -570,10 +570,12 @@ int forward_impl(const hexmoe_layer* layer, const void* x, int32_t x_dtype, int6
   void* xs = ws + w.xs;
   cudaError_t e = launch_align(topk_ids, ids_dtype == HEXMOE_I64, S, d.num_experts, bm, sid, eid, npp,
                                reinterpret_cast<int32_t*>(ws + w.align), align_scratch_bytes(S, d.num_experts), dev_err,
-                               st, true, seg_counts, seg_len);
+                               st, true, seg_counts, seg_len, gather ? gather->inv : nullptr);
   if (e != cudaSuccess) return cuda_fail(e, "align launch");
 
-  e = launch_gather_rows(x, x_dtype, tokens, d.hidden, sid, npp, w.max_blocks * bm, topk, S, xs, st, true, slot_row);
+  e = gather ? gather->launch(gather->ctx, xs, gather->inv, st)
+             : launch_gather_rows(x, x_dtype, tokens, d.hidden, sid, npp, w.max_blocks * bm, topk, S, xs, st, true,
+                                  slot_row);
   if (e != cudaSuccess) return cuda_fail(e, "gather launch");
   int rc = run_gate_up(layer, xs, bf16, tokens, topk, sid, eid, npp, bm, act, dev_err, st, true);
   if (rc) return rc;
@@ -601,7 +603,8 @@ size_t hexmoe::slots_workspace_bytes(const hexmoe_layer* layer, int64_t num_slot
 int hexmoe::forward_slot_space(const hexmoe_layer* layer, const void* x, int32_t x_dtype, int64_t num_slots,
                                const int32_t* slot_expert, const float* slot_weight, const int32_t* slot_row,
                                const int32_t* seg_counts, int64_t seg_len, void* y, int32_t block_m, void* workspace,
-                               size_t workspace_bytes, cudaStream_t st, void** y_used, const SlotOut* slot_out) {
+                               size_t workspace_bytes, cudaStream_t st, void** y_used, const SlotOut* slot_out,
+                               const GatherHook* gather) {
   if (!layer) return fail(HEXMOE_E_ARG, "forward_slot_space: null layer");
   if (!y) {
     // the per-slot rows go to the workspace's own y region
@@ -613,7 +616,7 @@ int hexmoe::forward_slot_space(const hexmoe_layer* layer, const void* x, int32_t
   if (y_used) *y_used = y;
   return forward_impl(layer, x, x_dtype, num_slots, 1, slot_weight, slot_expert, HEXMOE_I32, y,
                       x_dtype == HEXMOE_F16 ? HEXMOE_F16 : HEXMOE_BF16, y, block_m, workspace, workspace_bytes, st,
-                      slot_row, seg_counts, seg_len, slot_out);
+                      slot_row, seg_counts, seg_len, slot_out, gather);
 }
 
 extern "C" {

@@ -4,16 +4,20 @@
 //
 // Experts are sharded contiguously: rank r owns global experts [r*P, (r+1)*P),
 // P = ceil(E / world).  Every rank owns one region of device memory that it
-// exports by CUDA IPC and every other rank maps, so kernels on any rank store
-// straight into any rank's region over NVLink (plain stores from SMs):
+// exports by CUDA IPC and every other rank maps, so kernels on any rank load
+// from and store into any rank's region over NVLink (plain loads and stores
+// from SMs):
 //
 //   flags      disp[world], ret[world] (uint64): the epoch a source's dispatch /
 //              a destination's return has completed, written with release
 //              stores at system scope, polled with acquire loads
 //   counts     rows[world], slots[world]: what each source sent this epoch
-//   recv_x     [world][cap][H] 16-bit: one row per (token, this rank) pair of
-//              each source, in the source's token order
-//   rec_row    [world][seg_len] int32: per received slot, its row (src*cap + pos)
+//   xcopy      [cap][H] 16-bit: this rank's own token rows (the owners of
+//              their experts pull them from here)
+//   rowslot    [world][cap+1] int32: per row received from a source (one per
+//              token of it with a slot here, in token order), its first slot
+//              in the source's segment; entry rows[src] = slots[src]
+//   rowtok     [world][cap] int32: per received row, the source's token index
 //   rec_exp    [world][seg_len] int32: per received slot, its global expert
 //   rec_w      [world][seg_len] f32:   per received slot, its top-k weight
 //   rec_dst    [world][seg_len] int32: per received slot, where its output row
@@ -27,12 +31,16 @@
 //   plan      (a CTA per 256 tokens) per token and destination rank, the row
 //             position and the first slot offset (stable scans over tokens);
 //             the last CTA adds up the CTAs' totals and advances the epoch
-//   send      (all SMs) each token row read once and stored to every rank that
-//             owns one of its experts, with its slot records; the last CTA
-//             writes the counts and raises disp[me] = epoch on every rank
+//   send      (all SMs) each token row copied into this rank's own xcopy, and
+//             its slot and row records stored into every rank that owns one
+//             of its experts; the last CTA writes the counts and raises
+//             disp[me] = epoch on every rank
 //   wait      (1 CTA) disp[src] >= epoch for every source (bounded)
-//   experts   the layer over the received slots (align over the ragged slot
-//             space, gather through rec_row, gate/up, down); the down GEMM's
+//   experts   the layer over the received slots: align over the ragged slot
+//             space (which also records each slot's plan row), then the pull
+//             gather (a warp per received row: the row loaded once from its
+//             source's xcopy over NVLink and stored to the plan rows of all its
+//             slots here), gate/up, down; the down GEMM's
 //             epilogue stores each slot's row (top-k weight applied, rounded
 //             once) straight into its source's ret over NVLink, so the return
 //             runs under the GEMM, and every thread ends with a system fence
@@ -42,12 +50,12 @@
 //             the single-GPU layer's combine over the same per-slot rows, so
 //             the output equals the single-GPU layer's bit for bit
 //
-// Buffers are single: a source writes rank d's receive rows and slot records
-// for epoch e only after its own combine of epoch e-1 saw d's return flag of
-// e-1, which d raised after its down GEMM (the last reader of them) of e-1 had
-// finished; and d writes a source's ret for epoch e only after it saw that
-// source's dispatch of e, issued after the source's combine of e-1 had read
-// ret.  So every rank must
+// Buffers are single: a source rewrites its xcopy and rank d's records for
+// epoch e only after its own combine of epoch e-1 saw d's return flag of e-1,
+// which d raised after its down GEMM of e-1 (after d's gather had read xcopy,
+// and the last reader of the records) had finished; and d writes a source's ret
+// for epoch e only after it saw that source's dispatch of e, issued after the
+// source's combine of e-1 had read ret.  So every rank must
 // run every forward (the same sequence of calls on every rank).  Every wait is
 // bounded (2 s): a missing peer sets the device error word (timeout) instead of
 // hanging the GPU.
@@ -69,7 +77,7 @@ struct EpArgs {
   int32_t rank, world, E, P, H, topk;
   int64_t cap, seg_len;
   // region offsets
-  uint64_t o_disp, o_ret_flag, o_rows, o_slots, o_x, o_row, o_exp, o_w, o_dst, o_ret;
+  uint64_t o_disp, o_ret_flag, o_rows, o_slots, o_xcopy, o_rowslot, o_rowtok, o_exp, o_w, o_dst, o_ret;
   // this rank's private state
   int64_t* epoch;
   uint32_t* done;               // [3]: CTAs finished in send / return / plan
@@ -79,6 +87,7 @@ struct EpArgs {
   int64_t* plan_tot;            // [plan CTAs][kEpMaxWorld]: each plan CTA's totals (rows << 32 | slots)
   int64_t* plan_off;            // [plan CTAs][kEpMaxWorld]: their exclusive offsets over CTAs
   int32_t* cmap;                // [cap * topk]: the combine's row of slot (t, j): t * topk + j, -1 = bad expert id
+  int32_t* inv;                 // [world * seg_len]: the plan row of every received slot (written by the align)
   int32_t* dev_err;
 };
 
@@ -196,8 +205,9 @@ __global__ void __launch_bounds__(kPlanThreads) ep_plan_kernel(EpArgs a, const v
 }
 
 // ---------------------------------------------------------------- send
-// A warp per token: its row is read once (8 x 16 B per lane per 2048 inputs)
-// and stored to every destination rank; lanes j < topk write the slot records.
+// A warp per token: its row is copied into this rank's xcopy (rounded to bf16
+// from f32 input); lanes j < topk write the slot records into the rank that
+// owns expert j, the lane of a rank's first slot also the row record.
 constexpr int kSendThreads = 256;
 
 template <typename XT, bool I64>
@@ -218,6 +228,7 @@ __global__ void __launch_bounds__(kSendThreads) ep_send_kernel(EpArgs a, const X
       so[d] = d < a.world ? __ldg(a.soff + t * a.world + d) + static_cast<int32_t>(o & 0xffffffffll) : 0;
       if (pos[d] >= 0) pos[d] += static_cast<int32_t>(o >> 32);
     }
+    uint4* own = at<uint4>(a.self, a.o_xcopy) + t * hv;
     for (int c0 = 0; c0 < hv; c0 += 8 * 32) {
       uint4 v[8];
 #pragma unroll
@@ -235,14 +246,9 @@ __global__ void __launch_bounds__(kSendThreads) ep_send_kernel(EpArgs a, const X
         }
       }
 #pragma unroll
-      for (int d = 0; d < kEpMaxWorld; ++d) {
-        if (pos[d] < 0) continue;
-        uint4* dst = at<uint4>(a.peer[d], a.o_x) + (static_cast<int64_t>(a.rank) * a.cap + pos[d]) * hv;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int c = c0 + i * 32 + lane;
-          if (c < hv) dst[c] = v[i];
-        }
+      for (int i = 0; i < 8; ++i) {
+        const int c = c0 + i * 32 + lane;
+        if (c < hv) own[c] = v[i];
       }
     }
     // slot records (topk <= 32): the j-th slot of token t at its owner rank d
@@ -261,7 +267,10 @@ __global__ void __launch_bounds__(kSendThreads) ep_send_kernel(EpArgs a, const X
         if (q == d) { my_pos = pos[q]; my_so = so[q]; }
       uint8_t* R = a.peer[d];
       const int64_t seg = static_cast<int64_t>(a.rank) * a.seg_len;
-      at<int32_t>(R, a.o_row)[seg + my_so + rk] = static_cast<int32_t>(a.rank * a.cap + my_pos);
+      if (rk == 0) {
+        at<int32_t>(R, a.o_rowslot)[static_cast<int64_t>(a.rank) * (a.cap + 1) + my_pos] = my_so;
+        at<int32_t>(R, a.o_rowtok)[static_cast<int64_t>(a.rank) * a.cap + my_pos] = static_cast<int32_t>(t);
+      }
       at<int32_t>(R, a.o_exp)[seg + my_so + rk] = static_cast<int32_t>(e);
       at<float>(R, a.o_w)[seg + my_so + rk] = __ldg(w + t * a.topk + lane);
       at<int32_t>(R, a.o_dst)[seg + my_so + rk] = static_cast<int32_t>((a.rank * a.cap + t) * a.topk + lane);
@@ -282,6 +291,7 @@ __global__ void __launch_bounds__(kSendThreads) ep_send_kernel(EpArgs a, const X
     const int32_t rows = a.tot[2 * d], slots = a.tot[2 * d + 1];
     at<int32_t>(R, a.o_rows)[a.rank] = rows;
     at<int32_t>(R, a.o_slots)[a.rank] = slots;
+    at<int32_t>(R, a.o_rowslot)[static_cast<int64_t>(a.rank) * (a.cap + 1) + rows] = slots;
     __threadfence_system();
     st_release_sys(at<uint64_t>(R, a.o_disp) + a.rank, static_cast<uint64_t>(epoch));
   }
@@ -310,6 +320,56 @@ __global__ void ep_wait_kernel(EpArgs a, uint64_t o_flags) {
   __syncthreads();
 }
 
+// ---------------------------------------------------------------- gather
+// A warp per received row (source src, its row rho): the token row is loaded
+// once from the source's xcopy (over NVLink for another rank) and stored to the
+// plan rows of its slots here, slots s0 .. s1-1 of the source's segment.
+template <bool PDL>
+__global__ void __launch_bounds__(kSendThreads) ep_gather_kernel(EpArgs a, uint16_t* __restrict__ xs) {
+  if (PDL) pdl_wait();   // inv comes from the align
+  const int lane = threadIdx.x & 31;
+  int64_t start[kEpMaxWorld + 1];
+  start[0] = 0;
+#pragma unroll
+  for (int d = 0; d < kEpMaxWorld; ++d)
+    start[d + 1] = start[d] + (d < a.world ? __ldg(at<int32_t>(a.self, a.o_rows) + d) : 0);
+  const int64_t total = start[kEpMaxWorld];
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * kSendThreads) >> 5;
+  const int hv = a.H / 8;
+  for (int64_t g = (blockIdx.x * static_cast<int64_t>(kSendThreads) + threadIdx.x) >> 5; g < total; g += nwarps) {
+    int src = 0;
+#pragma unroll
+    for (int d = 1; d < kEpMaxWorld; ++d)
+      if (g >= start[d]) src = d;
+    const int64_t rho = g - start[src];
+    const int32_t* rs = at<int32_t>(a.self, a.o_rowslot) + static_cast<int64_t>(src) * (a.cap + 1);
+    const int32_t s0 = __ldg(rs + rho), s1 = __ldg(rs + rho + 1);
+    const int32_t tok = __ldg(at<int32_t>(a.self, a.o_rowtok) + static_cast<int64_t>(src) * a.cap + rho);
+    uint8_t* P = a.self;
+#pragma unroll
+    for (int q = 0; q < kEpMaxWorld; ++q) P = q == src ? a.peer[q] : P;
+    const uint4* row = at<const uint4>(P, a.o_xcopy) + static_cast<int64_t>(tok) * hv;
+    const int32_t* inv = a.inv + static_cast<int64_t>(src) * a.seg_len;
+    for (int c0 = 0; c0 < hv; c0 += 8 * 32) {
+      uint4 v[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int c = c0 + i * 32 + lane;
+        if (c < hv) v[i] = __ldcv(row + c);   // another rank's memory, rewritten every epoch: not cached
+      }
+      for (int s = s0; s < s1; ++s) {
+        uint4* dst = reinterpret_cast<uint4*>(xs + static_cast<int64_t>(__ldg(inv + s)) * a.H);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int c = c0 + i * 32 + lane;
+          if (c < hv) dst[c] = v[i];
+        }
+      }
+    }
+  }
+  if (PDL) pdl_launch_dependents();
+}
+
 // ---------------------------------------------------------------- signal
 // After the down GEMM, whose threads all ended with a system-scope fence after
 // their peer stores: ret flag[this rank] = epoch on every rank.
@@ -332,7 +392,7 @@ using namespace hexmoe;
 struct hexmoe_ep {
   int device, rank, world, E, P, H, topk, row_dtype;
   int64_t cap, seg_len;
-  uint64_t o_disp, o_ret_flag, o_rows, o_slots, o_x, o_row, o_exp, o_w, o_dst, o_ret;
+  uint64_t o_disp, o_ret_flag, o_rows, o_slots, o_xcopy, o_rowslot, o_rowtok, o_exp, o_w, o_dst, o_ret;
   size_t region_bytes;
   uint8_t* region;
   uint8_t* peer[kEpMaxWorld];
@@ -341,7 +401,7 @@ struct hexmoe_ep {
   uint8_t* local;
   int64_t* epoch;
   uint32_t* done;
-  int32_t *tot, *pos, *soff, *cmap;
+  int32_t *tot, *pos, *soff, *cmap, *inv;
   int64_t *plan_tot, *plan_off;
   int64_t last_tokens;
 };
@@ -357,10 +417,11 @@ EpArgs ep_args(const hexmoe_ep* ep, int32_t* dev_err) {
   a.rank = ep->rank; a.world = ep->world; a.E = ep->E; a.P = ep->P; a.H = ep->H; a.topk = ep->topk;
   a.cap = ep->cap; a.seg_len = ep->seg_len;
   a.o_disp = ep->o_disp; a.o_ret_flag = ep->o_ret_flag; a.o_rows = ep->o_rows; a.o_slots = ep->o_slots;
-  a.o_x = ep->o_x; a.o_row = ep->o_row; a.o_exp = ep->o_exp; a.o_w = ep->o_w; a.o_dst = ep->o_dst;
+  a.o_xcopy = ep->o_xcopy; a.o_rowslot = ep->o_rowslot; a.o_rowtok = ep->o_rowtok;
+  a.o_exp = ep->o_exp; a.o_w = ep->o_w; a.o_dst = ep->o_dst;
   a.o_ret = ep->o_ret;
   a.epoch = ep->epoch; a.done = ep->done; a.tot = ep->tot; a.pos = ep->pos; a.soff = ep->soff;
-  a.plan_tot = ep->plan_tot; a.plan_off = ep->plan_off; a.cmap = ep->cmap;
+  a.plan_tot = ep->plan_tot; a.plan_off = ep->plan_off; a.cmap = ep->cmap; a.inv = ep->inv;
   a.dev_err = dev_err;
   return a;
 }
@@ -383,6 +444,23 @@ int grid_for(int64_t work_warps, int per_cta_warps, int ctas_per_sm = 2) {
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t want = (work_warps + per_cta_warps - 1) / per_cta_warps;
   return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, static_cast<int64_t>(sms) * ctas_per_sm)));
+}
+
+// The GatherHook of the slot-space forward: ep_gather_kernel after the align
+// (programmatic dependent launch, as the kernels around it).
+cudaError_t ep_gather_launch(const void* ctx, void* xs, const int32_t* inv, cudaStream_t st) {
+  EpArgs a = *static_cast<const EpArgs*>(ctx);
+  a.inv = const_cast<int32_t*>(inv);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid_for(static_cast<int64_t>(a.world) * a.cap, kSendThreads / 32, 4)));
+  cfg.blockDim = dim3(kSendThreads);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, ep_gather_kernel<true>, a, static_cast<uint16_t*>(xs));
 }
 
 }  // namespace
@@ -413,8 +491,9 @@ int hexmoe_ep_init(int32_t rank, int32_t world, int32_t num_experts, int32_t hid
   ep->o_slots = off; off += 4 * kEpMaxWorld;
   off = up256(off);
   const size_t header = off;
-  ep->o_x = off; off = up256(off + W * ep->cap * hidden * 2);
-  ep->o_row = off; off = up256(off + W * ep->seg_len * 4);
+  ep->o_xcopy = off; off = up256(off + static_cast<size_t>(ep->cap) * hidden * 2);
+  ep->o_rowslot = off; off = up256(off + W * (ep->cap + 1) * 4);
+  ep->o_rowtok = off; off = up256(off + W * ep->cap * 4);
   ep->o_exp = off; off = up256(off + W * ep->seg_len * 4);
   ep->o_w = off; off = up256(off + W * ep->seg_len * 4);
   ep->o_dst = off; off = up256(off + W * ep->seg_len * 4);
@@ -424,7 +503,8 @@ int hexmoe_ep_init(int32_t rank, int32_t world, int32_t num_experts, int32_t hid
   if (e != cudaSuccess) { delete ep; return report_cuda_error(e, "hexmoe_ep_init: region allocation"); }
   const size_t plan_ctas = static_cast<size_t>((ep->cap + kPlanThreads - 1) / kPlanThreads);
   const size_t local_bytes = up256(8 + 16) + up256(W * 2 * 4) + 2 * up256(ep->cap * W * 4) +
-                             2 * up256(plan_ctas * kEpMaxWorld * 8) + up256(static_cast<size_t>(ep->cap) * topk * 4);
+                             2 * up256(plan_ctas * kEpMaxWorld * 8) + up256(static_cast<size_t>(ep->cap) * topk * 4) +
+                             up256(W * ep->seg_len * 4);
   e = cudaMalloc(&ep->local, local_bytes);
   if (e == cudaSuccess) e = cudaMemset(ep->region, 0, header);
   if (e == cudaSuccess) e = cudaMemset(ep->local, 0, local_bytes);
@@ -444,7 +524,8 @@ int hexmoe_ep_init(int32_t rank, int32_t world, int32_t num_experts, int32_t hid
   ep->soff = reinterpret_cast<int32_t*>(ep->local + lo); lo += up256(ep->cap * W * 4);
   ep->plan_tot = reinterpret_cast<int64_t*>(ep->local + lo); lo += up256(plan_ctas * kEpMaxWorld * 8);
   ep->plan_off = reinterpret_cast<int64_t*>(ep->local + lo); lo += up256(plan_ctas * kEpMaxWorld * 8);
-  ep->cmap = reinterpret_cast<int32_t*>(ep->local + lo);
+  ep->cmap = reinterpret_cast<int32_t*>(ep->local + lo); lo += up256(static_cast<size_t>(ep->cap) * topk * 4);
+  ep->inv = reinterpret_cast<int32_t*>(ep->local + lo);
   for (int d = 0; d < kEpMaxWorld; ++d) { ep->peer[d] = nullptr; ep->opened[d] = false; }
   ep->peer[rank] = ep->region;
   ep->connected = world == 1;
@@ -543,10 +624,12 @@ int hexmoe_ep_experts(hexmoe_ep* ep, const hexmoe_layer* local, int32_t block_m,
       so.base[r] = r < ep->world ? reinterpret_cast<uint16_t*>(ep->peer[r] + ep->o_ret) : nullptr;
     so.seg_rows = static_cast<int32_t>(ep->cap * ep->topk);
     so.fence = 1;
-    int rc = forward_slot_space(local, R + ep->o_x, ep->row_dtype, S, reinterpret_cast<const int32_t*>(R + ep->o_exp),
-                                reinterpret_cast<const float*>(R + ep->o_w), reinterpret_cast<const int32_t*>(R + ep->o_row),
-                                reinterpret_cast<const int32_t*>(R + ep->o_slots), ep->seg_len, nullptr, block_m,
-                                workspace, workspace_bytes, st, nullptr, &so);
+    // the activation rows come from the pull gather (the align records each slot's plan row)
+    const GatherHook gh{ep_gather_launch, &a, ep->inv};
+    int rc = forward_slot_space(local, R + ep->o_xcopy, ep->row_dtype, S,
+                                reinterpret_cast<const int32_t*>(R + ep->o_exp), reinterpret_cast<const float*>(R + ep->o_w),
+                                nullptr, reinterpret_cast<const int32_t*>(R + ep->o_slots), ep->seg_len, nullptr,
+                                block_m, workspace, workspace_bytes, st, nullptr, &so, &gh);
     if (rc) return rc;
   }
   // without local experts nothing can have been routed here: only the flags

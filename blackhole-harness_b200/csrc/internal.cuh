@@ -51,6 +51,16 @@ __device__ __forceinline__ uint16_t* slot_out_row(const SlotOut& so, uint16_t* y
   return b + static_cast<int64_t>(g - sg * so.seg_rows) * ld_out;
 }
 
+// The expert-parallel receive side's own gather (ep.cu): launch(ctx, xs, inv,
+// st) writes the plan-ordered activation rows xs itself, given inv [num_slots],
+// the plan row of every slot, which the align writes.  Replaces the plain
+// gather pass of the slot-space forward.
+struct GatherHook {
+  cudaError_t (*launch)(const void* ctx, void* xs, const int32_t* inv, cudaStream_t st);
+  const void* ctx;
+  int32_t* inv;
+};
+
 // Everything the grouped-GEMM kernel needs; passed by value as a
 // __grid_constant__ parameter (tensor maps must live in parameter space).
 struct GemmParams {
@@ -144,9 +154,10 @@ cudaError_t launch_code_tables(const float* levels, const float* es, int bits, i
 // Small kernels (kernels.cu).
 // seg_counts (optional): the ragged slot space of the expert-parallel receive
 // side, segments of seg_len slots of which only the first seg_counts[g] exist.
+// inv (optional, [S]): receives the plan row of every present slot.
 cudaError_t launch_align(const void* ids, bool ids64, int64_t S, int32_t E, int32_t bm, int32_t* sid, int32_t* eid,
                          int32_t* npp, int32_t* scratch, size_t scratch_bytes, int32_t* dev_err, cudaStream_t st,
-                         bool pdl, const int32_t* seg_counts = nullptr, int64_t seg_len = 0);
+                         bool pdl, const int32_t* seg_counts = nullptr, int64_t seg_len = 0, int32_t* inv = nullptr);
 size_t align_scratch_bytes(int64_t S, int32_t E);
 cudaError_t launch_dequant(const hexmoe_parts& parts, int bits, int block, int n, int rows, int cols, int rows_pad,
                            int cols_pad, const int32_t* experts, void* out, int out_dtype, int64_t stride_e,
@@ -175,12 +186,13 @@ const hexmoe_layer_desc* layer_desc(const hexmoe_layer* layer);
 // read or written).  Workspace: slots_workspace_bytes(layer, num_slots, block_m);
 // y == nullptr puts the rows into the workspace's own y region.  *y_used
 // (optional) receives where they went.  slot_out (optional) routes the rows
-// elsewhere (SlotOut); y is then not written.
+// elsewhere (SlotOut); y is then not written.  gather (optional) replaces the
+// gather pass (GatherHook); slot_row is then unused.
 int forward_slot_space(const hexmoe_layer* layer, const void* x, int32_t x_dtype, int64_t num_slots,
                        const int32_t* slot_expert, const float* slot_weight, const int32_t* slot_row,
                        const int32_t* seg_counts, int64_t seg_len, void* y, int32_t block_m, void* workspace,
                        size_t workspace_bytes, cudaStream_t st, void** y_used = nullptr,
-                       const SlotOut* slot_out = nullptr);
+                       const SlotOut* slot_out = nullptr, const GatherHook* gather = nullptr);
 size_t slots_workspace_bytes(const hexmoe_layer* layer, int64_t num_slots, int32_t block_m);
 int32_t* device_error_word();  // address of this device's error word (nullptr on failure)
 cudaError_t read_device_error(int32_t* value, bool clear);   // synchronous, current device

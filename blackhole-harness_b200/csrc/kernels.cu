@@ -106,6 +106,7 @@ __device__ __forceinline__ unsigned equal_lanes(uint32_t v, int nbits) {
 struct AlignRagged {
   const int32_t* counts;
   int64_t seg_len;
+  int32_t* inv;   // optional [S]: the plan row each slot is scattered to
   __device__ __forceinline__ bool present(int64_t s) const {
     return !counts || (s % seg_len) < __ldg(counts + s / seg_len);
   }
@@ -182,6 +183,7 @@ __device__ void warp_scatter(const void* ids, int64_t s_begin, int64_t s_end, in
       if (e >= 0) {
         const int rank = __popc(peers & ((1u << lane) - 1u));
         sid[base + rank] = static_cast<int32_t>(c0 + u * 32 + lane);
+        if (rg.inv) rg.inv[c0 + u * 32 + lane] = base + rank;
         if (rank == 0) my_pos[e] = base + __popc(peers);
       }
       __syncwarp();
@@ -480,8 +482,8 @@ size_t align_scratch_bytes(int64_t S, int32_t E) {
 
 cudaError_t launch_align(const void* ids, bool ids64, int64_t S, int32_t E, int32_t bm, int32_t* sid, int32_t* eid,
                          int32_t* npp, int32_t* scratch, size_t scratch_bytes, int32_t* dev_err, cudaStream_t st,
-                         bool pdl, const int32_t* seg_counts, int64_t seg_len) {
-  const AlignRagged rg{seg_counts, seg_counts ? seg_len : 1};
+                         bool pdl, const int32_t* seg_counts, int64_t seg_len, int32_t* inv) {
+  const AlignRagged rg{seg_counts, seg_counts ? seg_len : 1, inv};
   if (E > kAlignMaxExperts) return cudaErrorInvalidValue;
   static std::atomic<bool> configured[64] = {};   // per device
   static std::mutex mu;
@@ -515,7 +517,7 @@ cudaError_t launch_align(const void* ids, bool ids64, int64_t S, int32_t E, int3
   cfg.numAttrs = pdl ? 1 : 0;
   const size_t hist_bytes = static_cast<size_t>(kAlignWarps) * E * sizeof(int32_t);
   const size_t need = align_scratch_bytes(S, E);
-  if (!seg_counts && S <= kAlignSmall && E <= kAlignSmall) {
+  if (!seg_counts && !inv && S <= kAlignSmall && E <= kAlignSmall) {
     cfg.gridDim = dim3(1);
     cfg.blockDim = dim3(kAlignSmall);
     const int32_t S32 = static_cast<int32_t>(S);
