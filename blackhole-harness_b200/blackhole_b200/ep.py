@@ -22,8 +22,9 @@ ranks.
 
 On GPUs (EPMoE with local tiers) the four steps are the library's hexmoe_ep_*
 kernels over CUDA-IPC peer memory: stores straight into the owner's region over
-NVLink (the return from the down GEMM's own epilogue), epoch flags instead of
-host synchronisation, so a forward can be captured in a CUDA graph.  The only collective on the host is the one-time
+NVLink (the return from the down GEMM's own epilogue; the token rows pulled by
+their owners from the source's region), epoch flags instead of host
+synchronisation, so a forward can be captured in a CUDA graph.  The only collective on the host is the one-time
 exchange of the IPC handles at construction.  An expert id outside 0..E-1 is
 dropped and sets the device error word (hexmoe_device_status) on the GPU path.
 

@@ -259,13 +259,14 @@ HEXMOE_API int hexmoe_dequant(const hexmoe_parts* parts, int32_t bits, int32_t b
  * [r*P, (r+1)*P), P = ceil(num_experts / world), and runs them as a
  * hexmoe_layer built from its own tiers only (global expert ids kept).  Each
  * rank's context owns one device region that every other rank maps through
- * CUDA IPC; kernels store token rows, slot records and per-slot output rows
- * straight into the owning rank's region with plain stores, and signal with epoch flags
+ * CUDA IPC; kernels store slot records and per-slot output rows straight into
+ * the owning rank's region and load token rows from the source's region, with
+ * plain loads and stores, and signal with epoch flags
  * (release / acquire at system scope).  Nothing synchronises with the host, so
  * a forward can be captured in a CUDA graph.
  *
  * Per forward: every token row crosses once per rank that owns one of its
- * experts (not once per slot); the owner runs its experts on the received
+ * experts (not once per slot), pulled by the owner; the owner runs its experts on the received
  * slots, and its down GEMM stores each slot's weighted output row (rounded
  * once to the row dtype) straight into the home rank's buffer at the slot's
  * place; the home rank sums a token's k rows in top-k order in fp32 and rounds
@@ -287,8 +288,8 @@ typedef struct hexmoe_ep hexmoe_ep;
 /* Context of rank `rank` of `world` on the current device, for up to
  * max_tokens tokens per rank per forward, top-`topk` over num_experts global
  * experts of width `hidden`; rows travel as row_dtype (BF16 or F16).  Allocates
- * the shared region ((world + topk) x max_tokens x hidden x 2 bytes of rows
- * plus ~16 x world x max_tokens x topk bytes of slot records) and its private
+ * the shared region ((1 + topk) x max_tokens x hidden x 2 bytes of rows plus
+ * ~12 x world x max_tokens x (topk + 1) bytes of records) and its private
  * state; synchronises the device. */
 HEXMOE_API int hexmoe_ep_init(int32_t rank, int32_t world, int32_t num_experts, int32_t hidden, int32_t topk,
                               int64_t max_tokens, int32_t row_dtype, hexmoe_ep** out);
