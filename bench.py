@@ -9,8 +9,9 @@ top-8, SwiGLU, half the experts (seeded) 4-bit / 16-level and half 3-bit /
 one step is the single-GPU layer (hexmoe_forward: align plan, gather, gate/up
 GEMM with SwiGLU, down GEMM with the top-k weight, combine); at N>1 it is the
 expert-parallel layer (hexmoe_ep_forward: experts sharded 96/N per GPU, token
-rows dispatched to their experts' GPUs over NVLink peer memory, pre-summed
-partials returned), value = all ranks' tokens over the slowest rank's time.
+rows pulled by their experts' GPUs over NVLink peer memory, every slot's output
+row stored back into its home GPU by the down GEMM), value = all ranks' tokens
+over the slowest rank's time.
 Synthetic seeded data (blackhole_b200.hex_data): no dataset exists on this
 path.  Steps are replayed from a CUDA graph with inputs in HBM, timed with CUDA
 events on the launching stream; between timed steps a 256 MiB buffer is

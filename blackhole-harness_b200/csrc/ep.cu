@@ -435,9 +435,9 @@ int ep_check(const hexmoe_ep* ep, const char* what) {
   return HEXMOE_OK;
 }
 
-// Grid of the send / return kernels: a few CTAs per SM, warps looping over
-// their tokens / rows (each CTA ends with one system-scope fence, so fewer,
-// longer-lived CTAs fence less).
+// Grid of the send / gather kernels: a few CTAs per SM, warps looping over
+// their tokens / rows (each send CTA ends with one system-scope fence, so
+// fewer, longer-lived CTAs fence less).
 int grid_for(int64_t work_warps, int per_cta_warps, int ctas_per_sm = 2) {
   int sms = 148;
   int dev = 0;
